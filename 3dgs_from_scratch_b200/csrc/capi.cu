@@ -1,0 +1,99 @@
+// capi.cu -- status plumbing, launch accounting and small C-ABI utilities.
+#include <atomic>
+
+#include "gs_common.cuh"
+
+namespace gs {
+
+// One status word per device (module globals are instantiated per device).
+__device__ uint32_t g_status_word;
+
+static std::atomic<uint64_t> g_launches{0};
+static std::atomic<int> g_last_cuda_error{0};
+static uint32_t *g_status_ptr[64] = {nullptr};
+
+void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return GS_OK;
+  g_last_cuda_error.store((int)e);
+  return GS_ERR_CUDA;
+}
+
+int launch_status() { return cuda_status(cudaGetLastError()); }
+
+uint32_t *device_status_word() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (g_status_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = reinterpret_cast<uint32_t *>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_version(void) { return 1; }
+
+extern "C" int gs_last_cuda_error(void) { return g_last_cuda_error.load(); }
+
+extern "C" uint64_t gs_launch_count(void) { return g_launches.load(); }
+
+extern "C" int gs_sync(void *stream) {
+  return cuda_status(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));
+}
+
+static int read_and_clear_status(cudaStream_t st) {
+  uint32_t *w = device_status_word();
+  if (w == nullptr) return GS_ERR_CUDA;
+  uint32_t v = 0;
+  int rc = cuda_status(cudaMemcpyAsync(&v, w, sizeof(v), cudaMemcpyDeviceToHost, st));
+  if (rc) return rc;
+  rc = cuda_status(cudaStreamSynchronize(st));
+  if (rc) return rc;
+  if (v != 0) {
+    rc = cuda_status(cudaMemsetAsync(w, 0, sizeof(uint32_t), st));
+    if (rc) return rc;
+    return (int)v;
+  }
+  return GS_OK;
+}
+
+extern "C" int gs_check_status(void *stream) {
+  return read_and_clear_status(reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gs_read_total(const int64_t *total_dev, int64_t *total_host, void *stream) {
+  if (total_dev == nullptr || total_host == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = cuda_status(cudaMemcpyAsync(total_host, total_dev, sizeof(int64_t),
+                                       cudaMemcpyDeviceToHost, st));
+  if (rc) return rc;
+  return read_and_clear_status(st);
+}
+
+// Self-test of the bounded-wait mechanism: one thread waits on a flag that
+// nothing sets, gives up after kSpinLimit polls, records
+// GS_ERR_DEVICE_TIMEOUT in the status word and exits; the host reads it back.
+__global__ void bounded_wait_probe_kernel(const uint32_t *flag, uint32_t *status) {
+  uint32_t v, spins = 0;
+  do {
+    v = gs::ld_volatile_u32(flag);
+  } while (v == 0 && ++spins < gs::kSpinLimit);
+  if (v == 0) atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
+}
+
+extern "C" int gs_selftest_bounded_wait(const uint32_t *flag_dev, void *stream) {
+  if (flag_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  bounded_wait_probe_kernel<<<1, 1, 0, st>>>(flag_dev, device_status_word());
+  count_launch();
+  int rc = launch_status();
+  if (rc) return rc;
+  return read_and_clear_status(st);
+}

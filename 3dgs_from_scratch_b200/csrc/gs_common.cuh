@@ -1,0 +1,444 @@
+// gs_common.cuh -- shared device math, status plumbing and launch accounting
+// for the B200 Gaussian-splatting rasterizer.
+//
+// The per-Gaussian float expressions below keep the operand order of the
+// reference kernels (ruguangyou/3dgs_from_scratch src/cuda/kernel.cu) so that
+// nvcc contracts them into the same fused multiply-adds: depth bits and the
+// pixel-space tile rectangle feed the sort keys, which must match the
+// reference bit for bit. Everything else (memory layout, fusion, launch
+// shape) is this library's own.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gs_b200.h"
+
+namespace gs {
+
+constexpr float kLowPass = 0.3f;        // kernel.cu:23
+constexpr float kFovClamp = 1.3f;       // kernel.cu:24
+constexpr float kTransEps = 1e-10f;     // kernel.cu:25
+
+// Real SH constants, degree 0..3 (kernel.cu:7-22).
+constexpr float kC0 = 0.28209479177387814f;
+constexpr float kC1 = 0.4886025119029199f;
+constexpr float kC2xy = 1.0925484305920792f;
+constexpr float kC2zz = 0.31539156525252005f;
+constexpr float kC2xxyy = 0.5462742152960396f;
+constexpr float kC3a = 0.5900435899266435f;
+constexpr float kC3xyz = 2.890611442640554f;
+constexpr float kC3c = 0.4570457994644658f;
+constexpr float kC3zzz = 0.3731763325901154f;
+constexpr float kC3zxx = 1.445305721320277f;
+
+// ---- host-side plumbing (defined in capi.cu) ------------------------------
+void count_launch(int n = 1);
+int cuda_status(cudaError_t e);                 // maps and records a CUDA error
+int launch_status();                            // cudaGetLastError after launches
+uint32_t *device_status_word();                 // per-device status word (device ptr)
+
+// Bounded spin limit for look-back waits. A predecessor that is resident
+// publishes within microseconds; this bound (~ tens of ms) only ends a wait
+// that can never finish, which then records GS_ERR_DEVICE_TIMEOUT.
+constexpr uint32_t kSpinLimit = 1u << 20;
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_volatile_u32(uint32_t *p, uint32_t v) {
+  asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lane_id() {
+  uint32_t l;
+  asm("mov.u32 %0, %%laneid;" : "=r"(l));
+  return l;
+}
+
+// ---- projection -------------------------------------------------------------
+
+struct Cam {
+  float W[12];  // rows 0..2 of the row-major world_to_camera
+  float fx, fy, cx, cy;
+};
+
+__device__ __forceinline__ Cam load_cam(const float *__restrict__ w2c,
+                                        const float *__restrict__ K) {
+  Cam c;
+#pragma unroll
+  for (int i = 0; i < 12; ++i) c.W[i] = __ldg(w2c + i);
+  c.fx = __ldg(K + 0);
+  c.cx = __ldg(K + 2);
+  c.fy = __ldg(K + 4);
+  c.cy = __ldg(K + 5);
+  return c;
+}
+
+// Camera-space position (kernel.cu:27-44).
+__device__ __forceinline__ float3 to_camera(const Cam &c, float px, float py, float pz) {
+  float3 r;
+  r.x = c.W[0] * px + c.W[1] * py + c.W[2] * pz + c.W[3];
+  r.y = c.W[4] * px + c.W[5] * py + c.W[6] * pz + c.W[7];
+  r.z = c.W[8] * px + c.W[9] * py + c.W[10] * pz + c.W[11];
+  return r;
+}
+
+// Rotation of an (x, y, z, w) quaternion, row-major (kernel.cu:57-65).
+__device__ __forceinline__ void quat_to_rot(float x, float y, float z, float w, float R[9]) {
+  R[0] = 1 - 2 * y * y - 2 * z * z;
+  R[1] = 2 * x * y - 2 * z * w;
+  R[2] = 2 * x * z + 2 * y * w;
+  R[3] = 2 * x * y + 2 * z * w;
+  R[4] = 1 - 2 * x * x - 2 * z * z;
+  R[5] = 2 * y * z - 2 * x * w;
+  R[6] = 2 * x * z - 2 * y * w;
+  R[7] = 2 * y * z + 2 * x * w;
+  R[8] = 1 - 2 * x * x - 2 * y * y;
+}
+
+// Camera covariance Cc = W3 * A * W3^T for a symmetric world covariance A.
+__device__ __forceinline__ void cam_cov(const Cam &c, const float A[9], float Cc[9]) {
+  const float *W = c.W;
+  float WA[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      WA[i * 3 + j] = W[i * 4] * A[j] + W[i * 4 + 1] * A[3 + j] + W[i * 4 + 2] * A[6 + j];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      Cc[i * 3 + j] = WA[i * 3] * W[j * 4] + WA[i * 3 + 1] * W[j * 4 + 1] + WA[i * 3 + 2] * W[j * 4 + 2];
+}
+
+struct Jac {
+  float J0, J2, J4, J5, inv_z, x_ndc, y_ndc, xc, yc, lim_x, lim_y;
+};
+
+// Perspective Jacobian with the 1.3x FOV clamp (kernel.cu:110-127).
+__device__ __forceinline__ Jac jacobian(const Cam &c, int width, int height, float3 p) {
+  Jac j;
+  j.lim_x = kFovClamp * fmaxf(c.cx, (float)width - c.cx) / c.fx;
+  j.lim_y = kFovClamp * fmaxf(c.cy, (float)height - c.cy) / c.fy;
+  j.inv_z = 1.0f / p.z;
+  j.x_ndc = p.x * j.inv_z;
+  j.y_ndc = p.y * j.inv_z;
+  j.xc = fminf(j.lim_x, fmaxf(-j.lim_x, j.x_ndc));
+  j.yc = fminf(j.lim_y, fmaxf(-j.lim_y, j.y_ndc));
+  j.J0 = c.fx * j.inv_z;
+  j.J2 = -c.fx * j.xc * j.inv_z;
+  j.J4 = c.fy * j.inv_z;
+  j.J5 = -c.fy * j.yc * j.inv_z;
+  return j;
+}
+
+// Image-space covariance (a, b, c) with low-pass and symmetrisation
+// (kernel.cu:46-155).
+__device__ __forceinline__ float3 image_cov(const Cam &c, int width, int height, float3 p,
+                                            float sx, float sy, float sz, float qx, float qy,
+                                            float qz, float qw) {
+  float R[9];
+  quat_to_rot(qx, qy, qz, qw, R);
+  float s2[3] = {sx * sx, sy * sy, sz * sz};
+  float Cw[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      Cw[i * 3 + k] = R[i * 3] * s2[0] * R[k * 3] + R[i * 3 + 1] * s2[1] * R[k * 3 + 1] +
+                      R[i * 3 + 2] * s2[2] * R[k * 3 + 2];
+  float Cc[9];
+  cam_cov(c, Cw, Cc);
+  Jac j = jacobian(c, width, height, p);
+  float A0 = j.J0 * Cc[0] + j.J2 * Cc[6];
+  float A1 = j.J0 * Cc[1] + j.J2 * Cc[7];
+  float A2 = j.J0 * Cc[2] + j.J2 * Cc[8];
+  float B0 = j.J4 * Cc[3] + j.J5 * Cc[6];
+  float B1 = j.J4 * Cc[4] + j.J5 * Cc[7];
+  float B2 = j.J4 * Cc[5] + j.J5 * Cc[8];
+  float c00 = A0 * j.J0 + A2 * j.J2;
+  float c01 = A1 * j.J4 + A2 * j.J5;
+  float c10 = B0 * j.J0 + B2 * j.J2;
+  float c11 = B1 * j.J4 + B2 * j.J5;
+  return make_float3(c00 + kLowPass, 0.5f * (c01 + c10), c11 + kLowPass);
+}
+
+// Result of the per-Gaussian projection with the reference's culling order
+// (kernel.cu:438-500). visible == false means mask = 0.
+struct Projected {
+  bool visible;
+  bool cov_written;  // the reference writes cov_image before the radius cull
+  float u, v, depth;
+  float3 cov, conic;
+  float ru, rv;
+};
+
+__device__ __forceinline__ Projected project_one(const Cam &c, int width, int height,
+                                                 float near_plane, float far_plane,
+                                                 float min_opacity, float min_radius,
+                                                 float max_radius, float px, float py,
+                                                 float pz, float sx, float sy, float sz,
+                                                 float qx, float qy, float qz, float qw,
+                                                 float opac) {
+  Projected r;
+  r.visible = false;
+  r.cov_written = false;
+  if (opac < min_opacity) return r;
+  float3 pc = to_camera(c, px, py, pz);
+  if (pc.z < near_plane || pc.z > far_plane) return r;
+  r.u = c.fx * pc.x / pc.z + c.cx;
+  r.v = c.fy * pc.y / pc.z + c.cy;
+  r.depth = pc.z;
+  r.cov = image_cov(c, width, height, pc, sx, sy, sz, qx, qy, qz, qw);
+  r.cov_written = true;
+  float det = r.cov.x * r.cov.z - r.cov.y * r.cov.y;
+  float inv_det = 1.0f / fmaxf(det, 1e-12f);
+  r.ru = fmaxf(sqrtf(r.cov.x), 1e-12f) * 3.0f;
+  r.rv = fmaxf(sqrtf(r.cov.z), 1e-12f) * 3.0f;
+  float radius = fmaxf(r.ru, r.rv);
+  if (radius < min_radius || radius > max_radius) return r;
+  if (r.u < -r.ru || r.u > (float)width + r.ru || r.v < -r.rv || r.v > (float)height + r.rv)
+    return r;
+  r.conic = make_float3(r.cov.z * inv_det, -r.cov.y * inv_det, r.cov.x * inv_det);
+  r.visible = true;
+  return r;
+}
+
+// Backward of projection + covariance for one Gaussian (kernel.cu:157-409).
+// The off-diagonal conic gradient enters the Jacobian term as the full g01,
+// as the reference does (kernel.cu:384-389).
+__device__ __forceinline__ void project_backward_one(
+    const Cam &c, int width, int height, float3 pc, float gu, float gv, float sx, float sy,
+    float sz, float qi, float qj, float qk, float qr, float3 cov, float gA, float gB, float gC,
+    float gm[3], float gs[3], float gq[4]) {
+  const float *W = c.W;
+  const float fx = c.fx, fy = c.fy;
+  Jac j = jacobian(c, width, height, pc);
+  float x = pc.x, y = pc.y, z = pc.z;
+  float iz2 = j.inv_z * j.inv_z;
+  float iz3 = iz2 * j.inv_z;
+  bool xcl = fabsf(j.x_ndc) > j.lim_x;
+  bool ycl = fabsf(j.y_ndc) > j.lim_y;
+  float gm0 = (gu * fx * (W[0] * z - W[8] * x) + gv * fy * (W[4] * z - W[8] * y)) * iz2;
+  float gm1 = (gu * fx * (W[1] * z - W[9] * x) + gv * fy * (W[5] * z - W[9] * y)) * iz2;
+  float gm2 = (-gu * fx * (W[10] * x - W[2] * z) - gv * fy * (W[10] * y - W[6] * z)) * iz2;
+
+  float U[6];
+  U[0] = j.J0 * W[0] + j.J2 * W[8];
+  U[1] = j.J0 * W[1] + j.J2 * W[9];
+  U[2] = j.J0 * W[2] + j.J2 * W[10];
+  U[3] = j.J4 * W[4] + j.J5 * W[8];
+  U[4] = j.J4 * W[5] + j.J5 * W[9];
+  U[5] = j.J4 * W[6] + j.J5 * W[10];
+
+  float R[9];
+  quat_to_rot(qi, qj, qk, qr, R);
+  float M[9] = {R[0] * sx, R[1] * sy, R[2] * sz, R[3] * sx, R[4] * sy,
+                R[5] * sz, R[6] * sx, R[7] * sy, R[8] * sz};
+
+  float a = cov.x, b = cov.y, cc = cov.z;
+  float det = a * cc - b * b;
+  float id = 1.0f / fmaxf(det, 1e-12f);
+  float id2 = id * id;
+  float D[3][3] = {{-cc * cc * id2, b * cc * id2, -b * b * id2},
+                   {2.0f * b * cc * id2, -(a * cc + b * b) * id2, 2.0f * a * b * id2},
+                   {-b * b * id2, a * b * id2, -a * a * id2}};
+  float gcon[3] = {gA, gB, gC};
+  float gE2[3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    gE2[r] = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) gE2[r] += gcon[k] * D[r][k];
+  }
+  float gE[9];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float t0 = U[r] * U[k];
+      float t1 = U[r] * U[3 + k];
+      float t2 = U[k] * U[3 + r];
+      float t3 = U[3 + r] * U[3 + k];
+      gE[r * 3 + k] = gE2[0] * t0 + 0.5f * gE2[1] * (t1 + t2) + gE2[2] * t3;
+    }
+  float gM[9];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int col = 0; col < 3; ++col) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) acc += (gE[r * 3 + k] + gE[k * 3 + r]) * M[k * 3 + col];
+      gM[r * 3 + col] = acc;
+    }
+  gs[0] = gM[0] * R[0] + gM[3] * R[3] + gM[6] * R[6];
+  gs[1] = gM[1] * R[1] + gM[4] * R[4] + gM[7] * R[7];
+  gs[2] = gM[2] * R[2] + gM[5] * R[5] + gM[8] * R[8];
+
+  float dqi[9] = {0.0f, 2.0f * sy * qj, 2.0f * sz * qk, 2.0f * sx * qj, -4.0f * sy * qi,
+                  -2.0f * sz * qr, 2.0f * sx * qk, 2.0f * sy * qr, -4.0f * sz * qi};
+  float dqj[9] = {-4.0f * sx * qj, 2.0f * sy * qi, 2.0f * sz * qr, 2.0f * sx * qi, 0.0f,
+                  2.0f * sz * qk, -2.0f * sx * qr, 2.0f * sy * qk, -4.0f * sz * qj};
+  float dqk[9] = {-4.0f * sx * qk, -2.0f * sy * qr, 2.0f * sz * qi, 2.0f * sx * qr,
+                  -4.0f * sy * qk, 2.0f * sz * qj, 2.0f * sx * qi, 2.0f * sy * qj, 0.0f};
+  float dqr[9] = {0.0f, -2.0f * sy * qk, 2.0f * sz * qj, 2.0f * sx * qk, 0.0f,
+                  -2.0f * sz * qi, -2.0f * sx * qj, 2.0f * sy * qi, 0.0f};
+  float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    q0 += gM[k] * dqi[k];
+    q1 += gM[k] * dqj[k];
+    q2 += gM[k] * dqk[k];
+    q3 += gM[k] * dqr[k];
+  }
+  gq[0] = q0;
+  gq[1] = q1;
+  gq[2] = q2;
+  gq[3] = q3;
+
+  float E[9];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      E[r * 3 + k] = M[r * 3] * M[k * 3] + M[r * 3 + 1] * M[k * 3 + 1] + M[r * 3 + 2] * M[k * 3 + 2];
+  float Cc[9];
+  cam_cov(c, E, Cc);
+
+  float g00 = gE2[0], g01 = gE2[1], g11 = gE2[2];
+  float GJ00 = g00 * j.J0;
+  float GJ01 = g01 * j.J4;
+  float GJ02 = g00 * j.J2 + g01 * j.J5;
+  float GJ10 = g01 * j.J0;
+  float GJ11 = g11 * j.J4;
+  float GJ12 = g01 * j.J2 + g11 * j.J5;
+  float dJ00 = 2.0f * (GJ00 * Cc[0] + GJ01 * Cc[3] + GJ02 * Cc[6]);
+  float dJ02 = 2.0f * (GJ00 * Cc[2] + GJ01 * Cc[5] + GJ02 * Cc[8]);
+  float dJ11 = 2.0f * (GJ10 * Cc[1] + GJ11 * Cc[4] + GJ12 * Cc[7]);
+  float dJ12 = 2.0f * (GJ10 * Cc[2] + GJ11 * Cc[5] + GJ12 * Cc[8]);
+  float gx = xcl ? 0.0f : dJ02 * (-fx * iz2);
+  float gy = ycl ? 0.0f : dJ12 * (-fy * iz2);
+  float dJ02dz = xcl ? (fx * j.xc * iz2) : (2.0f * fx * x * iz3);
+  float dJ12dz = ycl ? (fy * j.yc * iz2) : (2.0f * fy * y * iz3);
+  float gz = dJ00 * (-fx * iz2) + dJ11 * (-fy * iz2) + dJ02 * dJ02dz + dJ12 * dJ12dz;
+  gm[0] = gm0 + (W[0] * gx + W[4] * gy + W[8] * gz);
+  gm[1] = gm1 + (W[1] * gx + W[5] * gy + W[9] * gz);
+  gm[2] = gm2 + (W[2] * gx + W[6] * gy + W[10] * gz);
+}
+
+// ---- spherical harmonics ----------------------------------------------------
+
+struct ViewDir {
+  float x, y, z, inv_norm;
+};
+
+__device__ __forceinline__ ViewDir view_dir(float cpx, float cpy, float cpz, float px,
+                                            float py, float pz) {
+  float dx = px - cpx, dy = py - cpy, dz = pz - cpz;
+  float n = sqrtf(dx * dx + dy * dy + dz * dz);
+  ViewDir d;
+  d.inv_norm = 1.0f / (n + 1e-8f);
+  d.x = dx * d.inv_norm;
+  d.y = dy * d.inv_norm;
+  d.z = dz * d.inv_norm;
+  return d;
+}
+
+// Basis values 0..15 (kernel.cu:578-595).
+__device__ __forceinline__ void sh_basis(float x, float y, float z, float b[16]) {
+  float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+  b[0] = kC0;
+  b[1] = -kC1 * y;
+  b[2] = kC1 * z;
+  b[3] = -kC1 * x;
+  b[4] = kC2xy * xy;
+  b[5] = kC2xy * yz;
+  b[6] = kC2zz * (3 * zz - 1);
+  b[7] = kC2xy * xz;
+  b[8] = kC2xxyy * (xx - yy);
+  b[9] = kC3a * y * (xx - yy);
+  b[10] = kC3xyz * (x * y * z);
+  b[11] = kC3c * y * (4 * zz - xx - yy);
+  b[12] = kC3zzz * z * (2 * zz - 3 * xx - 3 * yy);
+  b[13] = kC3c * x * (4 * zz - xx - yy);
+  b[14] = kC3zxx * z * (xx - yy);
+  b[15] = kC3a * x * (xx - 3 * yy);
+}
+
+// Sigmoid the way the reference computes it (kernel.cu:608-610).
+__device__ __forceinline__ float ref_sigmoid(float r) {
+  return (float)(1.0 / (1.0 + (double)expf(-r)));
+}
+
+// d(view-dependent colour)/d(mean) through the normalised direction
+// (kernel.cu:674-781); g is d loss / d raw colour, rest points at the 45
+// coefficients (15 bases x rgb) of one Gaussian.
+template <typename RestAt>
+__device__ __forceinline__ float3 sh_dir_backward(const ViewDir &d, float g0, float g1,
+                                                  float g2, RestAt rest) {
+  float x = d.x, y = d.y, z = d.z;
+  float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+  float bx[15] = {0.0f, 0.0f, -kC1, kC2xy * y, 0.0f, 0.0f, kC2xy * z, 2.0f * kC2xxyy * x,
+                  2.0f * kC3a * x * y, kC3xyz * y * z, -2.0f * kC3c * x * y,
+                  -6.0f * kC3zzz * x * z, kC3c * (4.0f * zz - 3.0f * xx - yy),
+                  2.0f * kC3zxx * x * z, 3.0f * kC3a * (xx - yy)};
+  float by[15] = {-kC1, 0.0f, 0.0f, kC2xy * x, kC2xy * z, 0.0f, 0.0f, -2.0f * kC2xxyy * y,
+                  kC3a * (xx - 3.0f * yy), kC3xyz * x * z, kC3c * (4.0f * zz - xx - 3.0f * yy),
+                  -6.0f * kC3zzz * y * z, -2.0f * kC3c * x * y, -2.0f * kC3zxx * y * z,
+                  -6.0f * kC3a * x * y};
+  float bz[15] = {0.0f, kC1, 0.0f, 0.0f, kC2xy * y, 6.0f * kC2zz * z, kC2xy * x, 0.0f, 0.0f,
+                  kC3xyz * x * y, 8.0f * kC3c * y * z, 3.0f * kC3zzz * (2.0f * zz - xx - yy),
+                  8.0f * kC3c * x * z, kC3zxx * (xx - yy), 0.0f};
+  float in = d.inv_norm;
+  float j00 = (1.0f - xx) * in, j01 = -xy * in, j02 = -xz * in;
+  float j11 = (1.0f - yy) * in, j12 = -yz * in, j22 = (1.0f - zz) * in;
+  float gx = 0.f, gy = 0.f, gz = 0.f;
+#pragma unroll
+  for (int k = 0; k < 15; ++k) {
+    float px = bx[k] * j00 + by[k] * j01 + bz[k] * j02;
+    float py = bx[k] * j01 + by[k] * j11 + bz[k] * j12;
+    float pz = bx[k] * j02 + by[k] * j12 + bz[k] * j22;
+    float r0 = rest(k, 0), r1 = rest(k, 1), r2 = rest(k, 2);
+    gx += g0 * r0 * px + g1 * r1 * px + g2 * r2 * px;
+    gy += g0 * r0 * py + g1 * r1 * py + g2 * r2 * py;
+    gz += g0 * r0 * pz + g1 * r1 * pz + g2 * r2 * pz;
+  }
+  return make_float3(gx, gy, gz);
+}
+
+// ---- tiles --------------------------------------------------------------------
+
+// floorf followed by the float->int32 conversion (kernel.cu:804-807).
+__device__ __forceinline__ int floor_i32(float f) { return (int32_t)floorf(f); }
+
+struct TileRect {
+  int x0, x1, y0, y1;  // inclusive tile coordinates
+  bool empty;
+};
+
+// Tile rectangle of a Gaussian (kernel.cu:799-816).
+__device__ __forceinline__ TileRect tile_rect(float u, float v, float ru, float rv, int width,
+                                              int height) {
+  int u0 = min(max(0, floor_i32(u - ru)), width - 1);
+  int u1 = min(max(0, floor_i32(u + ru)), width - 1);
+  int v0 = min(max(0, floor_i32(v - rv)), height - 1);
+  int v1 = min(max(0, floor_i32(v + rv)), height - 1);
+  TileRect t;
+  t.empty = (u0 > u1 || v0 > v1);
+  t.x0 = u0 / GS_TILE;
+  t.x1 = u1 / GS_TILE;
+  t.y0 = v0 / GS_TILE;
+  t.y1 = v1 / GS_TILE;
+  return t;
+}
+
+__host__ __device__ __forceinline__ int tiles_x_of(int width) { return (width + GS_TILE - 1) / GS_TILE; }
+__host__ __device__ __forceinline__ int tiles_y_of(int height) { return (height + GS_TILE - 1) / GS_TILE; }
+
+}  // namespace gs

@@ -1,0 +1,495 @@
+"""Benchmark: data-parallel training step of the Gaussian-splatting rasterizer.
+
+Workload: N = 1,000,000 SH-degree-3 Gaussians with
+the config's seeded synthetic distributions, 1920x1080 views, fx = fy = 1100,
+cameras on a radius-8 orbit around the scene (view 0 is the config's camera
+at (0, 0, -8)), L1 loss against a uniform-random target image. One step per
+rank = activations, `views_per_rank` rendered views fwd+bwd through the
+package's public render(), gradient all-reduce over NCCL when world > 1,
+and one Adam step over the six parameter groups. Weak scaling: every rank
+renders its own views of a replicated scene.
+
+value = views/s over all ranks, device-timed with CUDA events, max over
+ranks. e2e = the same step through render() with each step's target images
+(uint8) and cameras copied from pinned host memory and the loss read back,
+wall-clock timed. See DESIGN.md for the roofline definitions.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+gs = importlib.import_module("3dgs_from_scratch_b200")
+nat = importlib.import_module("3dgs_from_scratch_b200._native")
+scenes = gs.scenes
+
+METRIC = "fwd+bwd ms/view (1M SH3 Gauss, 1080p); train views/s at 1/2/4/8 B200"
+PEAKS_PATH = os.path.join(HERE, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+# algorithmic bytes / flops ("Roofline")
+PRE_FWD_BYTES_PER_G = 281
+PRE_BWD_BYTES_PER_G = 504
+LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
+BLEND_FWD_FLOP_PER_PAIR = 22
+BLEND_BWD_FLOP_PER_PAIR = 60
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--views-per-rank", type=int, default=4)
+    p.add_argument("--config", type=int, default=1)
+    p.add_argument("--n", type=int, default=None, help="override Gaussian count (tests/profiling)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--cpu-sample-views", type=int, default=2)
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        smax = float(rows[0][2])
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": reasons,
+                "samples": len(rows)}
+
+
+class StageTimer:
+    """CUDA events around each C-ABI call of interest, on the launching stream."""
+
+    WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_blend_forward", "gs_blend_backward",
+             "gs_preprocess_backward")
+
+    def __init__(self):
+        self.events = {k: [] for k in self.WATCH}
+        self._orig = None
+
+    def __enter__(self):
+        self._orig = nat.call
+        timer = self
+
+        def call(name, *args):
+            if name not in timer.events:
+                return timer._orig(name, *args)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            rc = timer._orig(name, *args)
+            b.record()
+            timer.events[name].append((a, b))
+            return rc
+
+        nat.call = call
+        return self
+
+    def __exit__(self, *exc):
+        nat.call = self._orig
+        return False
+
+    def mean_ms(self):
+        torch.cuda.synchronize()
+        return {k: (sum(a.elapsed_time(b) for a, b in v) / len(v) if v else None)
+                for k, v in self.events.items()}
+
+
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle port (the reference's algorithm restated in C)
+# ---------------------------------------------------------------------------
+
+def cpu_fwd_bwd_views(cfg, raw_np, views, targets):
+    from oracle import oracle as orc
+
+    a = raw_np
+    K = scenes.intrinsic_for(cfg).numpy()
+    t0 = time.perf_counter()
+    for w2c, tgt in zip(views, targets):
+        img, st = orc.render_forward(w2c, K, cfg.width, cfg.height, a["means"], a["scales"],
+                                     a["quaternions"], a["opacities"], a["sh_coeffs_dc"],
+                                     a["sh_coeffs_rest"])
+        g = (np.sign(img - tgt) / img.size).astype(np.float32)
+        orc.render_backward(g, st, w2c, K, cfg.width, cfg.height, a["means"], a["scales"],
+                            a["quaternions"], a["opacities"], a["sh_coeffs_dc"],
+                            a["sh_coeffs_rest"])
+    return time.perf_counter() - t0
+
+
+def cpu_setup(cfg, n, views):
+    from oracle import oracle as orc
+
+    orc.set_num_threads(os.cpu_count() or 1)
+    raw = scenes.make_gaussians(cfg, seed=0, n=n)
+    act = {k: v.numpy() for k, v in scenes.activate(raw).items()}
+    cams = scenes.orbit_cameras(cfg, views).numpy()
+    rng = np.random.default_rng(0)
+    tg = [rng.uniform(0, 255, (cfg.height, cfg.width, 3)).astype(np.float32) for _ in range(views)]
+    return act, cams, tg, orc.num_threads()
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return platform.processor()
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cfg = scenes.CONFIGS[args.config]
+    act, cams, tg, threads = cpu_setup(cfg, args.n, 1)
+    for _ in range(args.warmup):
+        cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1])
+    times = [cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1]) for _ in range(args.steps)]
+    sec = statistics.median(times)
+    value = 1.0 / sec
+    sample = (f"1 full view per step (N={act['means'].shape[0]}, {cfg.width}x{cfg.height}), "
+              f"fwd+bwd, median of {args.steps}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "views/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1000.0, "ms_per_view": sec * 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, cfg, 1),
+        "cpu_baseline": {"value": value, "unit": "views/s", "cores": threads, "kind": "port",
+                         "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": value, "unit": "views/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, cfg, views_per_rank):
+    return {"workload": f"config {args.config}: {cfg.n if args.n is None else args.n} SH3 "
+                        f"Gaussians, {cfg.width}x{cfg.height}, {views_per_rank} view(s)/rank per "
+                        f"step, orbit r={cfg.camera_distance}, L1 vs uniform target, Adam step",
+            "global_batch": views_per_rank * max(args.gpus, 1), "views_per_rank": views_per_rank,
+            "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
+            "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)"}
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+class Trainer:
+    def __init__(self, cfg, n, views, world, rank, device):
+        self.cfg = cfg
+        self.world = world
+        self.device = device
+        raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
+        self.names = list(raw)
+        numel = sum(v.numel() for v in raw.values())
+        self.flat_grad = torch.zeros(numel, device=device)
+        self.params = {}
+        off = 0
+        for k, v in raw.items():
+            p = v.clone().requires_grad_(True)
+            p.grad = self.flat_grad[off:off + v.numel()].view_as(v)
+            off += v.numel()
+            self.params[k] = p
+        lrs = {"means": 1.6e-4, "scales": 5e-3, "quaternions": 1e-3, "opacities": 5e-2,
+               "sh_coeffs_dc": 2.5e-3, "sh_coeffs_rest": 2.5e-3 / 20}
+        self.opt = torch.optim.Adam([{"params": [self.params[k]], "lr": lrs[k]} for k in self.names],
+                                    eps=1e-15, betas=(0.9, 0.999), fused=True)
+        cams = scenes.orbit_cameras(cfg, views * world)
+        self.cams = cams[rank * views:(rank + 1) * views].to(device)
+        self.K = scenes.intrinsic_for(cfg).to(device)
+        g = torch.Generator(device=device).manual_seed(1234 + rank)
+        self.targets = [torch.rand((cfg.height, cfg.width, 3), device=device, generator=g) * 255.0
+                        for _ in range(views)]
+        # e2e inputs: uint8 targets and cameras in pinned host memory
+        self.host_targets = [(t.cpu().round().clamp(0, 255).to(torch.uint8)).pin_memory()
+                             for t in self.targets]
+        self.host_cams = self.cams.cpu().pin_memory()
+        self.host_K = self.K.cpu().pin_memory()
+        self.host_loss = torch.zeros(len(self.targets), dtype=torch.float32).pin_memory()
+
+    def step(self, e2e=False):
+        p = self.params
+        act = scenes.activate(p)
+        losses = []
+        for v in range(len(self.targets)):
+            if e2e:
+                w2c = self.host_cams[v].to(self.device, non_blocking=True)
+                K = self.host_K.to(self.device, non_blocking=True)
+                tgt = self.host_targets[v].to(self.device, non_blocking=True).float()
+            else:
+                w2c, K, tgt = self.cams[v], self.K, self.targets[v]
+            img, pts, radii = gs.render(w2c, K, self.cfg.width, self.cfg.height, act["means"],
+                                        act["scales"], act["quaternions"], act["opacities"],
+                                        act["sh_coeffs_dc"], act["sh_coeffs_rest"])
+            loss = torch.nn.functional.l1_loss(img / 255.0, tgt / 255.0)
+            loss.backward(retain_graph=v + 1 < len(self.targets))
+            losses.append(loss.detach())
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(self.flat_grad)
+        self.opt.step()
+        self.flat_grad.zero_()
+        total = torch.stack(losses)
+        if e2e:
+            self.host_loss.copy_(total, non_blocking=True)
+        return total
+
+
+def count_pairs(tr, view=0):
+    """Evaluated (pixel, Gaussian) pairs of one view, in the reference's
+    counting: list entries visited before the transmittance break."""
+    cr = gs.cuda_rasterizer
+    cfg = tr.cfg
+    with torch.no_grad():
+        act = scenes.activate(tr.params)
+        w2c = tr.cams[view]
+        pts, depths, cov, conic, radii, mask = cr.project_points(
+            act["means"], act["scales"], act["quaternions"], act["opacities"], w2c, tr.K, 0.01,
+            100.0, 1 / 255, 0.5, 128.0, cfg.width, cfg.height)
+        off, ids = cr.compute_tile_intersection(pts, radii, depths, mask, cfg.width, cfg.height)
+        W, H = cfg.width, cfg.height
+        colors = torch.full((pts.shape[0], 3), 0.5, device=pts.device)
+        work_t = torch.empty(H * W, device=pts.device)
+        work_e = torch.empty(H * W, device=pts.device, dtype=torch.int32)
+        image = torch.zeros((H, W, 3), device=pts.device)
+        nat.call("gs_rasterize", off.shape[0], off.data_ptr(), ids.shape[0], ids.data_ptr(),
+                 pts.shape[0], pts.data_ptr(), conic.data_ptr(), act["opacities"].data_ptr(), colors.data_ptr(),
+                 W, H, 1e-4, 1e-4, 9.21, image.data_ptr(), work_t.data_ptr(), work_e.data_ptr(),
+                 nat.stream_ptr())
+        tx = (W + 15) // 16
+        vv, uu = torch.meshgrid(torch.arange(H, device=pts.device),
+                                torch.arange(W, device=pts.device), indexing="ij")
+        tile = ((vv // 16) * tx + (uu // 16)).reshape(-1)
+        offl = torch.cat([off.long(), torch.tensor([ids.shape[0]], device=off.device)])
+        s = offl[tile]
+        e = offl[tile + 1]
+        broke = work_t < 1e-4
+        visited = torch.where(broke, work_e.long() - s, e - s)
+        return int(visited.sum().item()), int(ids.shape[0]), int(mask.sum().item())
+
+
+def main():
+    args = parse()
+    world, rank, local = setup_dist(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    device = torch.device("cuda", local)
+    cfg = scenes.CONFIGS[args.config]
+    V = args.views_per_rank
+    tr = Trainer(cfg, args.n, V, world, rank, device)
+    n = tr.params["means"].shape[0]
+
+    for _ in range(args.warmup):
+        tr.step()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    launches0 = nat.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk, StageTimer() as stages:
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            tr.step()
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+    launches = nat.launch_count() - launches0
+    ms_total = max_over_ranks(start.elapsed_time(end), world)
+    ms_step = ms_total / args.steps
+    value = world * V * args.steps / (ms_total / 1000.0)
+    stage_ms = stages.mean_ms()
+
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(2):
+            tr.step(e2e=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tr.step(e2e=True)
+            torch.cuda.current_stream().synchronize()  # loss is on the host
+        barrier(world)
+        sec = max_over_ranks(time.perf_counter() - t0, world)
+        h2d = sum(t.numel() for t in tr.host_targets) + V * (16 + 9) * 4
+        e2e = {"value": world * V * args.steps / sec, "unit": "views/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(V * 4),
+               "timing": "wall clock, max over ranks"}
+
+    # roofline of the dominant stage
+    hbm, bf16, src = peaks()
+    E, K, visible = count_pairs(tr)
+    T = ((cfg.width + 15) // 16) * ((cfg.height + 15) // 16)
+    clocks = clk.summary()
+    sm_mhz = clocks.get("sm_max_mhz") or 1965.0
+    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12  # TFLOP/s, nominal at max SM clock
+    roof = {}
+    if stage_ms.get("gs_preprocess_forward"):
+        gbs = PRE_FWD_BYTES_PER_G * n / (stage_ms["gs_preprocess_forward"] * 1e-3) / 1e9
+        roof["preprocess_fwd"] = {"bound": "hbm", "ms": stage_ms["gs_preprocess_forward"],
+                                  "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_preprocess_backward"):
+        gbs = PRE_BWD_BYTES_PER_G * n / (stage_ms["gs_preprocess_backward"] * 1e-3) / 1e9
+        roof["preprocess_bwd"] = {"bound": "hbm", "ms": stage_ms["gs_preprocess_backward"],
+                                  "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_tile_layout"):
+        gbs = (LAYOUT_BYTES_PER_PAIR * K + 4 * T) / (stage_ms["gs_tile_layout"] * 1e-3) / 1e9
+        roof["tile_layout"] = {"bound": "hbm", "ms": stage_ms["gs_tile_layout"], "achieved": gbs,
+                               "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    for key, nm, fl in (("blend_fwd", "gs_blend_forward", BLEND_FWD_FLOP_PER_PAIR),
+                        ("blend_bwd", "gs_blend_backward", BLEND_BWD_FLOP_PER_PAIR)):
+        if stage_ms.get(nm):
+            tf = fl * E / (stage_ms[nm] * 1e-3) / 1e12
+            roof[key] = {"bound": "fp32", "ms": stage_ms[nm], "achieved": tf, "peak": fp32_peak,
+                         "unit": "TFLOP/s", "frac": tf / fp32_peak}
+    dom = max(roof, key=lambda k: roof[k]["ms"]) if roof else None
+    roofline = None
+    if dom:
+        r = roof[dom]
+        roofline = {"kernel": dom, "bound": r["bound"], "achieved": r["achieved"],
+                    "peak": r["peak"], "unit": r["unit"], "frac": r["frac"], "traffic": None,
+                    "peak_source": (f"{src} MEASURED_PEAKS.json hbm_gbs" if r["bound"] == "hbm"
+                                    else "nominal FP32: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
+                                         " (MEASURED_PEAKS.json has no FP32 figure)"),
+                    "work_per_launch": (f"{E} evaluated pairs" if r["bound"] == "fp32"
+                                        else "see DESIGN.md")}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        act, cams, tg, threads = cpu_setup(cfg, args.n, args.cpu_sample_views)
+        sec = cpu_fwd_bwd_views(cfg, act, cams, tg)
+        cpu = {"value": args.cpu_sample_views / sec, "unit": "views/s", "cores": threads,
+               "kind": "port",
+               "sample": f"{args.cpu_sample_views} full views fwd+bwd of the same scene "
+                         f"(oracle/gs_oracle.c, OpenMP)", "cpu": cpu_model()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "ms_per_view": ms_step / V, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, cfg, V), "e2e": e2e, "gpu_launches": int(launches),
+            "clocks": clocks, "roofline": roofline, "stages": roof,
+            "pairs": {"K": K, "evaluated_fwd": E, "visible": visible, "tiles": T},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,227 @@
+/*
+ * gs_b200.h -- C ABI of the B200 Gaussian-splatting rasterizer.
+ *
+ * Every entry point takes raw DEVICE pointers, sizes and thresholds by value,
+ * and a cudaStream_t (passed as void*; NULL means the legacy default stream).
+ * Every launch is asynchronous on that stream. No entry point allocates
+ * memory: outputs and scratch are caller-owned (the *_scratch_bytes queries
+ * give the scratch sizes). No entry point synchronises the stream except
+ * gs_read_total, gs_check_status and gs_sync. Every entry point returns a
+ * status code (GS_OK = 0); no C++ exception crosses this boundary.
+ *
+ * Array layouts are those of the reference's tensors: fp32, C-contiguous,
+ * means (N,3), scales (N,3), quaternions (N,4) in (x, y, z, w) order,
+ * opacities (N), sh_dc (N,3), sh_rest (N,15,3), world_to_camera (4,4)
+ * row-major, intrinsic (3,3) row-major, images (H,W,3).
+ *
+ * Reference interfaces replaced (ruguangyou/3dgs_from_scratch):
+ *   src/cuda/rasterizer.cpp:141-464 -- the pybind11 module `cuda_rasterizer`
+ *   src/cuda/kernel.cu:1113-1505    -- the launch_* host functions
+ */
+#ifndef GS_B200_H
+#define GS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GS_API __attribute__((visibility("default")))
+#else
+#define GS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define GS_OK 0
+#define GS_ERR_INVALID_ARGUMENT 1   /* bad size, null pointer, misalignment */
+#define GS_ERR_CUDA 2               /* a CUDA call failed: see gs_last_cuda_error */
+#define GS_ERR_DEVICE_TIMEOUT 3     /* a bounded device-side wait gave up */
+#define GS_ERR_CAPACITY 4           /* scratch too small / count beyond 2^30 */
+
+/* Tile edge in pixels; the reference hard-codes 16 (src/cuda/wrapper.py:267). */
+#define GS_TILE 16
+
+/* Library version, last CUDA error code seen, and the number of kernels this
+ * library has launched since load (for launch accounting in benchmarks). */
+GS_API int gs_version(void);
+GS_API int gs_last_cuda_error(void);
+GS_API uint64_t gs_launch_count(void);
+
+/* Device status word: bounded spin-waits (the sort's decoupled look-back,
+ * the scan's look-back) record GS_ERR_DEVICE_TIMEOUT here instead of
+ * hanging. gs_check_status synchronises `stream`, returns and clears it. */
+GS_API int gs_check_status(void *stream);
+GS_API int gs_sync(void *stream);
+
+/* Self-test of the bounded waits: launches one thread that polls the device
+ * word *flag_dev (which the caller leaves 0) until the spin limit, then
+ * returns the status it recorded -- GS_ERR_DEVICE_TIMEOUT -- with the CUDA
+ * context intact. No counterpart in the reference (which has no waits). */
+GS_API int gs_selftest_bounded_wait(const uint32_t *flag_dev, void *stream);
+
+/* ---- reference module functions (rasterizer.cpp:141-440) ---------------- */
+
+/* Replaces project_points (rasterizer.cpp:141-191; kernel.cu:411-500).
+ * Outputs must be zeroed by the caller, mask (uint8, N) set to 1. */
+GS_API int gs_project_points(int n, const float *means, const float *scales, const float *quats,
+                      const float *opacities, const float *world_to_camera,
+                      const float *intrinsic, float near_plane, float far_plane,
+                      float min_opacity, float min_radius, float max_radius, int width,
+                      int height, float *points_img, float *depths, float *cov_img,
+                      float *conic, float *radii, uint8_t *mask, void *stream);
+
+/* Replaces project_points_backward (rasterizer.cpp:193-232; kernel.cu:502-543).
+ * Outputs must be zeroed by the caller (unmasked Gaussians are not written). */
+GS_API int gs_project_points_backward(int n, const float *grad_points_img, const float *grad_conic,
+                               const float *means, const float *scales, const float *quats,
+                               const float *world_to_camera, const float *intrinsic,
+                               const float *cov_img, const uint8_t *mask, int width,
+                               int height, float *grad_means, float *grad_scales,
+                               float *grad_quats, void *stream);
+
+/* Replaces evaluate_spherical_harmonics (rasterizer.cpp:234-257;
+ * kernel.cu:545-617). camera_pos is a device float[3]. */
+GS_API int gs_evaluate_sh(int n, const float *camera_pos, const float *means, const float *sh_dc,
+                   const float *sh_rest, const uint8_t *mask, int sh_sigmoid, float *colors,
+                   void *stream);
+
+/* Replaces evaluate_spherical_harmonics_backward (rasterizer.cpp:259-290;
+ * kernel.cu:619-782). */
+GS_API int gs_evaluate_sh_backward(int n, const float *grad_colors, const float *camera_pos,
+                            const float *means, const float *sh_rest, const float *colors,
+                            const uint8_t *mask, int sh_sigmoid, float *grad_means,
+                            float *grad_dc, float *grad_rest, void *stream);
+
+/* ---- tile intersection: count -> scan -> (host reads total) -> sort -------
+ * Together these replace compute_tile_intersection (rasterizer.cpp:292-359;
+ * kernel.cu:784-914 and the CUB sort of kernel.cu:1341-1388). The reference
+ * reads the total with a blocking .item() (rasterizer.cpp:322); here the
+ * caller reads the device total with gs_read_total once per view. */
+
+/* Per-Gaussian tile-rectangle counts (kernel.cu:784-818) into `counts`. */
+GS_API int gs_count_tiles(int n, const float *points_img, const float *radii, const uint8_t *mask,
+                   int width, int height, int32_t *counts, void *stream);
+
+/* Exclusive scan of n int32 counts into `offsets`, total into *total_dev
+ * (device int64). Scratch: gs_scan_scratch_bytes(n). */
+GS_API size_t gs_scan_scratch_bytes(int n);
+GS_API int gs_exclusive_scan(int n, const int32_t *counts, int32_t *offsets, int64_t *total_dev,
+                      void *scratch, size_t scratch_bytes, void *stream);
+
+/* Copies the device total (and the device status word) to the host;
+ * synchronises `stream`. Returns GS_ERR_DEVICE_TIMEOUT if a bounded wait
+ * gave up since the last check. */
+GS_API int gs_read_total(const int64_t *total_dev, int64_t *total_host, void *stream);
+
+/* Scratch for gs_tile_layout with `total` pairs on a width x height image. */
+GS_API size_t gs_tile_layout_scratch_bytes(int64_t total, int width, int height);
+
+/* Emits (tile << 32 | depth bits, id) pairs in Gaussian order and tile
+ * row-major order (kernel.cu:820-873), sorts them stably with an in-house
+ * onesweep LSD radix sort over the 32 + ceil(log2 tiles) significant bits
+ * (the reference sorts all 64 with CUB, same result), and writes the
+ * per-tile start offsets (kernel.cu:875-914). Outputs: keys_sorted (total,
+ * may be NULL), ids_sorted (total), indexing_offset (tiles_x * tiles_y). */
+GS_API int gs_tile_layout(int n, const float *points_img, const float *radii, const float *depths,
+                   const uint8_t *mask, const int32_t *offsets, int64_t total, int width,
+                   int height, int64_t *keys_sorted, int32_t *ids_sorted,
+                   int32_t *indexing_offset, void *scratch, size_t scratch_bytes,
+                   void *stream);
+
+/* Stable LSD radix sort of (uint64 key, int32 value) pairs on key bits
+ * [0, end_bit). Replaces radix_sort_double_buffer (kernel.cu:1341-1388).
+ * keys/vals are sorted in place; keys_alt/vals_alt are ping-pong buffers of
+ * the same size. Scratch: gs_sort_scratch_bytes(n). */
+GS_API size_t gs_sort_scratch_bytes(int64_t n);
+GS_API int gs_sort_pairs(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt,
+                  int32_t *vals_alt, int end_bit, void *scratch, size_t scratch_bytes,
+                  void *stream);
+
+/* Replaces rasterize (rasterizer.cpp:361-395; kernel.cu:916-987). image
+ * must be zeroed by the caller. n is the number of Gaussians (rows of the
+ * per-Gaussian arrays); list entries outside [0, n) contribute nothing. work_final_t (float, H*W) and
+ * work_pixel_end (int32, H*W) are caller-owned work buffers that receive
+ * each pixel's final transmittance and end index. */
+GS_API int gs_rasterize(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                 const int32_t *ids_sorted, int n, const float *points_img, const float *conic,
+                 const float *opacities, const float *colors, int width, int height,
+                 float alpha_threshold, float transmittance_threshold,
+                 float chi_squared_threshold, float *image, float *work_final_t,
+                 int32_t *work_pixel_end, void *stream);
+
+/* Replaces rasterize_backward (rasterizer.cpp:397-440; kernel.cu:989-1111).
+ * Gradient outputs must be zeroed by the caller (they are accumulated).
+ * Like the reference, it first replays the forward per pixel (into the
+ * caller-owned work buffers, H*W each). */
+GS_API int gs_rasterize_backward(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                          const int32_t *ids_sorted, int n, const float *grad_image,
+                          const float *points_img, const float *conic,
+                          const float *opacities, const float *colors, int width,
+                          int height, float alpha_threshold, float transmittance_threshold,
+                          float chi_squared_threshold, float *grad_points_img,
+                          float *grad_conic, float *grad_opacities, float *grad_colors,
+                          float *work_final_t, int32_t *work_pixel_end, void *stream);
+
+/* ---- fused render path (used by render() in the Python package) ---------
+ * gs_preprocess_forward replaces project_points + evaluate_spherical_harmonics
+ * + the colour shift/clamp of wrapper.py:264-265 + count_tiles + the cumsum
+ * of rasterizer.cpp:319 in one pass: projection, EWA covariance, conic,
+ * radii, SH colour, tile count, and the exclusive scan of the tile counts
+ * (tile_offsets, total into *total_dev). The splat record is float[8] per
+ * Gaussian: conic (a, b, c), opacity, colour (r, g, b), 0. Every output
+ * element is written (zeros for culled Gaussians). tile_counts may be NULL.
+ * camera_pos is the device float[3] -R^T t (wrapper.py:260).
+ * Scratch: gs_preprocess_scratch_bytes(n). */
+GS_API size_t gs_preprocess_scratch_bytes(int n);
+GS_API int gs_preprocess_forward(int n, const float *means, const float *scales, const float *quats,
+                          const float *opacities, const float *sh_dc, const float *sh_rest,
+                          const float *world_to_camera, const float *intrinsic,
+                          const float *camera_pos, float near_plane, float far_plane,
+                          float min_opacity, float min_radius, float max_radius, int width,
+                          int height, int sh_sigmoid, float *points_img, float *depths,
+                          float *radii, uint8_t *mask, float *splat, int32_t *tile_counts,
+                          int32_t *tile_offsets, int64_t *total_dev, void *scratch,
+                          size_t scratch_bytes, void *stream);
+
+/* Blend forward over the splat records; also writes each pixel's final
+ * transmittance and end index (one past its last contributing list entry).
+ * Every pixel of the image (H,W,3) is written. */
+GS_API int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                     const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
+                     int width, int height, float alpha_threshold,
+                     float transmittance_threshold, float chi_squared_threshold,
+                     float *image, float *final_t, int32_t *pixel_end, void *stream);
+
+/* Blend backward: gradient outputs (grad_points_img (N,2), grad_splat (N,8))
+ * must be zeroed by the caller (they are accumulated). */
+GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                      const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
+                      const float *grad_image, const float *final_t,
+                      const int32_t *pixel_end, int width, int height,
+                      float alpha_threshold, float transmittance_threshold,
+                      float chi_squared_threshold, float *grad_points_img,
+                      float *grad_splat, void *stream);
+
+/* Fused preprocess backward: projection, covariance and SH chain for every
+ * Gaussian (zeros for culled ones), writing every output element. The
+ * upstream gradients are read with element strides (so column views of a
+ * packed buffer work): grad_points_img at gp[i*gp_stride + {0,1}], the splat
+ * gradient at gs[i*gs_stride + {0..6}] (conic a,b,c, opacity, r, g, b).
+ * grad_opacities receives the opacity gradient (may be NULL). */
+GS_API int gs_preprocess_backward(int n, const float *means, const float *scales,
+                           const float *quats, const float *sh_dc, const float *sh_rest,
+                           const float *world_to_camera, const float *intrinsic,
+                           const float *camera_pos, int width, int height, int sh_sigmoid,
+                           const uint8_t *mask, const float *grad_points_img, int gp_stride,
+                           const float *grad_splat, int gs_stride, float *grad_means,
+                           float *grad_scales, float *grad_quats, float *grad_opacities,
+                           float *grad_dc, float *grad_rest, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GS_B200_H */
