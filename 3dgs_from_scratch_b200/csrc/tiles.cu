@@ -161,7 +161,7 @@ constexpr uint32_t kLbValue = (1u << 30) - 1;
 
 // Histogram of every pass's digits in one read of the keys.
 __global__ void __launch_bounds__(256) sort_histogram_kernel(const uint64_t *__restrict__ keys,
-                                                             int64_t n, int passes,
+                                                             int64_t n, int passes, int end_bit,
                                                              uint32_t *__restrict__ hist) {
   __shared__ uint32_t sh[kMaxPasses * 256];
   for (int k = threadIdx.x; k < passes * 256; k += blockDim.x) sh[k] = 0;
@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(256) sort_histogram_kernel(const uint64_t *__r
     const bool valid = idx < n;
     const uint64_t key = valid ? keys[idx] : 0;
     for (int p = 0; p < passes; ++p) {
-      const uint32_t d = valid ? (uint32_t)((key >> (8 * p)) & 0xff) : 0x100u;
+      const int bits = min(8, end_bit - 8 * p);
+      const uint32_t d = valid ? (uint32_t)((key >> (8 * p)) & ((1u << bits) - 1u)) : 0x100u;
       const uint32_t peers = __match_any_sync(0xffffffffu, d);
       const uint32_t leader = 31 - __clz(peers);
       if (valid && lane == leader) atomicAdd(&sh[p * 256 + d], (uint32_t)__popc(peers));
@@ -224,7 +225,7 @@ struct SortSmem {
 __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
     const uint64_t *__restrict__ keys_in, const int32_t *__restrict__ vals_in,
     uint64_t *__restrict__ keys_out, int32_t *__restrict__ vals_out, int64_t n, int shift,
-    const uint32_t *__restrict__ hist, uint32_t *__restrict__ lookback,
+    uint32_t dmask, const uint32_t *__restrict__ hist, uint32_t *__restrict__ lookback,
     uint32_t *__restrict__ ticket, uint32_t *status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SortSmem &S = *reinterpret_cast<SortSmem *>(smem_raw);
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   for (int k = 0; k < kSortItems; ++k) {
     const int64_t idx = base + k * 32 + lane;
     const bool valid = idx < n;
-    const uint32_t d = valid ? (uint32_t)((key[k] >> shift) & 0xff) : 0x100u;
+    const uint32_t d = valid ? (uint32_t)((key[k] >> shift) & dmask) : 0x100u;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const uint32_t leader = 31 - __clz(peers);
     uint32_t old = 0;
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   for (int k = 0; k < kSortItems; ++k) {
     const int64_t idx = base + k * 32 + lane;
     if (idx < n) {
-      const uint32_t dk = (uint32_t)((key[k] >> shift) & 0xff);
+      const uint32_t dk = (uint32_t)((key[k] >> shift) & dmask);
       const uint32_t pos = S.lstart[dk] + S.whist[warp][dk] + rank[k];
       S.keys[pos] = key[k];
       S.vals[pos] = val[k];
@@ -322,7 +323,7 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   const int valid_count = (int)min((int64_t)kSortTile, n - tile_base);
   for (int p = t; p < valid_count; p += kSortThreads) {
     const uint64_t kk = S.keys[p];
-    const uint32_t dk = (uint32_t)((kk >> shift) & 0xff);
+    const uint32_t dk = (uint32_t)((kk >> shift) & dmask);
     const uint32_t out = S.gbase[dk] + ((uint32_t)p - S.lstart[dk]);
     if ((int64_t)out < n) {  // always true unless a look-back gave up
       keys_out[out] = kk;
@@ -364,10 +365,12 @@ static SortLayout sort_layout(int64_t n) {
   return L;
 }
 
-// Sorts (keys, vals) on bits [0, 8*passes); the result ends in the buffers
-// selected by the parity of `passes` (even: keys/vals, odd: alt).
+// Sorts (keys, vals) on bits [0, end_bit) in ceil(end_bit / 8) passes; the
+// result ends in the buffers selected by the parity of the pass count
+// (even: keys/vals, odd: alt).
 static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt,
-                    int32_t *vals_alt, int passes, void *scratch, cudaStream_t st) {
+                    int32_t *vals_alt, int end_bit, void *scratch, cudaStream_t st) {
+  const int passes = (end_bit + 7) / 8;
   if (n <= 0 || passes <= 0) return GS_OK;
   if (n > (int64_t)kLbValue) return GS_ERR_CAPACITY;
   SortLayout L = sort_layout(n);
@@ -383,7 +386,7 @@ static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int64_t hb = (n + 255) / 256;
   int hblocks = (int)(hb < (int64_t)sms * 4 ? hb : (int64_t)sms * 4);
-  sort_histogram_kernel<<<hblocks, 256, 0, st>>>(keys, n, passes, hist);
+  sort_histogram_kernel<<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
   count_launch();
   static int attr_done[64] = {0};
   const size_t smem = sizeof(SortSmem);
@@ -395,8 +398,10 @@ static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt
   uint64_t *kin = keys, *kout = keys_alt;
   int32_t *vin = vals, *vout = vals_alt;
   for (int p = 0; p < passes; ++p) {
+    const int bits = end_bit - 8 * p < 8 ? end_bit - 8 * p : 8;
     onesweep_pass_kernel<<<L.tiles, kSortThreads, smem, st>>>(
-        kin, vin, kout, vout, n, 8 * p, hist + 256 * p, lookback + (size_t)p * L.tiles * 256,
+        kin, vin, kout, vout, n, 8 * p, (1u << bits) - 1u, hist + 256 * p,
+        lookback + (size_t)p * L.tiles * 256,
         tickets + p, device_status_word());
     count_launch();
     uint64_t *tk = kin;
@@ -409,10 +414,10 @@ static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt
   return launch_status();
 }
 
-static int passes_for_tiles(int num_tiles) {
+static int key_bits_for_tiles(int num_tiles) {
   int tile_bits = 0;
   while ((1ll << tile_bits) < (long long)num_tiles) ++tile_bits;
-  return (32 + tile_bits + 7) / 8;
+  return 32 + tile_bits;
 }
 
 }  // namespace gs
@@ -466,7 +471,7 @@ extern "C" int gs_sort_pairs(int64_t n, uint64_t *keys, int32_t *vals, uint64_t 
   if (scratch == nullptr || scratch_bytes < gs_sort_scratch_bytes(n)) return GS_ERR_CAPACITY;
   int passes = (end_bit + 7) / 8;
   cudaStream_t st = as_stream(stream);
-  int rc = run_sort(n, keys, vals, keys_alt, vals_alt, passes, scratch, st);
+  int rc = run_sort(n, keys, vals, keys_alt, vals_alt, end_bit, scratch, st);
   if (rc) return rc;
   if (passes & 1) {
     rc = cuda_status(cudaMemcpyAsync(keys, keys_alt, n * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
@@ -509,7 +514,8 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
   uint64_t *keys_b = reinterpret_cast<uint64_t *>(p + kbytes);
   int32_t *vals_b = reinterpret_cast<int32_t *>(p + 2 * kbytes);
   void *sort_scratch = p + 2 * kbytes + vbytes;
-  const int passes = passes_for_tiles(num_tiles);
+  const int key_bits = key_bits_for_tiles(num_tiles);
+  const int passes = (key_bits + 7) / 8;
   // Emit into the buffer pair that the final pass does not write, so the
   // sorted result lands in (keys_a, ids_sorted).
   uint64_t *k0 = (passes & 1) ? keys_b : keys_a;
@@ -522,7 +528,7 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
         depths, mask, offsets, width, height, total, k0, v0);
     count_launch();
   }
-  rc = run_sort(total, k0, v0, k1, v1, passes, sort_scratch, st);
+  rc = run_sort(total, k0, v0, k1, v1, key_bits, sort_scratch, st);
   if (rc) return rc;
   ranges_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(keys_a, total, num_tiles,
                                                                   indexing_offset);

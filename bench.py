@@ -319,9 +319,11 @@ class Trainer:
             img, pts, radii = gs.render(w2c, K, self.cfg.width, self.cfg.height, act["means"],
                                         act["scales"], act["quaternions"], act["opacities"],
                                         act["sh_coeffs_dc"], act["sh_coeffs_rest"])
-            loss = torch.nn.functional.l1_loss(img / 255.0, tgt / 255.0)
-            loss.backward(retain_graph=v + 1 < len(self.targets))
-            losses.append(loss.detach())
+            losses.append(torch.nn.functional.l1_loss(img / 255.0, tgt / 255.0))
+        # one backward per step: the views' gradients meet at the activated
+        # parameters, so the activation backward runs once
+        torch.stack(losses).sum().backward()
+        losses = [x.detach() for x in losses]
         if self.world > 1:
             import torch.distributed as dist
 
