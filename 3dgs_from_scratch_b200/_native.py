@@ -46,6 +46,7 @@ SIGNATURES = {
     "gs_count_tiles": (I, [I, P, P, P, I, I, P, P]),
     "gs_scan_scratch_bytes": (SZ, [I]),
     "gs_exclusive_scan": (I, [I, P, P, P, P, SZ, P]),
+    "gs_exclusive_scan_noalloc": (I, [I, P, P, P, P]),
     "gs_read_total": (I, [P, P, P]),
     "gs_tile_layout_scratch_bytes": (SZ, [I64, I, I]),
     "gs_tile_layout": (I, [I, P, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),

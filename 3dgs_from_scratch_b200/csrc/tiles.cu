@@ -535,3 +535,56 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
   count_launch();
   return launch_status();
 }
+
+// ---- exclusive scan without caller-provided scratch -----------------------
+//
+// For callers that can hand over their input and output buffers but may not
+// allocate device memory themselves -- e.g. a host application that owns all
+// GPU memory through its own allocator, or a frame loop where a cudaMalloc /
+// cudaFree (which synchronise the device) is not allowed. The look-back state
+// the scan needs lives in this fixed device array instead: 64 KiB, enough for
+// up to kNoAllocScanMaxN counts, held by every GPU that loads the library
+// until the process exits.
+constexpr int kNoAllocScanMaxN = 1 << 24;  // 16,777,216 counts
+constexpr int kNoAllocScanWords = (kNoAllocScanMaxN + kScanTile - 1) / kScanTile + 1;
+static __device__ __align__(256) uint64_t g_noalloc_scan_words[kNoAllocScanWords];
+
+static uint64_t *g_noalloc_scan_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_scan_words for the current device, looked up
+// once per device (host code may not use the symbol itself as a pointer).
+static int noalloc_scan_words(uint64_t **out) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev));
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return GS_ERR_INVALID_ARGUMENT;
+  if (g_noalloc_scan_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scan_words));
+    if (rc) return rc;
+    g_noalloc_scan_ptr[dev] = reinterpret_cast<uint64_t *>(p);
+  }
+  *out = g_noalloc_scan_ptr[dev];
+  return GS_OK;
+}
+
+extern "C" int gs_exclusive_scan_noalloc(int n, const int32_t *counts, int32_t *offsets,
+                                         int64_t *total_dev, void *stream) {
+  if (n < 0 || total_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  if (n > kNoAllocScanMaxN) return GS_ERR_CAPACITY;
+  cudaStream_t st = as_stream(stream);
+  if (n == 0) return cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
+  if (counts == nullptr || offsets == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  uint64_t *words = nullptr;
+  int rc = noalloc_scan_words(&words);
+  if (rc) return rc;
+  const int tiles = (n + kScanTile - 1) / kScanTile;
+  // The array keeps the previous call's look-back words and ticket: clear the
+  // part this call uses (tiles + 1 words) before the launch, on the same stream.
+  rc = cuda_status(cudaMemsetAsync(words, 0, (size_t)(tiles + 1) * sizeof(uint64_t), st));
+  if (rc) return rc;
+  scan_kernel<<<tiles, kScanThreads, 0, st>>>(n, counts, offsets, total_dev, words, tiles,
+                                              device_status_word());
+  count_launch();
+  return launch_status();
+}

@@ -111,6 +111,20 @@ GS_API size_t gs_scan_scratch_bytes(int n);
 GS_API int gs_exclusive_scan(int n, const int32_t *counts, int32_t *offsets, int64_t *total_dev,
                       void *scratch, size_t scratch_bytes, void *stream);
 
+/* Same exclusive scan as gs_exclusive_scan, for callers that pass their
+ * input and output buffers but may not allocate device memory (e.g. a host
+ * application that owns all GPU memory through its own allocator, or a frame
+ * loop that must not call cudaMalloc/cudaFree, which synchronise the device).
+ * It allocates nothing: the look-back state lives in a fixed 64 KiB device
+ * array inside the library, so n is limited to 16,777,216 (larger n returns
+ * GS_ERR_CAPACITY). The first call on a device looks up that array's address
+ * (cudaGetSymbolAddress) and should come before any stream capture. All calls
+ * share the one array: calls whose kernels overlap on the GPU race, so issue
+ * them on one stream or otherwise serialise them. No counterpart in the
+ * reference, which allocates its scan output with torch (rasterizer.cpp:319). */
+GS_API int gs_exclusive_scan_noalloc(int n, const int32_t *counts, int32_t *offsets,
+                                     int64_t *total_dev, void *stream);
+
 /* Copies the device total (and the device status word) to the host;
  * synchronises `stream`. Returns GS_ERR_DEVICE_TIMEOUT if a bounded wait
  * gave up since the last check. */
