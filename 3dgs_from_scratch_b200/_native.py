@@ -48,16 +48,15 @@ SIGNATURES = {
     "gs_exclusive_scan": (I, [I, P, P, P, P, SZ, P]),
     "gs_exclusive_scan_noalloc": (I, [I, P, P, P, P]),
     "gs_read_total": (I, [P, P, P]),
-    "gs_tile_layout_scratch_bytes": (SZ, [I64, I, I]),
-    "gs_tile_layout": (I, [I, P, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
+    "gs_tile_layout_scratch_bytes": (SZ, [I, I64, I, I]),
+    "gs_tile_layout": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
     "gs_sort_scratch_bytes": (SZ, [I64]),
     "gs_sort_pairs": (I, [I64, P, P, P, P, I, P, SZ, P]),
     "gs_rasterize": (I, [I, P, I64, P, I, P, P, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_rasterize_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P, P, P,
                                   P, P]),
-    "gs_preprocess_scratch_bytes": (SZ, [I]),
     "gs_preprocess_forward": (I, [I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I, P, P, P,
-                                  P, P, P, P, P, P, SZ, P]),
+                                  P, P, P, P, P]),
     "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P]),
     "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, I, I, I, P, P, I, P, I, P, P, P, P,

@@ -1,33 +1,36 @@
 // blend.cu -- per-tile alpha blending, forward and backward.
 //
-// One 256-thread block per 16x16 tile, one thread per pixel. Warp w owns an
-// 8x4 pixel sub-block (2 across, 4 down), so a warp's pixels are spatially
-// compact. The tile's Gaussian list is streamed in batches of 256: each
-// thread stages one Gaussian's record in shared memory, together with an
-// 8-bit mask of the sub-blocks whose pixels that Gaussian can reach (a
-// conservative bound; see reach_mask), and then every warp walks the batch
-// from shared memory, skipping records its sub-block cannot see as one
-// uniform branch. Per pixel the arithmetic is the reference's, operation for
+// One 128-thread block per 16x16 tile, two pixels per thread (two
+// independent dependency chains per record). Warp w owns an 8x8 pixel block,
+// so a warp's pixels are spatially compact. The tile's Gaussian list is
+// streamed in batches of 256: each thread stages two Gaussians' records in
+// shared memory, together with a 4-bit mask of the warp blocks whose pixels
+// that Gaussian can reach (a conservative bound; see reach_mask), and then
+// every warp walks the batch from shared memory, skipping records its block
+// cannot see as one uniform branch. Per pixel the arithmetic is the reference's, operation for
 // operation (ruguangyou/3dgs_from_scratch src/cuda/kernel.cu:954-982 forward,
 // 1066-1110 backward), so images and per-pixel gradient terms match it.
 //
 // The forward records each pixel's final transmittance and the index one past
 // its last contributing list entry, so the backward needs no forward replay.
-// The backward walks each batch back to front, pre-reduces the 9 gradient
-// terms of a (warp, Gaussian) pair with a transposing warp-shuffle reduction
-// (14 shuffles instead of 45), accumulates warps into shared memory, and
-// issues one vector atomic per gradient group per (tile, Gaussian).
+// The backward walks each batch back to front, sums a thread's two pixels,
+// pre-reduces the 9 gradient terms of a (warp, Gaussian) pair with a
+// transposing warp-shuffle reduction (14 shuffles instead of 45), accumulates
+// warps into shared memory, and issues one vector atomic per gradient group
+// per (tile, Gaussian).
 #include "gs_common.cuh"
 
 namespace gs {
 
-constexpr int kBlendThreads = 256;
-constexpr int kBatch = 256;
+constexpr int kBlendThreads = 128;  // 4 warps per 16x16 tile, 2 pixels per thread
+constexpr int kBatch = 256;         // records staged per batch (2 per thread)
+constexpr int kWarps = kBlendThreads / 32;
 
-// Pixel owned by a thread: warp w -> 8x4 sub-block at (8*(w&1), 4*(w>>1)).
+// Pixels owned by thread t: warp w covers the 8x8 block at (8*(w&1), 8*(w>>1));
+// lane l takes column l&7 and rows (l>>3) and (l>>3)+4 of that block.
 __device__ __forceinline__ int2 pixel_in_tile(int t) {
   int w = t >> 5, l = t & 31;
-  return make_int2(8 * (w & 1) + (l & 7), 4 * (w >> 1) + (l >> 3));
+  return make_int2(8 * (w & 1) + (l & 7), 8 * (w >> 1) + (l >> 3));
 }
 
 // Gaussian record in shared memory: g0 = (u, v, A, B), g1 = (C, opacity, r, g), b.
@@ -36,22 +39,22 @@ struct Rec {
   float b;
 };
 
-// Bitmask of the tile's 8 warp sub-blocks that may hold a pixel with
-// q <= q_cut, where q_cut = min(chi2, 2 ln(opacity / alpha_thr)) bounds both
-// of the reference's skip tests (q > chi2, alpha < alpha_thr). The ellipse
-// {d : d^T Q d <= qc} lies in the box |dx| <= sqrt(qc C / det),
+// Bitmask of the tile's 4 warp blocks (8x8 pixels each) that may hold a pixel
+// with q <= q_cut, where q_cut = min(chi2, 2 ln(opacity / alpha_thr)) bounds
+// both of the reference's skip tests (q > chi2, alpha < alpha_thr). The
+// ellipse {d : d^T Q d <= qc} lies in the box |dx| <= sqrt(qc C / det),
 // |dy| <= sqrt(qc A / det). The float evaluation of q at a pixel has a
 // relative error below 3e-7 * R with R = 2 (A + C)^2 / det (the ratio of the
 // summed term magnitudes to q); conics with R >= 2000 reach everything, and
 // for the rest qc = 1.01 q_cut + 0.05 exceeds q_cut by far more than that
 // error, so a skipped record fails one of the reference's tests at every
-// pixel of the sub-block. Non-finite input reaches everything.
+// pixel of the block. Non-finite input reaches everything.
 __device__ __forceinline__ uint32_t reach_mask(float u, float v, float A, float B, float C,
                                                float opac, float alpha_thr, float chi_thr,
                                                int tile_x0, int tile_y0) {
   double q_cut = (double)chi_thr;
   if (alpha_thr > 0.0f) {
-    if (!(opac > 0.0f)) return 0xffu;  // degenerate opacity: evaluate normally
+    if (!(opac > 0.0f)) return 0xfu;  // degenerate opacity: evaluate normally
     double qa = 2.0 * log((double)opac / (double)alpha_thr);
     q_cut = fmin(q_cut, qa);
   }
@@ -59,16 +62,16 @@ __device__ __forceinline__ uint32_t reach_mask(float u, float v, float A, float 
   double det = a * c - b * b;
   if (!(A > 0.0f) || !(C > 0.0f) || !(det > 0.0) || !isfinite(u) || !isfinite(v) ||
       !isfinite(q_cut) || !(2.0 * (a + c) * (a + c) < 2000.0 * det))
-    return 0xffu;
+    return 0xfu;
   if (q_cut < -0.05) return 0u;  // opacity below the alpha threshold: alpha < thr everywhere
   double qc = fmax(q_cut, 0.0) * 1.01 + 0.05;
   double hx = sqrt(qc * c / det);
   double hy = sqrt(qc * a / det);
   uint32_t m = 0;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    double bx0 = tile_x0 + 8 * (w & 1), by0 = tile_y0 + 4 * (w >> 1);
-    bool hit = (u + hx >= bx0) && (u - hx <= bx0 + 7.0) && (v + hy >= by0) && (v - hy <= by0 + 3.0);
+  for (int w = 0; w < kWarps; ++w) {
+    double bx0 = tile_x0 + 8 * (w & 1), by0 = tile_y0 + 8 * (w >> 1);
+    bool hit = (u + hx >= bx0) && (u - hx <= bx0 + 7.0) && (v + hy >= by0) && (v - hy <= by0 + 7.0);
     m |= hit ? (1u << w) : 0u;
   }
   return m;
@@ -104,6 +107,37 @@ __device__ __forceinline__ Rec load_rec(int id, int n, const float2 *__restrict_
   return r;
 }
 
+// Forward state of one pixel.
+struct FwdPx {
+  float fu, fv, T, r, g, b;
+  int last;
+  bool done;
+};
+
+// One list entry for one pixel: kernel.cu:955-981, operation for operation.
+template <bool ACCUM>
+__device__ __forceinline__ void fwd_step(FwdPx &p, const float4 &g0, const float4 &g1, float cb,
+                                         int k, float alpha_thr, float trans_thr,
+                                         float chi_thr) {
+  const float du = p.fu - g0.x;
+  const float dv = p.fv - g0.y;
+  const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
+  float exponent = inv00 * du * du + 2.0f * inv01 * du * dv + inv11 * dv * dv;
+  if (exponent > chi_thr) return;
+  float alpha = expf(-0.5f * exponent) * g1.y;
+  if (alpha < alpha_thr) return;
+  if (ACCUM) {
+    float weight = alpha * p.T;
+    p.r += weight * g1.z;
+    p.g += weight * g1.w;
+    p.b += weight * cb;
+  }
+  float one_minus_alpha = 1.0f - alpha + kTransEps;
+  p.T *= one_minus_alpha;
+  p.last = k + 1;
+  if (p.T < trans_thr) p.done = true;
+}
+
 // Forward blend. With ACCUM = false only the transmittance bookkeeping is
 // done (the replay used by the reference-API backward).
 template <bool PACKED, bool ACCUM>
@@ -124,66 +158,59 @@ __global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(
   const int tile_x0 = (tile % tx) * GS_TILE, tile_y0 = (tile / tx) * GS_TILE;
   const int t = threadIdx.x, warp = t >> 5;
   const int2 pp = pixel_in_tile(t);
-  const int u = tile_x0 + pp.x, v = tile_y0 + pp.y;
-  const bool inside = (u < width) && (v < height);
-  const float fu = (float)u, fv = (float)v;
+  const int u = tile_x0 + pp.x, v0 = tile_y0 + pp.y, v1 = v0 + 4;
+  const bool in0 = (u < width) && (v0 < height);
+  const bool in1 = (u < width) && (v1 < height);
 
   const int s = offsets[tile];
   const int e = (tile + 1 < num_tiles) ? offsets[tile + 1] : (int)total;
 
-  float T = 1.0f, cr = 0.f, cg = 0.f, cb = 0.f;
-  int last = s;
-  bool done = !inside;
+  FwdPx p0{(float)u, (float)v0, 1.0f, 0.f, 0.f, 0.f, s, !in0};
+  FwdPx p1{(float)u, (float)v1, 1.0f, 0.f, 0.f, 0.f, s, !in1};
 
   for (int base = s; base < e; base += kBatch) {
-    if (__syncthreads_count(!done) == 0) break;
-    const int k = base + t;
-    if (k < e) {
-      int id = __ldg(ids + k);
-      Rec r = load_rec<PACKED>(id, n, points, splat, conic, opac, colors);
-      s_g0[t] = r.g0;
-      s_g1[t] = r.g1;
-      s_b[t] = r.b;
-      s_mask[t] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y, alpha_thr,
-                                      chi_thr, tile_x0, tile_y0);
+    if (__syncthreads_count(!(p0.done && p1.done)) == 0) break;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int slot = t + h * kBlendThreads;
+      const int k = base + slot;
+      if (k < e) {
+        int id = __ldg(ids + k);
+        Rec r = load_rec<PACKED>(id, n, points, splat, conic, opac, colors);
+        s_g0[slot] = r.g0;
+        s_g1[slot] = r.g1;
+        s_b[slot] = r.b;
+        s_mask[slot] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
+                                           alpha_thr, chi_thr, tile_x0, tile_y0);
+      }
     }
     __syncthreads();
     const int cnt = min(kBatch, e - base);
-    if (!__all_sync(0xffffffffu, done)) {
+    if (!__all_sync(0xffffffffu, p0.done && p1.done)) {
       for (int j = 0; j < cnt; ++j) {
         if (!((s_mask[j] >> warp) & 1u)) continue;  // uniform across the warp
-        if (done) break;
+        if (p0.done && p1.done) break;
         const float4 g0 = s_g0[j];
-        const float du = fu - g0.x;
-        const float dv = fv - g0.y;
         const float4 g1 = s_g1[j];
-        const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
-        float exponent = inv00 * du * du + 2.0f * inv01 * du * dv + inv11 * dv * dv;
-        if (exponent > chi_thr) continue;
-        float alpha = expf(-0.5f * exponent) * g1.y;
-        if (alpha < alpha_thr) continue;
-        if (ACCUM) {
-          float weight = alpha * T;
-          cr += weight * g1.z;
-          cg += weight * g1.w;
-          cb += weight * s_b[j];
-        }
-        float one_minus_alpha = 1.0f - alpha + kTransEps;
-        T *= one_minus_alpha;
-        last = base + j + 1;
-        if (T < trans_thr) done = true;
+        const float cb = ACCUM ? s_b[j] : 0.f;
+        if (!p0.done) fwd_step<ACCUM>(p0, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+        if (!p1.done) fwd_step<ACCUM>(p1, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
       }
     }
   }
-  if (inside) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const FwdPx &p = h ? p1 : p0;
+    const int v = h ? v1 : v0;
+    if (!(h ? in1 : in0)) continue;
     size_t px = (size_t)v * width + u;
     if (ACCUM && image) {
-      image[3 * px] = cr;
-      image[3 * px + 1] = cg;
-      image[3 * px + 2] = cb;
+      image[3 * px] = p.r;
+      image[3 * px + 1] = p.g;
+      image[3 * px + 2] = p.b;
     }
-    final_t[px] = T;
-    pixel_end[px] = last;
+    final_t[px] = p.T;
+    pixel_end[px] = p.last;
   }
 }
 
@@ -222,6 +249,50 @@ __device__ __forceinline__ float reduce1(float x) {
   return x;
 }
 
+// Backward state of one pixel.
+struct BwdPx {
+  float fu, fv, gr, gg, gb, Ta, suffix;
+  int end;
+};
+
+// One list entry for one pixel, back to front (kernel.cu:1068-1109). Adds the
+// pixel's 9 gradient terms into acc; returns whether it contributed. The two
+// divisions of the reference (kernel.cu:1088,1094) become one correctly
+// rounded reciprocal and two products.
+__device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float4 &g1, float c2,
+                                         float alpha_thr, float chi_thr, float acc[9]) {
+  const float du = p.fu - g0.x;
+  const float dv = p.fv - g0.y;
+  const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
+  float exponent = inv00 * du * du + 2.0f * inv01 * du * dv + inv11 * dv * dv;
+  if (exponent > chi_thr) return false;
+  float density = expf(-0.5f * exponent);
+  float alpha = density * g1.y;
+  if (alpha < alpha_thr) return false;
+  float one_minus_alpha = 1.0f - alpha + kTransEps;
+  float rcp = __frcp_rn(one_minus_alpha);
+  float prefix_t = p.Ta * rcp;
+  float weight = alpha * prefix_t;
+  const float c0 = g1.z, c1 = g1.w;
+  float grad_rgb = p.gr * c0 + p.gg * c1 + p.gb * c2;
+  float grad_alpha = prefix_t * grad_rgb - p.suffix * rcp;
+  float grad_u = inv00 * du + inv01 * dv;
+  float grad_v = inv01 * du + inv11 * dv;
+  float ag = alpha * grad_alpha;
+  acc[0] += grad_u * ag;
+  acc[1] += grad_v * ag;
+  acc[2] += -0.5f * du * du * ag;
+  acc[3] += -du * dv * ag;
+  acc[4] += -0.5f * dv * dv * ag;
+  acc[5] += density * grad_alpha;
+  acc[6] += weight * p.gr;
+  acc[7] += weight * p.gg;
+  acc[8] += weight * p.gb;
+  p.suffix += weight * grad_rgb;
+  p.Ta = prefix_t;
+  return true;
+}
+
 // Backward blend. Gradient slot order per Gaussian: 0,1 = d(u,v);
 // 2,3,4 = d(conic a,b,c); 5 = d opacity; 6,7,8 = d colour.
 template <bool PACKED>
@@ -239,7 +310,7 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(
   __shared__ float s_b[kBatch];
   __shared__ int32_t s_id[kBatch];
   __shared__ uint8_t s_mask[kBatch];
-  __shared__ float s_acc[kBatch * 9];
+  __shared__ float s_acc[9 * kBatch];
   __shared__ int s_max_end;
 
   const int tile = blockIdx.x;
@@ -248,27 +319,35 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
   const int2 pp = pixel_in_tile(t);
-  const int u = tile_x0 + pp.x, v = tile_y0 + pp.y;
-  const bool inside = (u < width) && (v < height);
-  const float fu = (float)u, fv = (float)v;
-
+  const int u = tile_x0 + pp.x;
   const int s = offsets[tile];
-  
-  float gr = 0.f, gg = 0.f, gb = 0.f, Ta = 1.f;
-  int my_end = s;
-  if (inside) {
-    size_t px = (size_t)v * width + u;
-    gr = grad_image[3 * px];
-    gg = grad_image[3 * px + 1];
-    gb = grad_image[3 * px + 2];
-    // kernel.cu:1028: pixels with an all-zero upstream gradient are skipped.
-    if (!(gr == 0.0f && gg == 0.0f && gb == 0.0f)) {
-      Ta = final_t[px];
-      my_end = pixel_end[px];
+
+  BwdPx px[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int v = tile_y0 + pp.y + 4 * h;
+    BwdPx &p = px[h];
+    p.fu = (float)u;
+    p.fv = (float)v;
+    p.gr = p.gg = p.gb = 0.f;
+    p.Ta = 1.f;
+    p.suffix = 0.f;
+    p.end = s;
+    if (u < width && v < height) {
+      size_t q = (size_t)v * width + u;
+      p.gr = grad_image[3 * q];
+      p.gg = grad_image[3 * q + 1];
+      p.gb = grad_image[3 * q + 2];
+      // kernel.cu:1028: pixels with an all-zero upstream gradient are skipped.
+      if (!(p.gr == 0.0f && p.gg == 0.0f && p.gb == 0.0f)) {
+        p.Ta = final_t[q];
+        p.end = pixel_end[q];
+      }
     }
   }
   if (t == 0) s_max_end = s;
   __syncthreads();
+  const int my_end = max(px[0].end, px[1].end);
   if (my_end > s) atomicMax(&s_max_end, my_end);
   __syncthreads();
   const int max_end = s_max_end;
@@ -277,97 +356,75 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) warp_end = max(warp_end, __shfl_xor_sync(0xffffffffu, warp_end, o));
 
-  float suffix = 0.0f;
   for (int bend = max_end; bend > s; bend -= kBatch) {
     const int bstart = max(s, bend - kBatch);
     const int cnt = bend - bstart;
     __syncthreads();
-    if (t < cnt) {
-      const int k = bstart + t;
-      int id = __ldg(ids + k);
-      Rec r = load_rec<PACKED>(id, n, points, splat, conic, opac, colors);
-      s_g0[t] = r.g0;
-      s_g1[t] = r.g1;
-      s_b[t] = r.b;
-      s_id[t] = id;
-      s_mask[t] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y, alpha_thr,
-                                      chi_thr, tile_x0, tile_y0);
-    }
 #pragma unroll
-    for (int q = 0; q < 9; ++q) s_acc[q * kBatch + t] = 0.f;
+    for (int h = 0; h < 2; ++h) {
+      const int slot = t + h * kBlendThreads;
+      if (slot < cnt) {
+        const int k = bstart + slot;
+        int id = __ldg(ids + k);
+        Rec r = load_rec<PACKED>(id, n, points, splat, conic, opac, colors);
+        s_g0[slot] = r.g0;
+        s_g1[slot] = r.g1;
+        s_b[slot] = r.b;
+        s_id[slot] = id;
+        s_mask[slot] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
+                                           alpha_thr, chi_thr, tile_x0, tile_y0);
+      }
+#pragma unroll
+      for (int q = 0; q < 9; ++q) s_acc[slot * 9 + q] = 0.f;
+    }
     __syncthreads();
     const int jmax = min(cnt, warp_end - bstart);  // entries beyond every lane's end are idle
     for (int j = jmax - 1; j >= 0; --j) {
       if (!((s_mask[j] >> warp) & 1u)) continue;  // uniform across the warp
       const int k = bstart + j;
-      float vals[9];
-      bool contrib = false;
-      if (k < my_end) {
-        const float4 g0 = s_g0[j];
-        const float4 g1 = s_g1[j];
-        const float du = fu - g0.x;
-        const float dv = fv - g0.y;
-        const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
-        float exponent = inv00 * du * du + 2.0f * inv01 * du * dv + inv11 * dv * dv;
-        if (exponent <= chi_thr) {
-          float density = expf(-0.5f * exponent);
-          float alpha = density * g1.y;
-          if (alpha >= alpha_thr) {
-            contrib = true;
-            float one_minus_alpha = 1.0f - alpha + kTransEps;
-            float prefix_t = Ta / one_minus_alpha;
-            float weight = alpha * prefix_t;
-            const float c0 = g1.z, c1 = g1.w, c2 = s_b[j];
-            float grad_rgb = gr * c0 + gg * c1 + gb * c2;
-            float grad_alpha = prefix_t * grad_rgb - suffix / one_minus_alpha;
-            float grad_u = inv00 * du + inv01 * dv;
-            float grad_v = inv01 * du + inv11 * dv;
-            vals[0] = grad_u * alpha * grad_alpha;
-            vals[1] = grad_v * alpha * grad_alpha;
-            vals[2] = -0.5f * du * du * alpha * grad_alpha;
-            vals[3] = -du * dv * alpha * grad_alpha;
-            vals[4] = -0.5f * dv * dv * alpha * grad_alpha;
-            vals[5] = density * grad_alpha;
-            vals[6] = weight * gr;
-            vals[7] = weight * gg;
-            vals[8] = weight * gb;
-            suffix += weight * grad_rgb;
-            Ta = prefix_t;
-          }
-        }
-      }
-      if (!__any_sync(0xffffffffu, contrib)) continue;
-      if (!contrib) {
+      const float4 g0 = s_g0[j];
+      const float4 g1 = s_g1[j];
+      const float c2 = s_b[j];
+      float acc[9];
 #pragma unroll
-        for (int q = 0; q < 9; ++q) vals[q] = 0.f;
-      }
-      float r8 = reduce8(vals, lane);
-      float r9 = reduce1(vals[8]);
-      if ((lane & 3) == 0) atomicAdd(&s_acc[((lane >> 2) & 7) * kBatch + j], r8);
-      if (lane == 1) atomicAdd(&s_acc[8 * kBatch + j], r9);
+      for (int q = 0; q < 9; ++q) acc[q] = 0.f;
+      bool contrib = false;
+      if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc);
+      if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc);
+      if (!__any_sync(0xffffffffu, contrib)) continue;
+      float r8 = reduce8(acc, lane);
+      float r9 = reduce1(acc[8]);
+      // [j][9] layout: the 8 writing lanes hit 8 consecutive words (distinct banks)
+      if ((lane & 3) == 0) atomicAdd(&s_acc[j * 9 + ((lane >> 2) & 7)], r8);
+      if (lane == 1) atomicAdd(&s_acc[j * 9 + 8], r9);
     }
     __syncthreads();
-    if (t < cnt && s_id[t] >= 0 && s_id[t] < n) {
-      const int id = s_id[t];
-      float a[9];
 #pragma unroll
-      for (int q = 0; q < 9; ++q) a[q] = s_acc[q * kBatch + t];
-      if (a[0] != 0.f || a[1] != 0.f) atomicAdd(reinterpret_cast<float2 *>(g_points) + id, make_float2(a[0], a[1]));
-      if (PACKED) {
-        float4 *gs4 = reinterpret_cast<float4 *>(g_splat) + 2 * (size_t)id;
-        if (a[2] != 0.f || a[3] != 0.f || a[4] != 0.f || a[5] != 0.f)
-          atomicAdd(gs4, make_float4(a[2], a[3], a[4], a[5]));
-        if (a[6] != 0.f || a[7] != 0.f || a[8] != 0.f)
-          atomicAdd(gs4 + 1, make_float4(a[6], a[7], a[8], 0.f));
-      } else {
-        size_t i3 = 3 * (size_t)id;
-        if (a[2] != 0.f) atomicAdd(g_conic + i3, a[2]);
-        if (a[3] != 0.f) atomicAdd(g_conic + i3 + 1, a[3]);
-        if (a[4] != 0.f) atomicAdd(g_conic + i3 + 2, a[4]);
-        if (a[5] != 0.f) atomicAdd(g_opac + id, a[5]);
-        if (a[6] != 0.f) atomicAdd(g_colors + i3, a[6]);
-        if (a[7] != 0.f) atomicAdd(g_colors + i3 + 1, a[7]);
-        if (a[8] != 0.f) atomicAdd(g_colors + i3 + 2, a[8]);
+    for (int h = 0; h < 2; ++h) {
+      const int slot = t + h * kBlendThreads;
+      if (slot < cnt && s_id[slot] >= 0 && s_id[slot] < n) {
+        const int id = s_id[slot];
+        float a[9];
+#pragma unroll
+        for (int q = 0; q < 9; ++q) a[q] = s_acc[slot * 9 + q];
+        if (a[0] != 0.f || a[1] != 0.f)
+          atomicAdd(reinterpret_cast<float2 *>(g_points) + id, make_float2(a[0], a[1]));
+        if (PACKED) {
+          float4 *gs4 = reinterpret_cast<float4 *>(g_splat) + 2 * (size_t)id;
+          if (a[2] != 0.f || a[3] != 0.f || a[4] != 0.f || a[5] != 0.f)
+            atomicAdd(gs4, make_float4(a[2], a[3], a[4], a[5]));
+          if (a[6] != 0.f || a[7] != 0.f || a[8] != 0.f)
+            atomicAdd(gs4 + 1, make_float4(a[6], a[7], a[8], 0.f));
+        } else {
+          size_t i3 = 3 * (size_t)id;
+          if (a[2] != 0.f) atomicAdd(g_conic + i3, a[2]);
+          if (a[3] != 0.f) atomicAdd(g_conic + i3 + 1, a[3]);
+          if (a[4] != 0.f) atomicAdd(g_conic + i3 + 2, a[4]);
+          if (a[5] != 0.f) atomicAdd(g_opac + id, a[5]);
+          if (a[6] != 0.f) atomicAdd(g_colors + i3, a[6]);
+          if (a[7] != 0.f) atomicAdd(g_colors + i3 + 1, a[7]);
+          if (a[8] != 0.f) atomicAdd(g_colors + i3 + 2, a[8]);
+        }
       }
     }
   }

@@ -184,74 +184,8 @@ __device__ __forceinline__ void stage_out(float *__restrict__ dst, const float *
   }
 }
 
-// Look-back words of the fused scan: bits 63..62 flag, 61..0 value.
-constexpr uint64_t kScanAgg = 1ull << 62;
-constexpr uint64_t kScanPrefix = 2ull << 62;
-constexpr uint64_t kScanValue = (1ull << 62) - 1;
-
-__device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t *p) {
-  uint64_t v;
-  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_volatile_u64(uint64_t *p, uint64_t v) {
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
-// Returns the exclusive prefix; *block_total receives the block sum.
-__device__ __forceinline__ int block_exclusive_scan(int x, int *block_total, int *s_warp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nwarps = (blockDim.x + 31) >> 5;
-  int incl = x;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  if (lane == 31) s_warp[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < nwarps ? s_warp[lane] : 0;
-    int wi = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += y;
-    }
-    if (lane < nwarps) s_warp[lane] = wi - w;  // exclusive warp offsets
-    if (lane == nwarps - 1) s_warp[32] = wi;   // block total
-  }
-  __syncthreads();
-  int r = incl - x + s_warp[warp];
-  *block_total = s_warp[32];
-  __syncthreads();
-  return r;
-}
-
-// Walks back over the predecessors' look-back words until an inclusive
-// prefix is found; bounded, records GS_ERR_DEVICE_TIMEOUT on give-up.
-__device__ __forceinline__ uint64_t scan_lookback(const uint64_t *__restrict__ words, int tile,
-                                                  uint32_t *status) {
-  uint64_t excl = 0;
-  for (int j = tile - 1; j >= 0; --j) {
-    uint64_t w;
-    uint32_t spins = 0;
-    do {
-      w = ld_volatile_u64(words + j);
-    } while ((w >> 62) == 0 && ++spins < kSpinLimit);
-    if ((w >> 62) == 0) {
-      atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
-      break;
-    }
-    excl += w & kScanValue;
-    if ((w >> 62) == 2) break;
-  }
-  return excl;
-}
-
-// Fused forward: one thread per Gaussian. scan_words has one uint64 per
-// block plus a block-ticket counter at index num_blocks; all zero on entry.
+// Fused forward: one thread per Gaussian. Tile counts are written per
+// Gaussian and their block sum is added into *total_out.
 __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(
     int n, const float *__restrict__ means, const float *__restrict__ scales,
     const float *__restrict__ quats, const float *__restrict__ opac,
@@ -261,20 +195,10 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(
     float min_radius, float max_radius, int width, int height, int sh_sigmoid,
     float2 *__restrict__ points, float *__restrict__ depths, float2 *__restrict__ radii,
     uint8_t *__restrict__ mask, float4 *__restrict__ splat, int32_t *__restrict__ tile_counts,
-    int32_t *__restrict__ tile_offsets, int64_t *__restrict__ total_out,
-    uint64_t *__restrict__ scan_words, int num_blocks, uint32_t *status) {
+    unsigned long long *__restrict__ total_out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
-  __shared__ int s_ticket;
-  __shared__ int s_warp[33];
-  __shared__ uint64_t s_prefix;
-
-  // Blocks take their slice in the order they start running, so every block
-  // a look-back waits on is already resident.
-  if (threadIdx.x == 0) s_ticket = (int)atomicAdd((unsigned long long *)(scan_words + num_blocks), 1ull);
-  __syncthreads();
-  const int blk = s_ticket;
-  const int first = blk * kPreBlock;
+  const int first = blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
   stage(S.means, means + 3 * f, 3 * cnt);
@@ -332,26 +256,13 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(
     mask[i] = p.visible ? 1 : 0;
     splat[2 * (size_t)i] = s0;
     splat[2 * (size_t)i + 1] = s1;
-    if (tile_counts) tile_counts[i] = count;
+    tile_counts[i] = count;
   }
-
-  // Exclusive scan of the tile counts across the grid (decoupled look-back).
-  int block_total;
-  int excl_in_block = block_exclusive_scan(count, &block_total, s_warp);
-  if (t == 0) {
-    uint64_t prefix = 0;
-    if (blk == 0) {
-      st_volatile_u64(scan_words, kScanPrefix | (uint64_t)block_total);
-    } else {
-      st_volatile_u64(scan_words + blk, kScanAgg | (uint64_t)block_total);
-      prefix = scan_lookback(scan_words, blk, status);
-      st_volatile_u64(scan_words + blk, kScanPrefix | (prefix + (uint64_t)block_total));
-    }
-    s_prefix = prefix;
-    if (blk == num_blocks - 1) *total_out = (int64_t)(prefix + (uint64_t)block_total);
-  }
-  __syncthreads();
-  if (t < cnt) tile_offsets[i] = (int32_t)(s_prefix + (uint64_t)excl_in_block);
+  // Sum of the tile counts: warp reduction, one atomic per warp.
+  unsigned long long c = (unsigned long long)count;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((t & 31) == 0 && c) atomicAdd(total_out, c);
 }
 
 // Fused backward: one thread per Gaussian. Writes every output element
@@ -527,11 +438,6 @@ extern "C" int gs_evaluate_sh_backward(int n, const float *grad_colors, const fl
   return launch_status();
 }
 
-extern "C" size_t gs_preprocess_scratch_bytes(int n) {
-  int blocks = (n + kPreBlock - 1) / kPreBlock;
-  return (size_t)(blocks + 1) * sizeof(uint64_t);
-}
-
 extern "C" int gs_preprocess_forward(int n, const float *means, const float *scales,
                                      const float *quats, const float *opacities,
                                      const float *sh_dc, const float *sh_rest,
@@ -541,36 +447,22 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
                                      float max_radius, int width, int height, int sh_sigmoid,
                                      float *points_img, float *depths, float *radii,
                                      uint8_t *mask, float *splat, int32_t *tile_counts,
-                                     int32_t *tile_offsets, int64_t *total_dev, void *scratch,
-                                     size_t scratch_bytes, void *stream) {
-  if (n < 0 || width <= 0 || height <= 0) return GS_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)splat & 15))
+                                     int64_t *total_dev, void *stream) {
+  if (n < 0 || width <= 0 || height <= 0 || total_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)splat & 15) ||
+      ((uintptr_t)total_dev & 7))
     return GS_ERR_INVALID_ARGUMENT;
   cudaStream_t st = as_stream(stream);
-  if (n == 0) {
-    return cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
-  }
-  int blocks = (n + kPreBlock - 1) / kPreBlock;
-  if (scratch_bytes < gs_preprocess_scratch_bytes(n) || scratch == nullptr)
-    return GS_ERR_CAPACITY;
-  int rc = cuda_status(cudaMemsetAsync(scratch, 0, gs_preprocess_scratch_bytes(n), st));
-  if (rc) return rc;
-  static bool attr_set = false;
-  size_t smem = sizeof(PreSmem);
-  if (!attr_set) {
-    cudaFuncSetAttribute(preprocess_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    cudaFuncSetAttribute(preprocess_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr_set = true;
-  }
-  preprocess_forward_kernel<<<blocks, kPreBlock, smem, st>>>(
+  int rc = cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
+  if (rc || n == 0) return rc;
+  if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  const int blocks = (n + kPreBlock - 1) / kPreBlock;
+  preprocess_forward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(
       n, means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
       camera_pos, near_plane, far_plane, min_opacity, min_radius, max_radius, width, height,
       sh_sigmoid, reinterpret_cast<float2 *>(points_img), depths,
       reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat), tile_counts,
-      tile_offsets, total_dev, reinterpret_cast<uint64_t *>(scratch), blocks,
-      device_status_word());
+      reinterpret_cast<unsigned long long *>(total_dev));
   count_launch();
   return launch_status();
 }
@@ -588,13 +480,7 @@ extern "C" int gs_preprocess_backward(int n, const float *means, const float *sc
   if (n < 0 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
     return GS_ERR_INVALID_ARGUMENT;
   if (n == 0) return GS_OK;
-  size_t smem = sizeof(PreSmem);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(preprocess_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr_set = true;
-  }
+  const size_t smem = sizeof(PreSmem);  // 30 KB: below the 48 KB default, no opt-in
   int blocks = (n + kPreBlock - 1) / kPreBlock;
   preprocess_backward_kernel<<<blocks, kPreBlock, smem, as_stream(stream)>>>(
       n, means, scales, quats, sh_dc, sh_rest, world_to_camera, intrinsic, camera_pos, width,

@@ -1,23 +1,28 @@
-// tiles.cu -- tile counting, exclusive scan, key duplication, onesweep radix
-// sort and tile ranges.
+// tiles.cu -- tile counting, exclusive scan, onesweep radix sort, tile layout.
 //
 // Sort: a stable LSD radix sort with 8-bit digits in the "onesweep" style
-// (one kernel per digit pass, single read and single write of the pairs per
-// pass). One upfront kernel histograms every pass's digits in a single read
-// of the keys. In a pass, each 256-thread block takes a 3840-pair tile
-// (ticketed in start order), ranks its digits warp by warp with match.any
-// (warp-striped layout keeps the ranking stable), publishes its per-digit
-// counts, obtains the global per-digit prefix from its predecessors by
-// decoupled look-back (bounded spins), shuffles the tile into digit order in
-// shared memory and writes it out in coalesced runs.
+// (one kernel per digit pass, one read and one write of the pairs per pass),
+// templated on the key width. One upfront kernel histograms every pass's
+// digits in a single read of the keys. In a pass, each 256-thread block
+// takes a tile of pairs (ticketed in start order), ranks its digits warp by
+// warp with match.any (the warp-striped layout keeps the ranking stable),
+// publishes its per-digit counts, obtains the global per-digit prefix from
+// its predecessors by decoupled look-back (bounded spins), shuffles the tile
+// into digit order in shared memory and writes it out in coalesced runs.
 //
-// Only the significant key bits are sorted: 32 depth bits + ceil(log2 tiles)
-// tile bits, i.e. 6 passes for up to 65536 tiles. The reference sorts all 64
-// bits with CUB (ruguangyou/3dgs_from_scratch src/cuda/kernel.cu:1341-1388);
-// the higher bits are zero, so the order is identical.
+// Tile layout: the reference emits (tile << 32 | depth bits, id) pairs in
+// Gaussian order and sorts all 64 key bits with CUB (ruguangyou/
+// 3dgs_from_scratch src/cuda/kernel.cu:820-873,1341-1388). The same order
+// comes out of two cheaper stable sorts: the N Gaussians by depth bits (4
+// passes over N, ties keep Gaussian order), then the K pairs -- emitted in
+// that depth order -- by tile id alone (2 passes of 16-bit keys up to 65536
+// tiles). Within a tile the entries end up ordered by depth bits, ties by
+// Gaussian id: exactly the reference's stable 64-bit order.
 #include "gs_common.cuh"
 
 namespace gs {
+
+static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // ---- tile counts (kernel.cu:784-818) -------------------------------------
 
@@ -48,7 +53,49 @@ __device__ __forceinline__ void st_vol64(uint64_t *p, uint64_t v) {
   asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Warp-parallel look-back over 64-bit words (flag in bits 63..62: 1 =
+// aggregate, 2 = inclusive prefix): lane i inspects predecessor tile-1-i,
+// 32 predecessors per step; bounded spins record GS_ERR_DEVICE_TIMEOUT.
+// Call with the whole warp; returns the exclusive prefix in every lane.
+__device__ __forceinline__ uint64_t warp_lookback64(const uint64_t *__restrict__ words, int tile,
+                                                    uint32_t *status) {
+  const uint32_t lane = lane_id();
+  uint64_t excl = 0;
+  int top = tile - 1;
+  while (top >= 0) {
+    const int j = top - (int)lane;
+    uint64_t w = 0;
+    if (j >= 0) {
+      uint32_t spins = 0;
+      do {
+        w = ld_vol64(words + j);
+      } while ((w >> 62) == 0 && ++spins < kSpinLimit);
+      if ((w >> 62) == 0) {
+        atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
+        w = 2ull << 62;  // give up: treat as a (wrong) prefix so the walk ends
+      }
+    } else {
+      w = 2ull << 62;  // before tile 0: a zero prefix
+    }
+    const uint32_t prefix_lanes = __ballot_sync(0xffffffffu, (w >> 62) == 2);
+    // nearest predecessor holding a prefix; with none in this window all 32
+    // aggregates count and the walk moves 32 tiles further back
+    const int stop = prefix_lanes ? __ffs(prefix_lanes) - 1 : 31;
+    uint64_t v = ((int)lane <= stop) ? (w & ((1ull << 62) - 1)) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    excl += v;
+    if (prefix_lanes) break;
+    top -= 32;
+  }
+  return excl;
+}
+
+// Exclusive scan of n counts (optionally gathered: in[gather[i]]) into out,
+// total into *total. words: one per tile plus the ticket counter at
+// words[num_tiles], all zero on entry.
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t *__restrict__ in,
+                                                            const int32_t *__restrict__ gather,
                                                             int32_t *__restrict__ out,
                                                             int64_t *__restrict__ total,
                                                             uint64_t *__restrict__ words,
@@ -66,8 +113,17 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     long long idx = base + k;
-    v[k] = idx < n ? in[idx] : 0;
-    sum += v[k];
+    int x = 0;
+    if (idx < n) {
+      if (gather) {
+        const int g = gather[idx];
+        x = (g >= 0 && g < n) ? in[g] : 0;  // out-of-range only with a corrupted permutation
+      } else {
+        x = in[idx];
+      }
+    }
+    v[k] = x;
+    sum += x;
   }
   long long incl = sum;
 #pragma unroll
@@ -77,37 +133,28 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
   }
   if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
-  if (t == 0) {
-    long long acc = 0;
-    for (int w = 0; w < kScanThreads / 32; ++w) {
-      long long x = s_warp[w];
-      s_warp[w] = acc;
-      acc += x;
+  if (warp == 0) {
+    long long wv = lane < kScanThreads / 32 ? s_warp[lane] : 0;
+    long long wi = wv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      long long y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
     }
-    s_warp[kScanThreads / 32] = acc;
-    const uint64_t agg = (uint64_t)acc;
+    const uint64_t agg = (uint64_t)__shfl_sync(0xffffffffu, wi, kScanThreads / 32 - 1);
+    if (lane < kScanThreads / 32) s_warp[lane] = wi - wv;
     uint64_t prefix = 0;
     if (tile == 0) {
-      st_vol64(words, (2ull << 62) | agg);
+      if (lane == 0) st_vol64(words, (2ull << 62) | agg);
     } else {
-      st_vol64(words + tile, (1ull << 62) | agg);
-      for (int j = tile - 1; j >= 0; --j) {
-        uint64_t w;
-        uint32_t spins = 0;
-        do {
-          w = ld_vol64(words + j);
-        } while ((w >> 62) == 0 && ++spins < kSpinLimit);
-        if ((w >> 62) == 0) {
-          atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
-          break;
-        }
-        prefix += w & ((1ull << 62) - 1);
-        if ((w >> 62) == 2) break;
-      }
-      st_vol64(words + tile, (2ull << 62) | (prefix + agg));
+      if (lane == 0) st_vol64(words + tile, (1ull << 62) | agg);
+      prefix = warp_lookback64(words, tile, status);
+      if (lane == 0) st_vol64(words + tile, (2ull << 62) | (prefix + agg));
     }
-    s_prefix = prefix;
-    if (tile == num_tiles - 1) *total = (int64_t)(prefix + agg);
+    if (lane == 0) {
+      s_prefix = prefix;
+      if (tile == num_tiles - 1) *total = (int64_t)(prefix + agg);
+    }
   }
   __syncthreads();
   long long run = (long long)s_prefix + s_warp[warp] + (incl - sum);
@@ -119,70 +166,54 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
   }
 }
 
-// ---- key duplication (kernel.cu:820-873) ------------------------------------
-
-__global__ void __launch_bounds__(256) keygen_kernel(int n, const float2 *__restrict__ points,
-                                                     const float2 *__restrict__ radii,
-                                                     const float *__restrict__ depths,
-                                                     const uint8_t *__restrict__ mask,
-                                                     const int32_t *__restrict__ offsets,
-                                                     int width, int height, int64_t total,
-                                                     uint64_t *__restrict__ keys,
-                                                     int32_t *__restrict__ vals) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n || !mask[i]) return;
-  float2 p = points[i], r = radii[i];
-  TileRect tr = tile_rect(p.x, p.y, r.x, r.y, width, height);
-  if (tr.empty) return;
-  const int tx = tiles_x_of(width);
-  const uint64_t dbits = (uint64_t)__float_as_uint(depths[i]);
-  int64_t o = offsets[i];
-  if (o < 0) return;
-  for (int y = tr.y0; y <= tr.y1; ++y)
-    for (int x = tr.x0; x <= tr.x1; ++x) {
-      if (o >= total) return;  // only reachable if the offsets were corrupted
-      uint64_t tid = (uint64_t)(y * tx + x);
-      keys[o] = (tid << 32) | dbits;
-      vals[o] = i;
-      ++o;
-    }
-}
-
 // ---- onesweep radix sort -----------------------------------------------------
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 15;
-constexpr int kSortTile = kSortThreads * kSortItems;  // 3840 pairs
 constexpr int kMaxPasses = 8;
 constexpr uint32_t kLbAgg = 1u << 30;
 constexpr uint32_t kLbPrefix = 2u << 30;
 constexpr uint32_t kLbValue = (1u << 30) - 1;
 
-// Histogram of every pass's digits in one read of the keys.
-__global__ void __launch_bounds__(256) sort_histogram_kernel(const uint64_t *__restrict__ keys,
+// Items per thread by key width (shared memory per tile: items * 256 * (key + 4) B).
+template <typename KT> struct SortItems;
+template <> struct SortItems<uint64_t> { static constexpr int value = 14; };
+template <> struct SortItems<uint32_t> { static constexpr int value = 16; };
+template <> struct SortItems<uint16_t> { static constexpr int value = 20; };
+
+template <typename KT>
+__device__ __forceinline__ uint32_t digit_of(KT key, int shift, uint32_t dmask) {
+  return (uint32_t)((uint64_t)key >> shift) & dmask;
+}
+
+// Histogram of every pass's digits in one read of the keys (sub-histograms
+// in shared memory shared by a few warps each, merged per block into global
+// counts).
+template <typename KT>
+__global__ void __launch_bounds__(256) sort_histogram_kernel(const KT *__restrict__ keys,
                                                              int64_t n, int passes, int end_bit,
                                                              uint32_t *__restrict__ hist) {
-  __shared__ uint32_t sh[kMaxPasses * 256];
-  for (int k = threadIdx.x; k < passes * 256; k += blockDim.x) sh[k] = 0;
+  constexpr int kMaxP = (int)sizeof(KT);            // 8-bit digits per key
+  constexpr int kCopies = sizeof(KT) == 8 ? 4 : 8;  // <= 32 KB of shared memory
+  __shared__ uint32_t sh[kCopies][kMaxP * 256];
+  const int copy = (threadIdx.x >> 5) % kCopies;
+  for (int k = threadIdx.x; k < kCopies * kMaxP * 256; k += blockDim.x) (&sh[0][0])[k] = 0;
   __syncthreads();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const uint32_t lane = lane_id();
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < n; base += stride) {
-    const int64_t idx = base + threadIdx.x;
-    const bool valid = idx < n;
-    const uint64_t key = valid ? keys[idx] : 0;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += stride) {
+    const KT key = keys[idx];
     for (int p = 0; p < passes; ++p) {
       const int bits = min(8, end_bit - 8 * p);
-      const uint32_t d = valid ? (uint32_t)((key >> (8 * p)) & ((1u << bits) - 1u)) : 0x100u;
-      const uint32_t peers = __match_any_sync(0xffffffffu, d);
-      const uint32_t leader = 31 - __clz(peers);
-      if (valid && lane == leader) atomicAdd(&sh[p * 256 + d], (uint32_t)__popc(peers));
+      atomicAdd(&sh[copy][p * 256 + digit_of(key, 8 * p, (1u << bits) - 1u)], 1u);
     }
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < passes * 256; k += blockDim.x)
-    if (sh[k]) atomicAdd(&hist[k], sh[k]);
+  for (int k = threadIdx.x; k < passes * 256; k += blockDim.x) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int w = 0; w < kCopies; ++w) c += sh[w][k];
+    if (c) atomicAdd(&hist[k], c);
+  }
 }
 
 // Block-wide exclusive scan of one uint32 per thread, blockDim == 256.
@@ -212,9 +243,10 @@ __device__ __forceinline__ uint32_t block_scan_256(uint32_t x, uint32_t *s_tmp) 
   return r;
 }
 
+template <typename KT, int ITEMS>
 struct SortSmem {
-  uint64_t keys[kSortTile];
-  int32_t vals[kSortTile];
+  KT keys[kSortThreads * ITEMS];
+  int32_t vals[kSortThreads * ITEMS];
   uint32_t whist[kSortWarps][256];
   uint32_t gbase[256];
   uint32_t lstart[256];
@@ -222,40 +254,43 @@ struct SortSmem {
   int tile;
 };
 
+// One digit pass. vals_in == nullptr means the identity (value = index).
+template <typename KT, int ITEMS>
 __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
-    const uint64_t *__restrict__ keys_in, const int32_t *__restrict__ vals_in,
-    uint64_t *__restrict__ keys_out, int32_t *__restrict__ vals_out, int64_t n, int shift,
+    const KT *__restrict__ keys_in, const int32_t *__restrict__ vals_in,
+    KT *__restrict__ keys_out, int32_t *__restrict__ vals_out, int64_t n, int shift,
     uint32_t dmask, const uint32_t *__restrict__ hist, uint32_t *__restrict__ lookback,
     uint32_t *__restrict__ ticket, uint32_t *status) {
+  constexpr int kTileItems = kSortThreads * ITEMS;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  SortSmem &S = *reinterpret_cast<SortSmem *>(smem_raw);
+  SortSmem<KT, ITEMS> &S = *reinterpret_cast<SortSmem<KT, ITEMS> *>(smem_raw);
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
   if (t == 0) S.tile = (int)atomicAdd(ticket, 1u);
   for (int k = t; k < kSortWarps * 256; k += kSortThreads) (&S.whist[0][0])[k] = 0;
   __syncthreads();
   const int tile = S.tile;
-  const int64_t base = (int64_t)tile * kSortTile + (int64_t)warp * (32 * kSortItems);
+  const int64_t base = (int64_t)tile * kTileItems + (int64_t)warp * (32 * ITEMS);
 
   // Load warp-striped: item k of lane l is element base + k*32 + l.
-  uint64_t key[kSortItems];
-  int32_t val[kSortItems];
+  KT key[ITEMS];
+  int32_t val[ITEMS];
 #pragma unroll
-  for (int k = 0; k < kSortItems; ++k) {
+  for (int k = 0; k < ITEMS; ++k) {
     const int64_t idx = base + k * 32 + lane;
     const bool valid = idx < n;
-    key[k] = valid ? keys_in[idx] : ~0ull;
-    val[k] = valid ? vals_in[idx] : 0;
+    key[k] = valid ? keys_in[idx] : (KT)0;
+    val[k] = valid ? (vals_in ? vals_in[idx] : (int32_t)idx) : 0;
   }
 
   // Stable warp-local ranks: running per-warp digit counts in shared memory.
-  uint32_t rank[kSortItems];
+  uint32_t rank[ITEMS];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
-  for (int k = 0; k < kSortItems; ++k) {
+  for (int k = 0; k < ITEMS; ++k) {
     const int64_t idx = base + k * 32 + lane;
     const bool valid = idx < n;
-    const uint32_t d = valid ? (uint32_t)((key[k] >> shift) & dmask) : 0x100u;
+    const uint32_t d = valid ? digit_of(key[k], shift, dmask) : 0x100u;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const uint32_t leader = 31 - __clz(peers);
     uint32_t old = 0;
@@ -284,19 +319,37 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
     st_volatile_u32(my_lb, kLbPrefix | cnt);
   } else {
     st_volatile_u32(my_lb, kLbAgg | cnt);
-    for (int j = tile - 1; j >= 0; --j) {
-      const uint32_t *w = lookback + (size_t)j * 256 + d;
-      uint32_t x;
-      uint32_t spins = 0;
-      do {
-        x = ld_volatile_u32(w);
-      } while ((x >> 30) == 0 && ++spins < kSpinLimit);
-      if ((x >> 30) == 0) {
-        atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
-        break;
+    // Decoupled look-back over kLookback predecessors per step: their words
+    // are loaded together (independent loads in flight), then consumed
+    // nearest first, re-polling (bounded) only those not yet published.
+    // Inspecting many predecessors per round trip keeps the first wave of
+    // tiles from forming a chain of one L2 round trip per tile.
+    constexpr int kLookback = 16;
+    int top = tile - 1;
+    bool found = false;
+    while (!found && top >= 0) {
+      uint32_t w[kLookback];
+#pragma unroll
+      for (int q = 0; q < kLookback; ++q) {
+        const int j = top - q;
+        w[q] = (j >= 0) ? ld_volatile_u32(lookback + (size_t)j * 256 + d) : kLbPrefix;
       }
-      excl += x & kLbValue;
-      if ((x >> 30) == 2) break;
+#pragma unroll
+      for (int q = 0; q < kLookback; ++q) {
+        if (found) break;
+        const int j = top - q;
+        uint32_t x = w[q];
+        uint32_t spins = 0;
+        while ((x >> 30) == 0 && ++spins < kSpinLimit) x = ld_volatile_u32(lookback + (size_t)j * 256 + d);
+        if ((x >> 30) == 0) {
+          atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
+          found = true;
+          break;
+        }
+        excl += x & kLbValue;  // (j < 0 contributes a zero prefix)
+        if ((x >> 30) == 2) found = true;
+      }
+      top -= kLookback;
     }
     st_volatile_u32(my_lb, kLbPrefix | ((excl + cnt) & kLbValue));
   }
@@ -308,10 +361,10 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
 
   // Shuffle into digit order in shared memory.
 #pragma unroll
-  for (int k = 0; k < kSortItems; ++k) {
+  for (int k = 0; k < ITEMS; ++k) {
     const int64_t idx = base + k * 32 + lane;
     if (idx < n) {
-      const uint32_t dk = (uint32_t)((key[k] >> shift) & dmask);
+      const uint32_t dk = digit_of(key[k], shift, dmask);
       const uint32_t pos = S.lstart[dk] + S.whist[warp][dk] + rank[k];
       S.keys[pos] = key[k];
       S.vals[pos] = val[k];
@@ -319,11 +372,11 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   }
   __syncthreads();
 
-  const int64_t tile_base = (int64_t)tile * kSortTile;
-  const int valid_count = (int)min((int64_t)kSortTile, n - tile_base);
+  const int64_t tile_base = (int64_t)tile * kTileItems;
+  const int valid_count = (int)min((int64_t)kTileItems, n - tile_base);
   for (int p = t; p < valid_count; p += kSortThreads) {
-    const uint64_t kk = S.keys[p];
-    const uint32_t dk = (uint32_t)((kk >> shift) & dmask);
+    const KT kk = S.keys[p];
+    const uint32_t dk = digit_of(kk, shift, dmask);
     const uint32_t out = S.gbase[dk] + ((uint32_t)p - S.lstart[dk]);
     if ((int64_t)out < n) {  // always true unless a look-back gave up
       keys_out[out] = kk;
@@ -332,32 +385,77 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   }
 }
 
-// ---- tile ranges (kernel.cu:875-914) -------------------------------------------
+// ---- tile layout kernels -------------------------------------------------------
 
-__global__ void __launch_bounds__(256) ranges_kernel(const uint64_t *__restrict__ keys,
+// Pairs in depth order: thread i takes the i-th Gaussian of the depth sort
+// and writes its tile ids (row-major over its rectangle) and its id at
+// offsets[i] (exclusive scan of the counts in depth order).
+template <typename KT>
+__global__ void __launch_bounds__(256) emit_pairs_kernel(int n, const int32_t *__restrict__ order,
+                                                         const int32_t *__restrict__ counts,
+                                                         const int32_t *__restrict__ offsets,
+                                                         const float2 *__restrict__ points,
+                                                         const float2 *__restrict__ radii,
+                                                         int width, int height, int64_t total,
+                                                         KT *__restrict__ keys,
+                                                         int32_t *__restrict__ vals) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int g = order[i];
+  if (g < 0 || g >= n || counts[g] <= 0) return;
+  const float2 p = points[g], r = radii[g];
+  const TileRect tr = tile_rect(p.x, p.y, r.x, r.y, width, height);
+  if (tr.empty) return;
+  const int tx = tiles_x_of(width);
+  int64_t o = offsets[i];
+  if (o < 0) return;
+  for (int y = tr.y0; y <= tr.y1; ++y)
+    for (int x = tr.x0; x <= tr.x1; ++x) {
+      if (o >= total) return;  // only reachable if the offsets were corrupted
+      keys[o] = (KT)(y * tx + x);
+      vals[o] = g;
+      ++o;
+    }
+}
+
+// Per-tile start offsets from the sorted tile ids (kernel.cu:875-914).
+template <typename KT>
+__global__ void __launch_bounds__(256) ranges_kernel(const KT *__restrict__ tiles_sorted,
                                                      int64_t n, int num_tiles,
                                                      int32_t *__restrict__ offsets) {
   const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
-  const int tile = min((int)(keys[k] >> 32), num_tiles - 1);
-  const int prev = (k == 0) ? -1 : min((int)(keys[k - 1] >> 32), num_tiles - 1);
+  const int tile = min((int)tiles_sorted[k], num_tiles - 1);
+  const int prev = (k == 0) ? -1 : min((int)tiles_sorted[k - 1], num_tiles - 1);
   for (int g = prev + 1; g <= tile; ++g) offsets[g] = (int32_t)k;
   if (k == n - 1)
     for (int g = tile + 1; g < num_tiles; ++g) offsets[g] = (int32_t)n;
 }
 
-// ---- host-side sort driver -------------------------------------------------------
+// The reference's 64-bit keys (tile << 32 | depth bits) of the sorted pairs,
+// for callers that ask for them.
+template <typename KT>
+__global__ void __launch_bounds__(256) full_keys_kernel(const KT *__restrict__ tiles_sorted,
+                                                        const int32_t *__restrict__ ids,
+                                                        const float *__restrict__ depths,
+                                                        int64_t n, uint64_t *__restrict__ out) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  out[k] = ((uint64_t)tiles_sorted[k] << 32) | (uint64_t)__float_as_uint(depths[ids[k]]);
+}
 
-static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+// ---- host-side sort driver -------------------------------------------------------
 
 struct SortLayout {
   size_t hist, lookback, tickets, total;
   int tiles;
 };
 
+template <typename KT>
 static SortLayout sort_layout(int64_t n) {
+  constexpr int kTileItems = kSortThreads * SortItems<KT>::value;
   SortLayout L;
-  L.tiles = (int)((n + kSortTile - 1) / kSortTile);
+  L.tiles = (int)((n + kTileItems - 1) / kTileItems);
   L.hist = 0;
   L.lookback = align_up(L.hist + kMaxPasses * 256 * sizeof(uint32_t), 256);
   L.tickets = align_up(L.lookback + (size_t)kMaxPasses * L.tiles * 256 * sizeof(uint32_t), 256);
@@ -365,46 +463,63 @@ static SortLayout sort_layout(int64_t n) {
   return L;
 }
 
+static int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = sms;
+  }
+  return cached[dev];
+}
+
 // Sorts (keys, vals) on bits [0, end_bit) in ceil(end_bit / 8) passes; the
-// result ends in the buffers selected by the parity of the pass count
-// (even: keys/vals, odd: alt).
-static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt,
-                    int32_t *vals_alt, int end_bit, void *scratch, cudaStream_t st) {
+// result ends in the buffers selected by the parity of the pass count (even:
+// keys/vals, odd: alt). vals == nullptr sorts the identity permutation (the
+// first pass generates it; vals must then not be read back for an even pass
+// count unless it points at storage, so callers pass real buffers when they
+// need the even-parity result).
+template <typename KT>
+static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *vals_alt,
+                    int end_bit, void *scratch, cudaStream_t st, const int32_t *vals_first = nullptr,
+                    bool identity_first = false) {
+  constexpr int ITEMS = SortItems<KT>::value;
   const int passes = (end_bit + 7) / 8;
   if (n <= 0 || passes <= 0) return GS_OK;
   if (n > (int64_t)kLbValue) return GS_ERR_CAPACITY;
-  SortLayout L = sort_layout(n);
+  SortLayout L = sort_layout<KT>(n);
   unsigned char *base = reinterpret_cast<unsigned char *>(scratch);
   uint32_t *hist = reinterpret_cast<uint32_t *>(base + L.hist);
   uint32_t *lookback = reinterpret_cast<uint32_t *>(base + L.lookback);
   uint32_t *tickets = reinterpret_cast<uint32_t *>(base + L.tickets);
   int rc = cuda_status(cudaMemsetAsync(scratch, 0, L.total, st));
   if (rc) return rc;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int64_t hb = (n + 255) / 256;
-  int hblocks = (int)(hb < (int64_t)sms * 4 ? hb : (int64_t)sms * 4);
-  sort_histogram_kernel<<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
+  const int64_t hb = (n + 255) / 256;
+  const int hblocks = (int)(hb < (int64_t)sm_count() * 4 ? hb : (int64_t)sm_count() * 4);
+  sort_histogram_kernel<KT><<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
   count_launch();
   static int attr_done[64] = {0};
-  const size_t smem = sizeof(SortSmem);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(onesweep_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(SortSmem<KT, ITEMS>);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute(onesweep_pass_kernel<KT, ITEMS>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_done[dev] = 1;
   }
-  uint64_t *kin = keys, *kout = keys_alt;
+  KT *kin = keys, *kout = keys_alt;
   int32_t *vin = vals, *vout = vals_alt;
   for (int p = 0; p < passes; ++p) {
     const int bits = end_bit - 8 * p < 8 ? end_bit - 8 * p : 8;
-    onesweep_pass_kernel<<<L.tiles, kSortThreads, smem, st>>>(
-        kin, vin, kout, vout, n, 8 * p, (1u << bits) - 1u, hist + 256 * p,
-        lookback + (size_t)p * L.tiles * 256,
-        tickets + p, device_status_word());
+    const int32_t *vsrc = (p == 0) ? (identity_first ? nullptr : (vals_first ? vals_first : vin)) : vin;
+    onesweep_pass_kernel<KT, ITEMS><<<L.tiles, kSortThreads, smem, st>>>(
+        kin, vsrc, kout, vout, n, 8 * p, (1u << bits) - 1u, hist + 256 * p,
+        lookback + (size_t)p * L.tiles * 256, tickets + p, device_status_word());
     count_launch();
-    uint64_t *tk = kin;
+    KT *tk = kin;
     kin = kout;
     kout = tk;
     int32_t *tv = vin;
@@ -414,10 +529,97 @@ static int run_sort(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt
   return launch_status();
 }
 
-static int key_bits_for_tiles(int num_tiles) {
-  int tile_bits = 0;
-  while ((1ll << tile_bits) < (long long)num_tiles) ++tile_bits;
-  return 32 + tile_bits;
+static int bits_for(int64_t count) {
+  int b = 0;
+  while ((1ll << b) < count) ++b;
+  return b;
+}
+
+// Scratch of the tile layout, carved in this order.
+struct LayoutScratch {
+  size_t dkeys_a, dkeys_b, dvals_a, dvals_b, offs, total8, tkeys_a, tkeys_b, tvals_b, sort, total;
+};
+
+static LayoutScratch layout_scratch(int n, int64_t total, int num_tiles) {
+  const size_t tk = num_tiles <= 65536 ? 2 : 4;
+  const size_t nn = (size_t)(n > 0 ? n : 1), kk = (size_t)(total > 0 ? total : 1);
+  LayoutScratch L;
+  L.dkeys_a = 0;
+  L.dkeys_b = align_up(L.dkeys_a + 4 * nn, 256);
+  L.dvals_a = align_up(L.dkeys_b + 4 * nn, 256);
+  L.dvals_b = align_up(L.dvals_a + 4 * nn, 256);
+  L.offs = align_up(L.dvals_b + 4 * nn, 256);
+  L.total8 = align_up(L.offs + 4 * nn, 256);  // the scan's int64 total (8-byte aligned)
+  L.tkeys_a = align_up(L.total8 + 8, 256);
+  L.tkeys_b = align_up(L.tkeys_a + tk * kk, 256);
+  L.tvals_b = align_up(L.tkeys_b + tk * kk, 256);
+  L.sort = align_up(L.tvals_b + 4 * kk, 256);
+  const size_t s1 = sort_layout<uint32_t>((int64_t)nn).total;
+  const size_t s2 = tk == 2 ? sort_layout<uint16_t>((int64_t)kk).total
+                            : sort_layout<uint32_t>((int64_t)kk).total;
+  const size_t scan = ((nn + kScanTile - 1) / kScanTile + 1) * sizeof(uint64_t);
+  L.total = align_up(L.sort + (s1 > s2 ? (s1 > scan ? s1 : scan) : (s2 > scan ? s2 : scan)), 256);
+  return L;
+}
+
+template <typename KT>
+static int tile_layout_impl(int n, const float2 *points, const float2 *radii, const float *depths,
+                            const int32_t *counts, int64_t total, int width, int height,
+                            uint64_t *keys_sorted, int32_t *ids_sorted, int32_t *indexing_offset,
+                            unsigned char *p, const LayoutScratch &L, cudaStream_t st) {
+  const int num_tiles = tiles_x_of(width) * tiles_y_of(height);
+  uint32_t *dk_a = reinterpret_cast<uint32_t *>(p + L.dkeys_a);
+  uint32_t *dk_b = reinterpret_cast<uint32_t *>(p + L.dkeys_b);
+  int32_t *dv_a = reinterpret_cast<int32_t *>(p + L.dvals_a);
+  int32_t *dv_b = reinterpret_cast<int32_t *>(p + L.dvals_b);
+  int32_t *offs = reinterpret_cast<int32_t *>(p + L.offs);
+  KT *tk_a = reinterpret_cast<KT *>(p + L.tkeys_a);
+  KT *tk_b = reinterpret_cast<KT *>(p + L.tkeys_b);
+  int32_t *tv_b = reinterpret_cast<int32_t *>(p + L.tvals_b);
+  void *sort_scratch = p + L.sort;
+
+  // 1. Gaussians by depth bits (stable, identity values): the depth keys are
+  //    copied first so the caller's depths stay untouched.
+  int rc = cuda_status(cudaMemcpyAsync(dk_a, depths, (size_t)n * 4, cudaMemcpyDeviceToDevice, st));
+  if (rc) return rc;
+  rc = run_sort<uint32_t>(n, dk_a, dv_a, dk_b, dv_b, 32, sort_scratch, st, nullptr, true);
+  if (rc) return rc;
+  const int32_t *order = dv_a;  // 4 passes: even, the result is back in (dk_a, dv_a)
+
+  // 2. exclusive scan of the counts in depth order
+  const int stiles = (n + kScanTile - 1) / kScanTile;
+  rc = cuda_status(cudaMemsetAsync(sort_scratch, 0, (size_t)(stiles + 1) * 8, st));
+  if (rc) return rc;
+  scan_kernel<<<stiles, kScanThreads, 0, st>>>(n, counts, order, offs,
+                                               reinterpret_cast<int64_t *>(p + L.total8),
+                                               reinterpret_cast<uint64_t *>(sort_scratch), stiles,
+                                               device_status_word());
+  count_launch();
+
+  // 3. pairs in depth order, 4. stable sort by tile id
+  const int tbits = bits_for(num_tiles) > 0 ? bits_for(num_tiles) : 1;
+  const int tpasses = (tbits + 7) / 8;
+  KT *k0 = (tpasses & 1) ? tk_b : tk_a;
+  int32_t *v0 = (tpasses & 1) ? tv_b : ids_sorted;
+  KT *k1 = (tpasses & 1) ? tk_a : tk_b;
+  int32_t *v1 = (tpasses & 1) ? ids_sorted : tv_b;
+  emit_pairs_kernel<KT><<<(n + 255) / 256, 256, 0, st>>>(n, order, counts, offs, points, radii,
+                                                         width, height, total, k0, v0);
+  count_launch();
+  rc = run_sort<KT>(total, k0, v0, k1, v1, tbits, sort_scratch, st);
+  if (rc) return rc;
+  // the sorted tile ids are in tk_a, the ids in ids_sorted
+
+  // 5. tile ranges
+  ranges_kernel<KT><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(tk_a, total, num_tiles,
+                                                                     indexing_offset);
+  count_launch();
+  if (keys_sorted) {
+    full_keys_kernel<KT><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(tk_a, ids_sorted, depths,
+                                                                          total, keys_sorted);
+    count_launch();
+  }
+  return launch_status();
 }
 
 }  // namespace gs
@@ -454,14 +656,16 @@ extern "C" int gs_exclusive_scan(int n, const int32_t *counts, int32_t *offsets,
   int tiles = (n + kScanTile - 1) / kScanTile;
   int rc = cuda_status(cudaMemsetAsync(scratch, 0, gs_scan_scratch_bytes(n), st));
   if (rc) return rc;
-  scan_kernel<<<tiles, kScanThreads, 0, st>>>(n, counts, offsets, total_dev,
+  scan_kernel<<<tiles, kScanThreads, 0, st>>>(n, counts, nullptr, offsets, total_dev,
                                               reinterpret_cast<uint64_t *>(scratch), tiles,
                                               device_status_word());
   count_launch();
   return launch_status();
 }
 
-extern "C" size_t gs_sort_scratch_bytes(int64_t n) { return sort_layout(n > 0 ? n : 1).total; }
+extern "C" size_t gs_sort_scratch_bytes(int64_t n) {
+  return sort_layout<uint64_t>(n > 0 ? n : 1).total;
+}
 
 extern "C" int gs_sort_pairs(int64_t n, uint64_t *keys, int32_t *vals, uint64_t *keys_alt,
                              int32_t *vals_alt, int end_bit, void *scratch,
@@ -471,7 +675,7 @@ extern "C" int gs_sort_pairs(int64_t n, uint64_t *keys, int32_t *vals, uint64_t 
   if (scratch == nullptr || scratch_bytes < gs_sort_scratch_bytes(n)) return GS_ERR_CAPACITY;
   int passes = (end_bit + 7) / 8;
   cudaStream_t st = as_stream(stream);
-  int rc = run_sort(n, keys, vals, keys_alt, vals_alt, end_bit, scratch, st);
+  int rc = run_sort<uint64_t>(n, keys, vals, keys_alt, vals_alt, end_bit, scratch, st);
   if (rc) return rc;
   if (passes & 1) {
     rc = cuda_status(cudaMemcpyAsync(keys, keys_alt, n * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
@@ -481,21 +685,15 @@ extern "C" int gs_sort_pairs(int64_t n, uint64_t *keys, int32_t *vals, uint64_t 
   return rc;
 }
 
-// Scratch of gs_tile_layout: key buffer A (unless the caller keeps the keys),
-// key buffer B, value buffer B, sort state.
-extern "C" size_t gs_tile_layout_scratch_bytes(int64_t total, int width, int height) {
-  (void)width;
-  (void)height;
-  size_t t = (size_t)(total > 0 ? total : 1);
-  size_t bytes = align_up(t * sizeof(uint64_t), 256) * 2 + align_up(t * sizeof(int32_t), 256);
-  return bytes + gs_sort_scratch_bytes(total);
+extern "C" size_t gs_tile_layout_scratch_bytes(int n, int64_t total, int width, int height) {
+  return layout_scratch(n, total, tiles_x_of(width) * tiles_y_of(height)).total;
 }
 
 extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii,
-                              const float *depths, const uint8_t *mask, const int32_t *offsets,
-                              int64_t total, int width, int height, int64_t *keys_sorted,
-                              int32_t *ids_sorted, int32_t *indexing_offset, void *scratch,
-                              size_t scratch_bytes, void *stream) {
+                              const float *depths, const int32_t *counts, int64_t total,
+                              int width, int height, int64_t *keys_sorted, int32_t *ids_sorted,
+                              int32_t *indexing_offset, void *scratch, size_t scratch_bytes,
+                              void *stream) {
   if (n < 0 || width <= 0 || height <= 0 || total < 0) return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7)) return GS_ERR_INVALID_ARGUMENT;
   if (total >= (int64_t)kLbValue) return GS_ERR_CAPACITY;
@@ -503,37 +701,18 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
   const int num_tiles = tiles_x_of(width) * tiles_y_of(height);
   // rasterizer.cpp:352: offsets start at zero; with no pairs they stay zero.
   int rc = cuda_status(cudaMemsetAsync(indexing_offset, 0, (size_t)num_tiles * sizeof(int32_t), st));
-  if (rc || total == 0) return rc;
-  if (scratch == nullptr || scratch_bytes < gs_tile_layout_scratch_bytes(total, width, height))
-    return GS_ERR_CAPACITY;
+  if (rc || total == 0 || n == 0) return rc;
+  const LayoutScratch L = layout_scratch(n, total, num_tiles);
+  if (scratch == nullptr || scratch_bytes < L.total) return GS_ERR_CAPACITY;
   unsigned char *p = reinterpret_cast<unsigned char *>(scratch);
-  const size_t kbytes = align_up((size_t)total * sizeof(uint64_t), 256);
-  const size_t vbytes = align_up((size_t)total * sizeof(int32_t), 256);
-  uint64_t *keys_a = keys_sorted ? reinterpret_cast<uint64_t *>(keys_sorted)
-                                 : reinterpret_cast<uint64_t *>(p);
-  uint64_t *keys_b = reinterpret_cast<uint64_t *>(p + kbytes);
-  int32_t *vals_b = reinterpret_cast<int32_t *>(p + 2 * kbytes);
-  void *sort_scratch = p + 2 * kbytes + vbytes;
-  const int key_bits = key_bits_for_tiles(num_tiles);
-  const int passes = (key_bits + 7) / 8;
-  // Emit into the buffer pair that the final pass does not write, so the
-  // sorted result lands in (keys_a, ids_sorted).
-  uint64_t *k0 = (passes & 1) ? keys_b : keys_a;
-  int32_t *v0 = (passes & 1) ? vals_b : ids_sorted;
-  uint64_t *k1 = (passes & 1) ? keys_a : keys_b;
-  int32_t *v1 = (passes & 1) ? ids_sorted : vals_b;
-  if (n > 0) {
-    keygen_kernel<<<(n + 255) / 256, 256, 0, st>>>(
-        n, reinterpret_cast<const float2 *>(points_img), reinterpret_cast<const float2 *>(radii),
-        depths, mask, offsets, width, height, total, k0, v0);
-    count_launch();
-  }
-  rc = run_sort(total, k0, v0, k1, v1, key_bits, sort_scratch, st);
-  if (rc) return rc;
-  ranges_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(keys_a, total, num_tiles,
-                                                                  indexing_offset);
-  count_launch();
-  return launch_status();
+  const float2 *pts = reinterpret_cast<const float2 *>(points_img);
+  const float2 *rad = reinterpret_cast<const float2 *>(radii);
+  uint64_t *ks = reinterpret_cast<uint64_t *>(keys_sorted);
+  if (num_tiles <= 65536)
+    return tile_layout_impl<uint16_t>(n, pts, rad, depths, counts, total, width, height, ks,
+                                      ids_sorted, indexing_offset, p, L, st);
+  return tile_layout_impl<uint32_t>(n, pts, rad, depths, counts, total, width, height, ks,
+                                    ids_sorted, indexing_offset, p, L, st);
 }
 
 // ---- exclusive scan without caller-provided scratch -----------------------
@@ -583,8 +762,8 @@ extern "C" int gs_exclusive_scan_noalloc(int n, const int32_t *counts, int32_t *
   // part this call uses (tiles + 1 words) before the launch, on the same stream.
   rc = cuda_status(cudaMemsetAsync(words, 0, (size_t)(tiles + 1) * sizeof(uint64_t), st));
   if (rc) return rc;
-  scan_kernel<<<tiles, kScanThreads, 0, st>>>(n, counts, offsets, total_dev, words, tiles,
-                                              device_status_word());
+  scan_kernel<<<tiles, kScanThreads, 0, st>>>(n, counts, nullptr, offsets, total_dev, words,
+                                              tiles, device_status_word());
   count_launch();
   return launch_status();
 }

@@ -135,20 +135,20 @@ def _read_total(total_dev, dev):
     return int(host.item())
 
 
-def tile_layout_from_offsets(points_image, radii, depths, mask, offsets, total, width, height,
-                             return_keys=False):
-    """Key duplication + onesweep sort + tile ranges, given the per-Gaussian
-    output offsets (exclusive scan of the tile counts) and their total."""
+def tile_layout_from_counts(points_image, radii, depths, counts, total, width, height,
+                            return_keys=False):
+    """Tile layout (pairs sorted by tile then depth bits, and per-tile start
+    offsets) from the per-Gaussian tile counts and their total."""
     dev = points_image.device
     tx, ty = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
     indexing_offset = torch.empty((tx * ty,), device=dev, dtype=torch.int32)
     ids = torch.empty((total,), device=dev, dtype=torch.int32)
     keys = torch.empty((total,), device=dev, dtype=torch.int64) if return_keys else None
-    nbytes = int(nat.query("gs_tile_layout_scratch_bytes", total, int(width), int(height)))
-    scratch = torch.empty((nbytes,), device=dev, dtype=torch.uint8)
     n = points_image.shape[0]
+    nbytes = int(nat.query("gs_tile_layout_scratch_bytes", n, total, int(width), int(height)))
+    scratch = torch.empty((nbytes,), device=dev, dtype=torch.uint8)
     nat.call("gs_tile_layout", n, points_image.data_ptr(), radii.data_ptr(), depths.data_ptr(),
-             _mask_u8(mask).data_ptr(), offsets.data_ptr(), int(total), int(width), int(height),
+             counts.data_ptr(), int(total), int(width), int(height),
              keys.data_ptr() if keys is not None else None, ids.data_ptr(),
              indexing_offset.data_ptr(), scratch.data_ptr(), nbytes, nat.stream_ptr(dev))
     if return_keys:
@@ -167,7 +167,7 @@ def compute_tile_intersection(points_image, radii, depths, mask, width, height, 
     n = pts.shape[0]
     with torch.cuda.device(dev):
         st = nat.stream_ptr(dev)
-        counts = torch.zeros((n,), device=dev, dtype=torch.int32)
+        counts = torch.zeros((max(n, 1),), device=dev, dtype=torch.int32)
         offsets = torch.empty((max(n, 1),), device=dev, dtype=torch.int32)
         total_dev = torch.zeros((1,), device=dev, dtype=torch.int64)
         nat.call("gs_count_tiles", n, pts.data_ptr(), rad.data_ptr(), _mask_u8(m).data_ptr(),
@@ -177,8 +177,8 @@ def compute_tile_intersection(points_image, radii, depths, mask, width, height, 
         nat.call("gs_exclusive_scan", n, counts.data_ptr(), offsets.data_ptr(),
                  total_dev.data_ptr(), scratch.data_ptr(), sbytes, st)
         total = _read_total(total_dev, dev)
-        return tile_layout_from_offsets(pts, rad, dep, m, offsets, total, int(width),
-                                        int(height), return_keys=return_keys)
+        return tile_layout_from_counts(pts, rad, dep, counts, total, int(width), int(height),
+                                       return_keys=return_keys)
 
 
 def rasterize(indexing_offset, gaussian_ids_sorted, points_image, cov_inv_image, opacities,

@@ -123,7 +123,7 @@ def _require(name, t, dtype, dev, shape_tail=None):
 
 
 class _Preprocess(torch.autograd.Function):
-    """Fused projection + covariance + SH + tile counts/scan; backward is the
+    """Fused projection + covariance + SH + tile counts; backward is the
     fused chain through projection, covariance and SH."""
 
     @staticmethod
@@ -137,24 +137,21 @@ class _Preprocess(torch.autograd.Function):
         radii = torch.empty((n, 2), **f)
         mask = torch.empty((n,), device=dev, dtype=torch.bool)
         splat = torch.empty((n, 8), **f)
-        offsets = torch.empty((max(n, 1),), device=dev, dtype=torch.int32)
+        counts = torch.empty((max(n, 1),), device=dev, dtype=torch.int32)
         total_dev = torch.empty((1,), device=dev, dtype=torch.int64)
-        sbytes = int(nat.query("gs_preprocess_scratch_bytes", n))
-        scratch = torch.empty((max(sbytes, 8),), device=dev, dtype=torch.uint8)
         nat.call("gs_preprocess_forward", n, means.data_ptr(), scales.data_ptr(),
                  quaternions.data_ptr(), opacities.data_ptr(), sh_dc.data_ptr(),
                  sh_rest.data_ptr(), world_to_camera.data_ptr(), intrinsic.data_ptr(),
                  camera_pos.data_ptr(), opts["near_plane"], opts["far_plane"],
                  opts["min_opacity"], opts["min_radius"], opts["max_radius"], opts["width"],
                  opts["height"], int(opts["sh_sigmoid"]), points.data_ptr(), depths.data_ptr(),
-                 radii.data_ptr(), mask.view(torch.uint8).data_ptr(), splat.data_ptr(), None,
-                 offsets.data_ptr(), total_dev.data_ptr(), scratch.data_ptr(), sbytes,
-                 nat.stream_ptr(dev))
+                 radii.data_ptr(), mask.view(torch.uint8).data_ptr(), splat.data_ptr(),
+                 counts.data_ptr(), total_dev.data_ptr(), nat.stream_ptr(dev))
         ctx.save_for_backward(means, scales, quaternions, sh_dc, sh_rest, world_to_camera,
                               intrinsic, camera_pos, mask)
         ctx.opts = opts
-        ctx.mark_non_differentiable(depths, radii, mask, offsets, total_dev)
-        return points, splat, depths, radii, mask, offsets, total_dev
+        ctx.mark_non_differentiable(depths, radii, mask, counts, total_dev)
+        return points, splat, depths, radii, mask, counts, total_dev
 
     @staticmethod
     def backward(ctx, g_points, g_splat, _gd, _gr, _gm, _go, _gt):
@@ -263,11 +260,11 @@ def render(world_to_camera, intrinsic, width, height, means, scales, quaternions
     with torch.cuda.device(dev):
         # wrapper.py:260, computed the same way
         camera_pos = (-world_to_camera[:3, :3].t() @ world_to_camera[:3, 3]).contiguous()
-        points, splat, depths, radii, mask, offsets, total_dev = _Preprocess.apply(
+        points, splat, depths, radii, mask, counts, total_dev = _Preprocess.apply(
             means, scales, quaternions, opacities, sh_coeffs_dc, sh_coeffs_rest,
             world_to_camera, intrinsic, camera_pos.detach(), opts)
         total = cuda_rasterizer._read_total(total_dev, dev)
-        indexing_offset, ids = cuda_rasterizer.tile_layout_from_offsets(
-            points.detach(), radii, depths, mask, offsets, total, width, height)
+        indexing_offset, ids = cuda_rasterizer.tile_layout_from_counts(
+            points.detach(), radii, depths, counts, total, width, height)
         image = _Blend.apply(points, splat, indexing_offset, ids, opts)
     return image.clamp(0, 1) * 255, points, radii

@@ -130,20 +130,22 @@ GS_API int gs_exclusive_scan_noalloc(int n, const int32_t *counts, int32_t *offs
  * gave up since the last check. */
 GS_API int gs_read_total(const int64_t *total_dev, int64_t *total_host, void *stream);
 
-/* Scratch for gs_tile_layout with `total` pairs on a width x height image. */
-GS_API size_t gs_tile_layout_scratch_bytes(int64_t total, int width, int height);
+/* Scratch for gs_tile_layout: n Gaussians, `total` pairs, width x height image. */
+GS_API size_t gs_tile_layout_scratch_bytes(int n, int64_t total, int width, int height);
 
-/* Emits (tile << 32 | depth bits, id) pairs in Gaussian order and tile
- * row-major order (kernel.cu:820-873), sorts them stably with an in-house
- * onesweep LSD radix sort over the 32 + ceil(log2 tiles) significant bits
- * (the reference sorts all 64 with CUB, same result), and writes the
- * per-tile start offsets (kernel.cu:875-914). Outputs: keys_sorted (total,
- * may be NULL), ids_sorted (total), indexing_offset (tiles_x * tiles_y). */
+/* Builds the reference's tile layout (kernel.cu:820-914 with the CUB sort of
+ * kernel.cu:1341-1388): the per-tile lists of Gaussian ids ordered by
+ * (tile, depth bits), ties by Gaussian id, and the per-tile start offsets.
+ * Done as two stable onesweep radix sorts -- the n Gaussians by depth bits,
+ * then the pairs (emitted in that order) by tile id -- which yields the
+ * reference's order exactly. counts are the per-Gaussian tile counts
+ * (gs_count_tiles, 0 for culled Gaussians), total their sum. Outputs:
+ * keys_sorted (the reference's 64-bit keys; may be NULL), ids_sorted (total),
+ * indexing_offset (tiles_x * tiles_y). */
 GS_API int gs_tile_layout(int n, const float *points_img, const float *radii, const float *depths,
-                   const uint8_t *mask, const int32_t *offsets, int64_t total, int width,
-                   int height, int64_t *keys_sorted, int32_t *ids_sorted,
-                   int32_t *indexing_offset, void *scratch, size_t scratch_bytes,
-                   void *stream);
+                   const int32_t *counts, int64_t total, int width, int height,
+                   int64_t *keys_sorted, int32_t *ids_sorted, int32_t *indexing_offset,
+                   void *scratch, size_t scratch_bytes, void *stream);
 
 /* Stable LSD radix sort of (uint64 key, int32 value) pairs on key bits
  * [0, end_bit). Replaces radix_sort_double_buffer (kernel.cu:1341-1388).
@@ -181,15 +183,13 @@ GS_API int gs_rasterize_backward(int num_tiles, const int32_t *indexing_offset, 
 
 /* ---- fused render path (used by render() in the Python package) ---------
  * gs_preprocess_forward replaces project_points + evaluate_spherical_harmonics
- * + the colour shift/clamp of wrapper.py:264-265 + count_tiles + the cumsum
- * of rasterizer.cpp:319 in one pass: projection, EWA covariance, conic,
- * radii, SH colour, tile count, and the exclusive scan of the tile counts
- * (tile_offsets, total into *total_dev). The splat record is float[8] per
- * Gaussian: conic (a, b, c), opacity, colour (r, g, b), 0. Every output
- * element is written (zeros for culled Gaussians). tile_counts may be NULL.
- * camera_pos is the device float[3] -R^T t (wrapper.py:260).
- * Scratch: gs_preprocess_scratch_bytes(n). */
-GS_API size_t gs_preprocess_scratch_bytes(int n);
+ * + the colour shift/clamp of wrapper.py:264-265 + count_tiles + the total of
+ * rasterizer.cpp:319-322 in one pass: projection, EWA covariance, conic,
+ * radii, SH colour, per-Gaussian tile counts, and their sum added into
+ * *total_dev (int64; zeroed by this call before the kernel). The splat record
+ * is float[8] per Gaussian: conic (a, b, c), opacity, colour (r, g, b), 0.
+ * Every output element is written (zeros for culled Gaussians). camera_pos is
+ * the device float[3] -R^T t (wrapper.py:260). */
 GS_API int gs_preprocess_forward(int n, const float *means, const float *scales, const float *quats,
                           const float *opacities, const float *sh_dc, const float *sh_rest,
                           const float *world_to_camera, const float *intrinsic,
@@ -197,8 +197,7 @@ GS_API int gs_preprocess_forward(int n, const float *means, const float *scales,
                           float min_opacity, float min_radius, float max_radius, int width,
                           int height, int sh_sigmoid, float *points_img, float *depths,
                           float *radii, uint8_t *mask, float *splat, int32_t *tile_counts,
-                          int32_t *tile_offsets, int64_t *total_dev, void *scratch,
-                          size_t scratch_bytes, void *stream);
+                          int64_t *total_dev, void *stream);
 
 /* Blend forward over the splat records; also writes each pixel's final
  * transmittance and end index (one past its last contributing list entry).

@@ -450,3 +450,22 @@ def test_cfg1_layout_and_image_properties(gs, orc):
                         16, 1e-4, 1e-4, 9.21)
     d = np.abs(img - ref)
     assert (d > 1e-4).mean() < 1e-5 and d.max() < 1e-2, ((d > 1e-4).sum(), d.max())
+
+
+@pytest.mark.parametrize("n", [1, 2047, 2048, 2049, 131_079, 1_000_000, 5_000_001])
+def test_exclusive_scan_matches_cumsum(gs, n):
+    """The look-back scan against torch.cumsum, at sizes whose look-back
+    windows reach past 32 predecessors without finding a prefix."""
+    nat = importlib.import_module("3dgs_from_scratch_b200._native")
+    g = torch.Generator(DEV).manual_seed(n)
+    c = torch.randint(0, 50, (n,), dtype=torch.int32, device=DEV, generator=g)
+    out = torch.empty(n, dtype=torch.int32, device=DEV)
+    tot = torch.zeros(1, dtype=torch.int64, device=DEV)
+    nb = int(nat.query("gs_scan_scratch_bytes", n))
+    sc = torch.empty(nb, dtype=torch.uint8, device=DEV)
+    nat.call("gs_exclusive_scan", n, c.data_ptr(), out.data_ptr(), tot.data_ptr(), sc.data_ptr(), nb,
+             nat.stream_ptr())
+    ref = torch.cumsum(c.long(), 0) - c.long()
+    assert torch.equal(out.long(), ref)
+    assert int(tot.item()) == int(c.long().sum().item())
+    assert nat.query("gs_check_status", nat.stream_ptr()) == 0

@@ -56,8 +56,7 @@ def test_host_queries(gs):
     a = lib.gs_sort_scratch_bytes(10_000)
     b = lib.gs_sort_scratch_bytes(10_000_000)
     assert 0 < a < b
-    assert lib.gs_tile_layout_scratch_bytes(1000, 64, 64) > 1000 * 20
-    assert lib.gs_preprocess_scratch_bytes(1000) >= 8 * 8
+    assert lib.gs_tile_layout_scratch_bytes(100, 1000, 64, 64) > 1000 * 6
     assert lib.gs_scan_scratch_bytes(100_000) >= 8
 
 
