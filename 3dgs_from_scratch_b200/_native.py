@@ -59,6 +59,7 @@ SIGNATURES = {
                                   P, P, P, P, P]),
     "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P]),
+    "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
     "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, I, I, I, P, P, I, P, I, P, P, P, P,
                                    P, P, P]),
 }

@@ -1,0 +1,105 @@
+// adam.cu -- one-launch Adam over a flat fp32 parameter buffer.
+//
+// The training loop of the reference (scripts/train.py:17-44,219-221) runs
+// six torch.optim.Adam instances, one per parameter group (means, scales,
+// quaternions, opacities, sh_dc, sh_rest), each with its own learning rate
+// and eps = 1e-15. When the six groups are laid out back to back in one flat
+// buffer (as the data-parallel trainer does, so that one all-reduce covers
+// every gradient), a single grid-stride kernel updates all of them: per
+// element it reads param, grad, exp_avg, exp_avg_sq and writes param,
+// exp_avg, exp_avg_sq (28 B), 128-bit vectorised. Arithmetic follows
+// torch.optim.Adam's default (non-amsgrad, no weight decay) update:
+//   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2
+//   p -= lr / (1 - b1^t) * m / (sqrt(v) / sqrt(1 - b2^t) + eps)
+#include "gs_common.cuh"
+
+namespace gs {
+
+constexpr int kAdamMaxGroups = 8;
+
+struct AdamGroups {
+  int64_t end[kAdamMaxGroups];  // exclusive end (in elements) of each group, multiples of 4
+  float step_size[kAdamMaxGroups];   // lr / (1 - b1^t)
+  float inv_bc2_sqrt[kAdamMaxGroups];  // 1 / sqrt(1 - b2^t)
+  float eps[kAdamMaxGroups];
+  int count;
+};
+
+__device__ __forceinline__ float adam_one(float &p, float g, float &m, float &v, float b1,
+                                          float b2, float step, float ibc2, float eps) {
+  m = b1 * m + (1.0f - b1) * g;
+  v = b2 * v + (1.0f - b2) * g * g;
+  const float denom = sqrtf(v) * ibc2 + eps;
+  p = p - step * (m / denom);
+  return p;
+}
+
+__global__ void __launch_bounds__(256) adam_kernel(float4 *__restrict__ p, const float4 *__restrict__ g,
+                                                   float4 *__restrict__ m, float4 *__restrict__ v,
+                                                   int64_t n4, AdamGroups G, float b1, float b2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int64_t e = 4 * i;
+    int grp = 0;
+#pragma unroll
+    for (int k = 0; k < kAdamMaxGroups - 1; ++k) grp += (k < G.count - 1 && e >= G.end[k]) ? 1 : 0;
+    const float st = G.step_size[grp], ib = G.inv_bc2_sqrt[grp], ep = G.eps[grp];
+    float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
+    adam_one(pp.x, gg.x, mm.x, vv.x, b1, b2, st, ib, ep);
+    adam_one(pp.y, gg.y, mm.y, vv.y, b1, b2, st, ib, ep);
+    adam_one(pp.z, gg.z, mm.z, vv.z, b1, b2, st, ib, ep);
+    adam_one(pp.w, gg.w, mm.w, vv.w, b1, b2, st, ib, ep);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_adam_step(int64_t n, float *params, const float *grads, float *exp_avg,
+                            float *exp_avg_sq, int num_groups, const int64_t *group_ends,
+                            const float *lrs, const float *eps, float beta1, float beta2,
+                            int64_t step, void *stream) {
+  if (n < 0 || num_groups < 1 || num_groups > kAdamMaxGroups || step < 1 || (n & 3))
+    return GS_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)params | (uintptr_t)grads | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq) & 15))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return GS_OK;
+  AdamGroups G;
+  G.count = num_groups;
+  const double bc1 = 1.0 - pow((double)beta1, (double)step);
+  const double bc2 = 1.0 - pow((double)beta2, (double)step);
+  int64_t prev = 0;
+  for (int k = 0; k < kAdamMaxGroups; ++k) {
+    if (k < num_groups) {
+      if (group_ends[k] < prev || (group_ends[k] & 3)) return GS_ERR_INVALID_ARGUMENT;
+      prev = group_ends[k];
+      G.end[k] = group_ends[k];
+      G.step_size[k] = (float)((double)lrs[k] / bc1);
+      G.inv_bc2_sqrt[k] = (float)(1.0 / sqrt(bc2));
+      G.eps[k] = eps[k];
+    } else {
+      G.end[k] = n;
+      G.step_size[k] = 0.f;
+      G.inv_bc2_sqrt[k] = 1.f;
+      G.eps[k] = 1.f;
+    }
+  }
+  if (prev != n) return GS_ERR_INVALID_ARGUMENT;
+  const int64_t n4 = n / 4;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n4 + 255) / 256;
+  const int grid = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  adam_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
+      reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), n4, G, beta1,
+      beta2);
+  count_launch();
+  return launch_status();
+}

@@ -5,14 +5,18 @@
 //    backwards; ruguangyou/3dgs_from_scratch src/cuda/kernel.cu:411-782),
 //    one thread per Gaussian, writing the reference's separate output arrays;
 //  * the fused path used by render(): one forward kernel that does projection,
-//    EWA covariance, conic, radii, SH colour, tile count and the exclusive scan
-//    of the tile counts (decoupled look-back) in a single pass, and one
-//    backward kernel for the whole projection + covariance + SH chain.
+//    EWA covariance, conic, radii, SH colour and tile counts (plus their sum)
+//    in a single pass, and one backward kernel for the whole projection +
+//    covariance + SH chain.
 //
-// The fused kernels stage each block's contiguous slice of the AoS parameter
-// arrays (means, scales, quats, opacities, sh_dc, sh_rest: 236 B/Gaussian)
-// into shared memory with 128-bit coalesced loads, so every warp-wide global
-// access is a full, aligned transaction even for the 180 B/Gaussian SH block.
+// The fused kernels work on chunks of 128 Gaussians: each chunk's contiguous
+// slice of the AoS parameter arrays (means, scales, quats, opacities, sh_dc,
+// sh_rest: 236 B/Gaussian) is brought into shared memory by the TMA engine
+// (cp.async.bulk, completion on an mbarrier) in persistent, double-buffered
+// blocks, so the next chunk streams in while the current one is computed; the
+// backward's 236 B/Gaussian of gradients leave through bulk stores. A tail
+// chunk, or unaligned pointers, use a one-chunk-per-block variant that stages
+// with 128-bit loads.
 #include "gs_common.cuh"
 
 namespace gs {
@@ -148,9 +152,10 @@ __global__ void __launch_bounds__(256) sh_backward_kernel(
 // fused path
 // ---------------------------------------------------------------------------
 
-constexpr int kPreBlock = 128;  // Gaussians (and threads) per block
+constexpr int kPreBlock = 128;  // Gaussians (and threads) per chunk
 
-// Shared-memory image of one block's parameter slice, AoS as in HBM.
+// Shared-memory image of one chunk's parameter slice, AoS as in HBM. Every
+// member starts on a 16-byte boundary (bulk-copy destinations).
 struct PreSmem {
   float means[kPreBlock * 3];
   float scales[kPreBlock * 3];
@@ -184,187 +189,338 @@ __device__ __forceinline__ void stage_out(float *__restrict__ dst, const float *
   }
 }
 
-// Fused forward: one thread per Gaussian. Tile counts are written per
-// Gaussian and their block sum is added into *total_out.
-__global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(
-    int n, const float *__restrict__ means, const float *__restrict__ scales,
-    const float *__restrict__ quats, const float *__restrict__ opac,
-    const float *__restrict__ dc, const float *__restrict__ rest,
-    const float *__restrict__ w2c, const float *__restrict__ K,
-    const float *__restrict__ campos, float near_plane, float far_plane, float min_opacity,
-    float min_radius, float max_radius, int width, int height, int sh_sigmoid,
-    float2 *__restrict__ points, float *__restrict__ depths, float2 *__restrict__ radii,
-    uint8_t *__restrict__ mask, float4 *__restrict__ splat, int32_t *__restrict__ tile_counts,
-    unsigned long long *__restrict__ total_out) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
-  const int first = blockIdx.x * kPreBlock;
-  const int cnt = min(kPreBlock, n - first);
-  const size_t f = (size_t)first;
-  stage(S.means, means + 3 * f, 3 * cnt);
-  stage(S.scales, scales + 3 * f, 3 * cnt);
-  stage(S.quats, quats + 4 * f, 4 * cnt);
-  stage(S.opac, opac + f, cnt);
-  stage(S.dc, dc + 3 * f, 3 * cnt);
-  stage(S.rest, rest + 45 * f, 45 * cnt);
-  __syncthreads();
+struct PreFwdArgs {
+  const float *means, *scales, *quats, *opac, *dc, *rest, *w2c, *K, *campos;
+  float near_plane, far_plane, min_opacity, min_radius, max_radius;
+  int width, height, sh_sigmoid;
+  float2 *points;
+  float *depths;
+  float2 *radii;
+  uint8_t *mask;
+  float4 *splat;
+  int32_t *tile_counts;
+  unsigned long long *total;
+};
 
-  const int t = threadIdx.x;
-  const int i = first + t;
+// Forward for Gaussian i = first + t from the staged chunk; returns its tile count.
+__device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S, int t, int i) {
+  Cam c = load_cam(A.w2c, A.K);
+  const float *m = S.means + 3 * t;
+  const float *s = S.scales + 3 * t;
+  const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+  Projected p = project_one(c, A.width, A.height, A.near_plane, A.far_plane, A.min_opacity,
+                            A.min_radius, A.max_radius, m[0], m[1], m[2], s[0], s[1], s[2], q.x,
+                            q.y, q.z, q.w, S.opac[t]);
+  float2 pt = make_float2(0.f, 0.f), rd = make_float2(0.f, 0.f);
+  float depth = 0.f;
+  float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = make_float4(0.f, 0.f, 0.f, 0.f);
   int count = 0;
-  if (t < cnt) {
-    Cam c = load_cam(w2c, K);
-    const float *m = S.means + 3 * t;
-    const float *s = S.scales + 3 * t;
-    const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
-    Projected p = project_one(c, width, height, near_plane, far_plane, min_opacity, min_radius,
-                              max_radius, m[0], m[1], m[2], s[0], s[1], s[2], q.x, q.y, q.z, q.w,
-                              S.opac[t]);
-    float2 pt = make_float2(0.f, 0.f), rd = make_float2(0.f, 0.f);
-    float depth = 0.f;
-    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p.visible) {
-      ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), m[0], m[1], m[2]);
-      float b[16];
-      sh_basis(d.x, d.y, d.z, b);
-      const float *r = S.rest + 45 * t;
-      float rgb[3];
+  if (p.visible) {
+    ViewDir d = view_dir(__ldg(A.campos), __ldg(A.campos + 1), __ldg(A.campos + 2), m[0], m[1], m[2]);
+    float b[16];
+    sh_basis(d.x, d.y, d.z, b);
+    const float *r = S.rest + 45 * t;
+    float rgb[3];
 #pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        float a = b[0] * S.dc[3 * t + ch];
+    for (int ch = 0; ch < 3; ++ch) {
+      float a = b[0] * S.dc[3 * t + ch];
 #pragma unroll
-        for (int k = 0; k < 15; ++k) a += b[k + 1] * r[k * 3 + ch];
-        if (sh_sigmoid) {
-          a = ref_sigmoid(a);
-        } else {
-          a = a + 0.5f;                 // wrapper.py:264-265: clamp_min(colors + 0.5, 0)
-          a = (a < 0.0f) ? 0.0f : a;    // NaN propagates, as in torch.clamp_min
-        }
-        rgb[ch] = a;
+      for (int k = 0; k < 15; ++k) a += b[k + 1] * r[k * 3 + ch];
+      if (A.sh_sigmoid) {
+        a = ref_sigmoid(a);
+      } else {
+        a = a + 0.5f;               // wrapper.py:264-265: clamp_min(colors + 0.5, 0)
+        a = (a < 0.0f) ? 0.0f : a;  // NaN propagates, as in torch.clamp_min
       }
-      pt = make_float2(p.u, p.v);
-      rd = make_float2(p.ru, p.rv);
-      depth = p.depth;
-      s0 = make_float4(p.conic.x, p.conic.y, p.conic.z, S.opac[t]);
-      s1 = make_float4(rgb[0], rgb[1], rgb[2], 0.f);
-      TileRect tr = tile_rect(p.u, p.v, p.ru, p.rv, width, height);
-      count = tr.empty ? 0 : (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
+      rgb[ch] = a;
     }
-    points[i] = pt;
-    radii[i] = rd;
-    depths[i] = depth;
-    mask[i] = p.visible ? 1 : 0;
-    splat[2 * (size_t)i] = s0;
-    splat[2 * (size_t)i + 1] = s1;
-    tile_counts[i] = count;
+    pt = make_float2(p.u, p.v);
+    rd = make_float2(p.ru, p.rv);
+    depth = p.depth;
+    s0 = make_float4(p.conic.x, p.conic.y, p.conic.z, S.opac[t]);
+    s1 = make_float4(rgb[0], rgb[1], rgb[2], 0.f);
+    TileRect tr = tile_rect(p.u, p.v, p.ru, p.rv, A.width, A.height);
+    count = tr.empty ? 0 : (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
   }
-  // Sum of the tile counts: warp reduction, one atomic per warp.
+  A.points[i] = pt;
+  A.radii[i] = rd;
+  A.depths[i] = depth;
+  A.mask[i] = p.visible ? 1 : 0;
+  A.splat[2 * (size_t)i] = s0;
+  A.splat[2 * (size_t)i + 1] = s1;
+  A.tile_counts[i] = count;
+  return count;
+}
+
+// Sum of the tile counts: warp reduction, one atomic per warp.
+__device__ __forceinline__ void add_total(unsigned long long *total, int count) {
   unsigned long long c = (unsigned long long)count;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if ((t & 31) == 0 && c) atomicAdd(total_out, c);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(total, c);
 }
 
-// Fused backward: one thread per Gaussian. Writes every output element
-// (zeros for Gaussians that were culled).
-__global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(
-    int n, const float *__restrict__ means, const float *__restrict__ scales,
-    const float *__restrict__ quats, const float *__restrict__ dc,
-    const float *__restrict__ rest, const float *__restrict__ w2c,
-    const float *__restrict__ K, const float *__restrict__ campos, int width, int height,
-    int sh_sigmoid, const uint8_t *__restrict__ mask, const float *__restrict__ g_points,
-    int gp_stride, const float *__restrict__ g_splat, int gs_stride,
-    float *__restrict__ g_means, float *__restrict__ g_scales, float *__restrict__ g_quats,
-    float *__restrict__ g_opac, float *__restrict__ g_dc, float *__restrict__ g_rest) {
+// Fused forward, one chunk per block, staged with 128-bit loads. Handles
+// Gaussians [base, n) (any alignment); used for the tail of the pipelined
+// kernel and when a pointer is not 16-byte aligned.
+__global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArgs A, int n, int base) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
-  const int first = blockIdx.x * kPreBlock;
+  const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
-  stage(S.means, means + 3 * f, 3 * cnt);
-  stage(S.scales, scales + 3 * f, 3 * cnt);
-  stage(S.quats, quats + 4 * f, 4 * cnt);
-  stage(S.dc, dc + 3 * f, 3 * cnt);
-  stage(S.rest, rest + 45 * f, 45 * cnt);
+  stage(S.means, A.means + 3 * f, 3 * cnt);
+  stage(S.scales, A.scales + 3 * f, 3 * cnt);
+  stage(S.quats, A.quats + 4 * f, 4 * cnt);
+  stage(S.opac, A.opac + f, cnt);
+  stage(S.dc, A.dc + 3 * f, 3 * cnt);
+  stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
-
   const int t = threadIdx.x;
-  const int i = first + t;
-  // Results for means/scales/quats/dc are staged in place of the inputs
-  // (each thread only overwrites its own slots after reading them); the
-  // 45 SH-rest gradients go to S.rest the same way.
-  if (t < cnt) {
-    float *m = S.means + 3 * t;
-    float *s = S.scales + 3 * t;
-    float *qq = S.quats + 4 * t;
-    float *dcc = S.dc + 3 * t;
-    float *r = S.rest + 45 * t;
-    float opac_grad = 0.f;
-    if (mask[i]) {
-      Cam c = load_cam(w2c, K);
-      float px = m[0], py = m[1], pz = m[2];
-      float sx = s[0], sy = s[1], sz = s[2];
-      float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
-      float3 pc = to_camera(c, px, py, pz);
-      float3 cov = image_cov(c, width, height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
-      const float *gp = g_points + (size_t)i * gp_stride;
-      const float *gsp = g_splat + (size_t)i * gs_stride;
-      float gm[3], gsc[3], gq[4];
-      project_backward_one(c, width, height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
-                           cov, gsp[0], gsp[1], gsp[2], gm, gsc, gq);
-      opac_grad = gsp[3];
+  const int count = (t < cnt) ? pre_fwd_one(A, S, t, first + t) : 0;
+  add_total(A.total, count);
+}
 
-      ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), px, py, pz);
-      float b[16];
-      sh_basis(d.x, d.y, d.z, b);
-      float g[3];
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        float raw = b[0] * dcc[ch];
-#pragma unroll
-        for (int k = 0; k < 15; ++k) raw += b[k + 1] * r[k * 3 + ch];
-        float gc = gsp[4 + ch];
-        if (sh_sigmoid) {
-          float col = ref_sigmoid(raw);
-          gc *= col * (1.0f - col);
-        } else {
-          gc = (raw + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
-        }
-        g[ch] = gc;
-      }
-      float3 gmsh = sh_dir_backward(d, g[0], g[1], g[2], [&](int k, int ch) { return r[k * 3 + ch]; });
-#pragma unroll
-      for (int k = 0; k < 15; ++k)
-#pragma unroll
-        for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = g[ch] * b[k + 1];
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) dcc[ch] = g[ch] * b[0];
-      m[0] = gm[0] + gmsh.x;
-      m[1] = gm[1] + gmsh.y;
-      m[2] = gm[2] + gmsh.z;
-      s[0] = gsc[0];
-      s[1] = gsc[1];
-      s[2] = gsc[2];
-      qq[0] = gq[0];
-      qq[1] = gq[1];
-      qq[2] = gq[2];
-      qq[3] = gq[3];
-    } else {
-#pragma unroll
-      for (int k = 0; k < 3; ++k) m[k] = s[k] = dcc[k] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) qq[k] = 0.f;
-#pragma unroll
-      for (int k = 0; k < 45; ++k) r[k] = 0.f;
-    }
-    if (g_opac) g_opac[i] = opac_grad;
+// Bulk loads of one full chunk (kPreBlock Gaussians from `first`) into S,
+// completing on `bar`. With opac == nullptr the opacities are not loaded.
+__device__ __forceinline__ void issue_chunk(PreSmem &S, uint64_t *bar, size_t f, const float *means,
+                                            const float *scales, const float *quats,
+                                            const float *opac, const float *dc,
+                                            const float *rest) {
+  const uint32_t bytes = kPreBlock * 4 * (3 + 3 + 4 + 3 + 45) + (opac ? kPreBlock * 4 : 0);
+  mbar_expect_tx(bar, bytes);
+  bulk_load(S.means, means + 3 * f, kPreBlock * 12, bar);
+  bulk_load(S.scales, scales + 3 * f, kPreBlock * 12, bar);
+  bulk_load(S.quats, quats + 4 * f, kPreBlock * 16, bar);
+  if (opac) bulk_load(S.opac, opac + f, kPreBlock * 4, bar);
+  bulk_load(S.dc, dc + 3 * f, kPreBlock * 12, bar);
+  bulk_load(S.rest, rest + 45 * f, kPreBlock * 180, bar);
+}
+
+// Fused forward, persistent and double-buffered: while a block computes chunk
+// c from one shared-memory stage, the TMA engine fills the other stage with
+// chunk c + gridDim.x. Only full chunks; all parameter pointers 16-byte aligned.
+__global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreFwdArgs A,
+                                                                           int num_chunks,
+                                                                           uint32_t *status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
+  __shared__ __align__(8) uint64_t bars[2];
+  const int t = threadIdx.x;
+  if (t == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  stage_out(g_means + 3 * f, S.means, 3 * cnt);
-  stage_out(g_scales + 3 * f, S.scales, 3 * cnt);
-  stage_out(g_quats + 4 * f, S.quats, 4 * cnt);
-  stage_out(g_dc + 3 * f, S.dc, 3 * cnt);
-  stage_out(g_rest + 45 * f, S.rest, 45 * cnt);
+  int c = blockIdx.x;
+  if (t == 0 && c < num_chunks)
+    issue_chunk(stg[0], &bars[0], (size_t)c * kPreBlock, A.means, A.scales, A.quats, A.opac, A.dc,
+                A.rest);
+  uint32_t phase = 0;  // bit s: parity of the next completion of bars[s]
+  int s = 0;
+  for (; c < num_chunks; c += gridDim.x) {
+    const int nc = c + gridDim.x;
+    if (t == 0 && nc < num_chunks)
+      issue_chunk(stg[s ^ 1], &bars[s ^ 1], (size_t)nc * kPreBlock, A.means, A.scales, A.quats,
+                  A.opac, A.dc, A.rest);
+    // every thread polls (bounded); the abort decision is made block-wide
+    if (!__syncthreads_and(mbar_wait(&bars[s], (phase >> s) & 1u))) {
+      if (t == 0) {
+        atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
+        // let the copies already issued land before the block exits (bounded)
+        mbar_wait(&bars[s], (phase >> s) & 1u);
+        if (nc < num_chunks) mbar_wait(&bars[s ^ 1], (phase >> (s ^ 1)) & 1u);
+      }
+      return;
+    }
+    phase ^= 1u << s;
+    const int count = pre_fwd_one(A, stg[s], t, c * kPreBlock + t);
+    add_total(A.total, count);
+    __syncthreads();  // every thread is done with stg[s] before it is refilled
+    s ^= 1;
+  }
+}
+
+struct PreBwdArgs {
+  const float *means, *scales, *quats, *dc, *rest, *w2c, *K, *campos;
+  int width, height, sh_sigmoid;
+  const uint8_t *mask;
+  const float *g_points;
+  int gp_stride;
+  const float *g_splat;
+  int gs_stride;
+  float *g_means, *g_scales, *g_quats, *g_opac, *g_dc, *g_rest;
+};
+
+// Backward for Gaussian i = first + t: reads the staged parameters and
+// overwrites them in place with its gradients (zeros for culled Gaussians).
+__device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int t, int i) {
+  float *m = S.means + 3 * t;
+  float *s = S.scales + 3 * t;
+  float *qq = S.quats + 4 * t;
+  float *dcc = S.dc + 3 * t;
+  float *r = S.rest + 45 * t;
+  float opac_grad = 0.f;
+  if (A.mask[i]) {
+    Cam c = load_cam(A.w2c, A.K);
+    float px = m[0], py = m[1], pz = m[2];
+    float sx = s[0], sy = s[1], sz = s[2];
+    float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+    float3 pc = to_camera(c, px, py, pz);
+    float3 cov = image_cov(c, A.width, A.height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
+    const float *gp = A.g_points + (size_t)i * A.gp_stride;
+    const float *gsp = A.g_splat + (size_t)i * A.gs_stride;
+    float gm[3], gsc[3], gq[4];
+    project_backward_one(c, A.width, A.height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
+                         cov, gsp[0], gsp[1], gsp[2], gm, gsc, gq);
+    opac_grad = gsp[3];
+
+    ViewDir d = view_dir(__ldg(A.campos), __ldg(A.campos + 1), __ldg(A.campos + 2), px, py, pz);
+    float b[16];
+    sh_basis(d.x, d.y, d.z, b);
+    float g[3];
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      float raw = b[0] * dcc[ch];
+#pragma unroll
+      for (int k = 0; k < 15; ++k) raw += b[k + 1] * r[k * 3 + ch];
+      float gc = gsp[4 + ch];
+      if (A.sh_sigmoid) {
+        float col = ref_sigmoid(raw);
+        gc *= col * (1.0f - col);
+      } else {
+        gc = (raw + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
+      }
+      g[ch] = gc;
+    }
+    float3 gmsh = sh_dir_backward(d, g[0], g[1], g[2], [&](int k, int ch) { return r[k * 3 + ch]; });
+#pragma unroll
+    for (int k = 0; k < 15; ++k)
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = g[ch] * b[k + 1];
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) dcc[ch] = g[ch] * b[0];
+    m[0] = gm[0] + gmsh.x;
+    m[1] = gm[1] + gmsh.y;
+    m[2] = gm[2] + gmsh.z;
+    s[0] = gsc[0];
+    s[1] = gsc[1];
+    s[2] = gsc[2];
+    qq[0] = gq[0];
+    qq[1] = gq[1];
+    qq[2] = gq[2];
+    qq[3] = gq[3];
+  } else {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) m[k] = s[k] = dcc[k] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) qq[k] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 45; ++k) r[k] = 0.f;
+  }
+  if (A.g_opac) A.g_opac[i] = opac_grad;
+}
+
+// Fused backward, one chunk per block (tail / unaligned fallback).
+__global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdArgs A, int n, int base) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
+  const int first = base + blockIdx.x * kPreBlock;
+  const int cnt = min(kPreBlock, n - first);
+  const size_t f = (size_t)first;
+  stage(S.means, A.means + 3 * f, 3 * cnt);
+  stage(S.scales, A.scales + 3 * f, 3 * cnt);
+  stage(S.quats, A.quats + 4 * f, 4 * cnt);
+  stage(S.dc, A.dc + 3 * f, 3 * cnt);
+  stage(S.rest, A.rest + 45 * f, 45 * cnt);
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < cnt) pre_bwd_one(A, S, t, first + t);
+  __syncthreads();
+  stage_out(A.g_means + 3 * f, S.means, 3 * cnt);
+  stage_out(A.g_scales + 3 * f, S.scales, 3 * cnt);
+  stage_out(A.g_quats + 4 * f, S.quats, 4 * cnt);
+  stage_out(A.g_dc + 3 * f, S.dc, 3 * cnt);
+  stage_out(A.g_rest + 45 * f, S.rest, 45 * cnt);
+}
+
+// Fused backward, persistent and double-buffered like the forward; the
+// gradients leave shared memory through bulk stores. Before a stage is
+// refilled its stores must have read their source (bulk wait_group.read).
+__global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(PreBwdArgs A,
+                                                                            int num_chunks,
+                                                                            uint32_t *status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
+  __shared__ __align__(8) uint64_t bars[2];
+  const int t = threadIdx.x;
+  if (t == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int c = blockIdx.x;
+  if (t == 0 && c < num_chunks)
+    issue_chunk(stg[0], &bars[0], (size_t)c * kPreBlock, A.means, A.scales, A.quats, nullptr, A.dc,
+                A.rest);
+  uint32_t phase = 0;
+  int s = 0;
+  for (; c < num_chunks; c += gridDim.x) {
+    const int nc = c + gridDim.x;
+    if (t == 0 && nc < num_chunks) {
+      bulk_wait_read_all();  // stg[s ^ 1]'s stores from the previous chunk have read it
+      issue_chunk(stg[s ^ 1], &bars[s ^ 1], (size_t)nc * kPreBlock, A.means, A.scales, A.quats,
+                  nullptr, A.dc, A.rest);
+    }
+    if (!__syncthreads_and(mbar_wait(&bars[s], (phase >> s) & 1u))) {
+      if (t == 0) {
+        atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
+        mbar_wait(&bars[s], (phase >> s) & 1u);
+        if (nc < num_chunks) mbar_wait(&bars[s ^ 1], (phase >> (s ^ 1)) & 1u);
+        bulk_wait_all();
+      }
+      return;
+    }
+    phase ^= 1u << s;
+    const int i0 = c * kPreBlock;
+    pre_bwd_one(A, stg[s], t, i0 + t);
+    fence_proxy_async_smem();  // this thread's shared writes are visible to the bulk stores
+    __syncthreads();
+    if (t == 0) {
+      const size_t f = (size_t)i0;
+      PreSmem &S = stg[s];
+      bulk_store(A.g_means + 3 * f, S.means, kPreBlock * 12);
+      bulk_store(A.g_scales + 3 * f, S.scales, kPreBlock * 12);
+      bulk_store(A.g_quats + 4 * f, S.quats, kPreBlock * 16);
+      bulk_store(A.g_dc + 3 * f, S.dc, kPreBlock * 12);
+      bulk_store(A.g_rest + 45 * f, S.rest, kPreBlock * 180);
+      bulk_commit();
+    }
+    s ^= 1;
+  }
+  if (t == 0) bulk_wait_all();
+}
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+static int pipe_grid(int num_chunks, const void *kernel, size_t smem) {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int per_sm = 0;
+  if (dev >= 0 && dev < 64 && cached[dev]) {
+    per_sm = cached[dev];
+  } else {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kPreBlock, smem);
+    if (per_sm < 1) per_sm = 1;
+    if (dev >= 0 && dev < 64) cached[dev] = per_sm;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int g = sms * per_sm;
+  return num_chunks < g ? num_chunks : g;
 }
 
 }  // namespace gs
@@ -456,14 +612,34 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
   int rc = cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
   if (rc || n == 0) return rc;
   if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
-  const int blocks = (n + kPreBlock - 1) / kPreBlock;
-  preprocess_forward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(
-      n, means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
-      camera_pos, near_plane, far_plane, min_opacity, min_radius, max_radius, width, height,
-      sh_sigmoid, reinterpret_cast<float2 *>(points_img), depths,
-      reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat), tile_counts,
-      reinterpret_cast<unsigned long long *>(total_dev));
-  count_launch();
+  PreFwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
+               camera_pos, near_plane, far_plane, min_opacity, min_radius, max_radius, width,
+               height, sh_sigmoid, reinterpret_cast<float2 *>(points_img), depths,
+               reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat),
+               tile_counts, reinterpret_cast<unsigned long long *>(total_dev)};
+  const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
+                       aligned16(opacities) && aligned16(sh_dc) && aligned16(sh_rest);
+  const int full = pipe_ok ? n / kPreBlock : 0;
+  if (full > 0) {
+    const size_t smem = 2 * sizeof(PreSmem);
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(preprocess_forward_pipe_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[dev] = 1;
+    }
+    const int grid = pipe_grid(full, (const void *)preprocess_forward_pipe_kernel, smem);
+    preprocess_forward_pipe_kernel<<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
+    count_launch();
+  }
+  const int base = full * kPreBlock;
+  if (base < n) {
+    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
+    preprocess_forward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(A, n, base);
+    count_launch();
+  }
   return launch_status();
 }
 
@@ -480,12 +656,35 @@ extern "C" int gs_preprocess_backward(int n, const float *means, const float *sc
   if (n < 0 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
     return GS_ERR_INVALID_ARGUMENT;
   if (n == 0) return GS_OK;
-  const size_t smem = sizeof(PreSmem);  // 30 KB: below the 48 KB default, no opt-in
-  int blocks = (n + kPreBlock - 1) / kPreBlock;
-  preprocess_backward_kernel<<<blocks, kPreBlock, smem, as_stream(stream)>>>(
-      n, means, scales, quats, sh_dc, sh_rest, world_to_camera, intrinsic, camera_pos, width,
-      height, sh_sigmoid, mask, grad_points_img, gp_stride, grad_splat, gs_stride, grad_means,
-      grad_scales, grad_quats, grad_opacities, grad_dc, grad_rest);
-  count_launch();
+  cudaStream_t st = as_stream(stream);
+  PreBwdArgs A{means, scales, quats, sh_dc, sh_rest, world_to_camera, intrinsic, camera_pos,
+               width, height, sh_sigmoid, mask, grad_points_img, gp_stride, grad_splat,
+               gs_stride, grad_means, grad_scales, grad_quats, grad_opacities, grad_dc,
+               grad_rest};
+  const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
+                       aligned16(sh_dc) && aligned16(sh_rest) && aligned16(grad_means) &&
+                       aligned16(grad_scales) && aligned16(grad_quats) && aligned16(grad_dc) &&
+                       aligned16(grad_rest);
+  const int full = pipe_ok ? n / kPreBlock : 0;
+  if (full > 0) {
+    const size_t smem = 2 * sizeof(PreSmem);
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(preprocess_backward_pipe_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[dev] = 1;
+    }
+    const int grid = pipe_grid(full, (const void *)preprocess_backward_pipe_kernel, smem);
+    preprocess_backward_pipe_kernel<<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
+    count_launch();
+  }
+  const int base = full * kPreBlock;
+  if (base < n) {
+    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
+    preprocess_backward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(A, n, base);
+    count_launch();
+  }
   return launch_status();
 }

@@ -34,6 +34,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 gs = importlib.import_module("3dgs_from_scratch_b200")
 nat = importlib.import_module("3dgs_from_scratch_b200._native")
+dp = importlib.import_module("3dgs_from_scratch_b200.dp")
 scenes = gs.scenes
 
 METRIC = "fwd+bwd ms/view (1M SH3 Gauss, 1080p); train views/s at 1/2/4/8 B200"
@@ -74,46 +75,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and throttle-reason sampling (NVML, every 10 ms) during the
+    timed region, in a background thread."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
+        self.samples = []
+        self._stop = None
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            self._stop = None
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+                self._stop.wait(0.01)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(2)
         return False
 
     def summary(self):
-        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
-        if not rows:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows]
-        smax = float(rows[0][2])
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": reasons,
-                "samples": len(rows)}
+        reasons = sorted({name for _, rs in self.samples for name, bit in self.REASONS.items()
+                          if rs & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
 
 
 class StageTimer:
@@ -265,7 +278,8 @@ def workload_config(args, cfg, views_per_rank):
                         f"step, orbit r={cfg.camera_distance}, L1 vs uniform target, Adam step",
             "global_batch": views_per_rank * max(args.gpus, 1), "views_per_rank": views_per_rank,
             "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
-            "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)"}
+            "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
+            "optimizer": "Adam, six groups in one flat buffer, one native launch"}
 
 
 # ---------------------------------------------------------------------------
@@ -278,22 +292,11 @@ class Trainer:
         self.world = world
         self.device = device
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
-        self.names = list(raw)
-        numel = sum(v.numel() for v in raw.values())
-        self.flat_grad = torch.zeros(numel, device=device)
-        self.params = {}
-        off = 0
-        for k, v in raw.items():
-            p = v.clone().requires_grad_(True)
-            p.grad = self.flat_grad[off:off + v.numel()].view_as(v)
-            off += v.numel()
-            self.params[k] = p
-        lrs = {"means": 1.6e-4, "scales": 5e-3, "quaternions": 1e-3, "opacities": 5e-2,
-               "sh_coeffs_dc": 2.5e-3, "sh_coeffs_rest": 2.5e-3 / 20}
-        self.opt = torch.optim.Adam([{"params": [self.params[k]], "lr": lrs[k]} for k in self.names],
-                                    eps=1e-15, betas=(0.9, 0.999), fused=True)
+        self.fp = dp.FlatParams(raw)  # replicas: identical on every rank
+        self.params = self.fp.params
         cams = scenes.orbit_cameras(cfg, views * world)
-        self.cams = cams[rank * views:(rank + 1) * views].to(device)
+        mine = dp.shard_views(views * world, rank, world)
+        self.cams = cams[mine].to(device)
         self.K = scenes.intrinsic_for(cfg).to(device)
         g = torch.Generator(device=device).manual_seed(1234 + rank)
         self.targets = [torch.rand((cfg.height, cfg.width, 3), device=device, generator=g) * 255.0
@@ -306,8 +309,7 @@ class Trainer:
         self.host_loss = torch.zeros(len(self.targets), dtype=torch.float32).pin_memory()
 
     def step(self, e2e=False):
-        p = self.params
-        act = scenes.activate(p)
+        act = scenes.activate(self.params)
         losses = []
         for v in range(len(self.targets)):
             if e2e:
@@ -323,14 +325,10 @@ class Trainer:
         # one backward per step: the views' gradients meet at the activated
         # parameters, so the activation backward runs once
         torch.stack(losses).sum().backward()
-        losses = [x.detach() for x in losses]
-        if self.world > 1:
-            import torch.distributed as dist
-
-            dist.all_reduce(self.flat_grad)
-        self.opt.step()
-        self.flat_grad.zero_()
-        total = torch.stack(losses)
+        self.fp.allreduce_grads()
+        self.fp.adam_step()
+        self.fp.zero_grad()
+        total = torch.stack([x.detach() for x in losses])
         if e2e:
             self.host_loss.copy_(total, non_blocking=True)
         return total

@@ -233,6 +233,19 @@ GS_API int gs_preprocess_backward(int n, const float *means, const float *scales
                            float *grad_scales, float *grad_quats, float *grad_opacities,
                            float *grad_dc, float *grad_rest, void *stream);
 
+/* ---- training step helpers -------------------------------------------------
+ * One-launch Adam over a flat fp32 buffer holding consecutive parameter
+ * groups (group k = elements [group_ends[k-1], group_ends[k]), host arrays of
+ * num_groups <= 8 entries, each end a multiple of 4, the last equal to n).
+ * Same update as torch.optim.Adam (no amsgrad, no weight decay) with the
+ * per-group learning rates and eps of scripts/train.py:17-44; `step` is the
+ * 1-based step count used for bias correction. All four buffers 16-byte
+ * aligned. */
+GS_API int gs_adam_step(int64_t n, float *params, const float *grads, float *exp_avg,
+                        float *exp_avg_sq, int num_groups, const int64_t *group_ends,
+                        const float *lrs, const float *eps, float beta1, float beta2,
+                        int64_t step, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
