@@ -49,6 +49,12 @@ LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
 BLEND_FWD_FLOP_PER_PAIR = 22
 BLEND_BWD_FLOP_PER_PAIR = 60
 
+# DRAM bytes (read + write) per launch at config 1, from the ncu --set full
+# capture summarised in profiles/kernels_cfg1_full.md (dram__bytes_read.sum +
+# dram__bytes_write.sum).
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 274.4e6, "preprocess_bwd": 459.5e6,
+                     "blend_fwd": 58.3e6, "blend_bwd": 110.0e6}
+
 
 def parse():
     p = argparse.ArgumentParser()
@@ -456,7 +462,10 @@ def main():
     if dom:
         r = roof[dom]
         roofline = {"kernel": dom, "bound": r["bound"], "achieved": r["achieved"],
-                    "peak": r["peak"], "unit": r["unit"], "frac": r["frac"], "traffic": None,
+                    "peak": r["peak"], "unit": r["unit"], "frac": r["frac"],
+                    "traffic": NCU_TRAFFIC_BYTES.get(dom) if args.config == 1 and args.n is None
+                    else None,
+                    "traffic_unit": "bytes/launch (ncu, profiles/kernels_cfg1_full.md)",
                     "peak_source": (f"{src} MEASURED_PEAKS.json hbm_gbs" if r["bound"] == "hbm"
                                     else "nominal FP32: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
                                          " (MEASURED_PEAKS.json has no FP32 figure)"),
