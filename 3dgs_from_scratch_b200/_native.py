@@ -55,13 +55,14 @@ SIGNATURES = {
     "gs_rasterize": (I, [I, P, I64, P, I, P, P, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_rasterize_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P, P, P,
                                   P, P]),
-    "gs_preprocess_forward": (I, [I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I, P, P, P,
-                                  P, P, P, P, P]),
+    "gs_preprocess_forward": (I, [I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I, I, P, P,
+                                  P, P, P, P, P, P]),
     "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P]),
+    "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
-    "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, I, I, I, P, P, I, P, I, P, P, P, P,
-                                   P, P, P]),
+    "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P, I, P, I, P,
+                                   P, P, P, P, P, P]),
 }
 
 _lib = None

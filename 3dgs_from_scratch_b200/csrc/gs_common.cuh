@@ -115,6 +115,15 @@ __device__ __forceinline__ void bulk_store(void *gdst, const void *smem_src, uin
                "r"(smem_addr(smem_src)), "r"(bytes)
                : "memory");
 }
+// Shared -> global bulk reduction: global[i] += shared[i] (fp32), tracked by
+// bulk groups like bulk_store.
+__device__ __forceinline__ void bulk_reduce_add(float *gdst, const float *smem_src,
+                                                uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
+                   gdst),
+               "r"(smem_addr(smem_src)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the committed bulk stores have read their shared-memory source.
 __device__ __forceinline__ void bulk_wait_read_all() {
@@ -398,6 +407,30 @@ __device__ __forceinline__ void project_backward_one(
   gm[0] = gm0 + (W[0] * gx + W[4] * gy + W[8] * gz);
   gm[1] = gm1 + (W[1] * gx + W[5] * gy + W[9] * gz);
   gm[2] = gm2 + (W[2] * gx + W[6] * gy + W[10] * gz);
+}
+
+// ---- parameter activations (scripts/train.py:135-140 of the reference) --------
+
+// exp(log-scale), q / max(|q|, 1e-12), sigmoid(logit): the activations the
+// reference applies in Torch before render().
+struct Activated {
+  float sx, sy, sz, qx, qy, qz, qw, opac, qnorm;
+};
+
+__device__ __forceinline__ Activated activate_params(float lsx, float lsy, float lsz, float qx,
+                                                     float qy, float qz, float qw, float logit) {
+  Activated a;
+  a.sx = expf(lsx);
+  a.sy = expf(lsy);
+  a.sz = expf(lsz);
+  a.qnorm = sqrtf(qx * qx + qy * qy + qz * qz + qw * qw);
+  const float nq = fmaxf(a.qnorm, 1e-12f);
+  a.qx = qx / nq;
+  a.qy = qy / nq;
+  a.qz = qz / nq;
+  a.qw = qw / nq;
+  a.opac = 1.0f / (1.0f + expf(-logit));
+  return a;
 }
 
 // ---- spherical harmonics ----------------------------------------------------

@@ -189,10 +189,16 @@ __device__ __forceinline__ void stage_out(float *__restrict__ dst, const float *
   }
 }
 
+__device__ __forceinline__ void stage_add(float *__restrict__ dst, const float *__restrict__ src,
+                                          int count) {
+  for (int k = threadIdx.x; k < count; k += blockDim.x) dst[k] += src[k];
+}
+
 struct PreFwdArgs {
   const float *means, *scales, *quats, *opac, *dc, *rest, *w2c, *K, *campos;
   float near_plane, far_plane, min_opacity, min_radius, max_radius;
   int width, height, sh_sigmoid;
+  int activate;  // parameters are raw (log-scales, unnormalised quats, logits)
   float2 *points;
   float *depths;
   float2 *radii;
@@ -208,9 +214,16 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
   const float *m = S.means + 3 * t;
   const float *s = S.scales + 3 * t;
   const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+  float sx = s[0], sy = s[1], sz = s[2], qx = q.x, qy = q.y, qz = q.z, qw = q.w, op = S.opac[t];
+  if (A.activate) {
+    const Activated a = activate_params(sx, sy, sz, qx, qy, qz, qw, op);
+    sx = a.sx; sy = a.sy; sz = a.sz;
+    qx = a.qx; qy = a.qy; qz = a.qz; qw = a.qw;
+    op = a.opac;
+  }
   Projected p = project_one(c, A.width, A.height, A.near_plane, A.far_plane, A.min_opacity,
-                            A.min_radius, A.max_radius, m[0], m[1], m[2], s[0], s[1], s[2], q.x,
-                            q.y, q.z, q.w, S.opac[t]);
+                            A.min_radius, A.max_radius, m[0], m[1], m[2], sx, sy, sz, qx, qy, qz,
+                            qw, op);
   float2 pt = make_float2(0.f, 0.f), rd = make_float2(0.f, 0.f);
   float depth = 0.f;
   float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -237,7 +250,7 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
     pt = make_float2(p.u, p.v);
     rd = make_float2(p.ru, p.rv);
     depth = p.depth;
-    s0 = make_float4(p.conic.x, p.conic.y, p.conic.z, S.opac[t]);
+    s0 = make_float4(p.conic.x, p.conic.y, p.conic.z, op);
     s1 = make_float4(rgb[0], rgb[1], rgb[2], 0.f);
     TileRect tr = tile_rect(p.u, p.v, p.ru, p.rv, A.width, A.height);
     count = tr.empty ? 0 : (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
@@ -343,8 +356,10 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
 }
 
 struct PreBwdArgs {
-  const float *means, *scales, *quats, *dc, *rest, *w2c, *K, *campos;
+  const float *means, *scales, *quats, *opac, *dc, *rest, *w2c, *K, *campos;
   int width, height, sh_sigmoid;
+  int activate;    // parameters are raw; gradients are w.r.t. the raw parameters
+  int accumulate;  // add the gradients into the outputs instead of writing them
   const uint8_t *mask;
   const float *g_points;
   int gp_stride;
@@ -367,6 +382,14 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int
     float px = m[0], py = m[1], pz = m[2];
     float sx = s[0], sy = s[1], sz = s[2];
     float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+    Activated act;
+    if (A.activate) {
+      act = activate_params(sx, sy, sz, q.x, q.y, q.z, q.w, S.opac[t]);
+      sx = act.sx;
+      sy = act.sy;
+      sz = act.sz;
+      q = make_float4(act.qx, act.qy, act.qz, act.qw);
+    }
     float3 pc = to_camera(c, px, py, pz);
     float3 cov = image_cov(c, A.width, A.height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
     const float *gp = A.g_points + (size_t)i * A.gp_stride;
@@ -374,7 +397,27 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int
     float gm[3], gsc[3], gq[4];
     project_backward_one(c, A.width, A.height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
                          cov, gsp[0], gsp[1], gsp[2], gm, gsc, gq);
+    if (A.activate) {
+      // exp backward (scale), normalisation backward (quaternion)
+      gsc[0] *= act.sx;
+      gsc[1] *= act.sy;
+      gsc[2] *= act.sz;
+      const float nq = fmaxf(act.qnorm, 1e-12f);
+      if (act.qnorm >= 1e-12f) {
+        const float dot = q.x * gq[0] + q.y * gq[1] + q.z * gq[2] + q.w * gq[3];
+        gq[0] = (gq[0] - q.x * dot) / nq;
+        gq[1] = (gq[1] - q.y * dot) / nq;
+        gq[2] = (gq[2] - q.z * dot) / nq;
+        gq[3] = (gq[3] - q.w * dot) / nq;
+      } else {
+        gq[0] /= nq;
+        gq[1] /= nq;
+        gq[2] /= nq;
+        gq[3] /= nq;
+      }
+    }
     opac_grad = gsp[3];
+    if (A.activate) opac_grad = opac_grad * (1.0f - act.opac) * act.opac;  // sigmoid backward
 
     ViewDir d = view_dir(__ldg(A.campos), __ldg(A.campos + 1), __ldg(A.campos + 2), px, py, pz);
     float b[16];
@@ -419,7 +462,12 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int
 #pragma unroll
     for (int k = 0; k < 45; ++k) r[k] = 0.f;
   }
-  if (A.g_opac) A.g_opac[i] = opac_grad;
+  if (A.g_opac) {
+    if (A.accumulate)
+      A.g_opac[i] += opac_grad;
+    else
+      A.g_opac[i] = opac_grad;
+  }
 }
 
 // Fused backward, one chunk per block (tail / unaligned fallback).
@@ -432,17 +480,26 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdAr
   stage(S.means, A.means + 3 * f, 3 * cnt);
   stage(S.scales, A.scales + 3 * f, 3 * cnt);
   stage(S.quats, A.quats + 4 * f, 4 * cnt);
+  if (A.activate) stage(S.opac, A.opac + f, cnt);
   stage(S.dc, A.dc + 3 * f, 3 * cnt);
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
   const int t = threadIdx.x;
   if (t < cnt) pre_bwd_one(A, S, t, first + t);
   __syncthreads();
-  stage_out(A.g_means + 3 * f, S.means, 3 * cnt);
-  stage_out(A.g_scales + 3 * f, S.scales, 3 * cnt);
-  stage_out(A.g_quats + 4 * f, S.quats, 4 * cnt);
-  stage_out(A.g_dc + 3 * f, S.dc, 3 * cnt);
-  stage_out(A.g_rest + 45 * f, S.rest, 45 * cnt);
+  if (A.accumulate) {
+    stage_add(A.g_means + 3 * f, S.means, 3 * cnt);
+    stage_add(A.g_scales + 3 * f, S.scales, 3 * cnt);
+    stage_add(A.g_quats + 4 * f, S.quats, 4 * cnt);
+    stage_add(A.g_dc + 3 * f, S.dc, 3 * cnt);
+    stage_add(A.g_rest + 45 * f, S.rest, 45 * cnt);
+  } else {
+    stage_out(A.g_means + 3 * f, S.means, 3 * cnt);
+    stage_out(A.g_scales + 3 * f, S.scales, 3 * cnt);
+    stage_out(A.g_quats + 4 * f, S.quats, 4 * cnt);
+    stage_out(A.g_dc + 3 * f, S.dc, 3 * cnt);
+    stage_out(A.g_rest + 45 * f, S.rest, 45 * cnt);
+  }
 }
 
 // Fused backward, persistent and double-buffered like the forward; the
@@ -463,8 +520,8 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
   __syncthreads();
   int c = blockIdx.x;
   if (t == 0 && c < num_chunks)
-    issue_chunk(stg[0], &bars[0], (size_t)c * kPreBlock, A.means, A.scales, A.quats, nullptr, A.dc,
-                A.rest);
+    issue_chunk(stg[0], &bars[0], (size_t)c * kPreBlock, A.means, A.scales, A.quats,
+                A.activate ? A.opac : nullptr, A.dc, A.rest);
   uint32_t phase = 0;
   int s = 0;
   for (; c < num_chunks; c += gridDim.x) {
@@ -472,7 +529,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
     if (t == 0 && nc < num_chunks) {
       bulk_wait_read_all();  // stg[s ^ 1]'s stores from the previous chunk have read it
       issue_chunk(stg[s ^ 1], &bars[s ^ 1], (size_t)nc * kPreBlock, A.means, A.scales, A.quats,
-                  nullptr, A.dc, A.rest);
+                  A.activate ? A.opac : nullptr, A.dc, A.rest);
     }
     if (!__syncthreads_and(mbar_wait(&bars[s], (phase >> s) & 1u))) {
       if (t == 0) {
@@ -491,11 +548,19 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
     if (t == 0) {
       const size_t f = (size_t)i0;
       PreSmem &S = stg[s];
-      bulk_store(A.g_means + 3 * f, S.means, kPreBlock * 12);
-      bulk_store(A.g_scales + 3 * f, S.scales, kPreBlock * 12);
-      bulk_store(A.g_quats + 4 * f, S.quats, kPreBlock * 16);
-      bulk_store(A.g_dc + 3 * f, S.dc, kPreBlock * 12);
-      bulk_store(A.g_rest + 45 * f, S.rest, kPreBlock * 180);
+      if (A.accumulate) {  // global += shared, performed by the TMA engine in L2
+        bulk_reduce_add(A.g_means + 3 * f, S.means, kPreBlock * 12);
+        bulk_reduce_add(A.g_scales + 3 * f, S.scales, kPreBlock * 12);
+        bulk_reduce_add(A.g_quats + 4 * f, S.quats, kPreBlock * 16);
+        bulk_reduce_add(A.g_dc + 3 * f, S.dc, kPreBlock * 12);
+        bulk_reduce_add(A.g_rest + 45 * f, S.rest, kPreBlock * 180);
+      } else {
+        bulk_store(A.g_means + 3 * f, S.means, kPreBlock * 12);
+        bulk_store(A.g_scales + 3 * f, S.scales, kPreBlock * 12);
+        bulk_store(A.g_quats + 4 * f, S.quats, kPreBlock * 16);
+        bulk_store(A.g_dc + 3 * f, S.dc, kPreBlock * 12);
+        bulk_store(A.g_rest + 45 * f, S.rest, kPreBlock * 180);
+      }
       bulk_commit();
     }
     s ^= 1;
@@ -601,9 +666,9 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
                                      const float *camera_pos, float near_plane,
                                      float far_plane, float min_opacity, float min_radius,
                                      float max_radius, int width, int height, int sh_sigmoid,
-                                     float *points_img, float *depths, float *radii,
-                                     uint8_t *mask, float *splat, int32_t *tile_counts,
-                                     int64_t *total_dev, void *stream) {
+                                     int activate, float *points_img, float *depths,
+                                     float *radii, uint8_t *mask, float *splat,
+                                     int32_t *tile_counts, int64_t *total_dev, void *stream) {
   if (n < 0 || width <= 0 || height <= 0 || total_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)splat & 15) ||
       ((uintptr_t)total_dev & 7))
@@ -614,7 +679,7 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
   if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
   PreFwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
                camera_pos, near_plane, far_plane, min_opacity, min_radius, max_radius, width,
-               height, sh_sigmoid, reinterpret_cast<float2 *>(points_img), depths,
+               height, sh_sigmoid, activate, reinterpret_cast<float2 *>(points_img), depths,
                reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat),
                tile_counts, reinterpret_cast<unsigned long long *>(total_dev)};
   const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
@@ -644,10 +709,11 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
 }
 
 extern "C" int gs_preprocess_backward(int n, const float *means, const float *scales,
-                                      const float *quats, const float *sh_dc,
-                                      const float *sh_rest, const float *world_to_camera,
-                                      const float *intrinsic, const float *camera_pos,
-                                      int width, int height, int sh_sigmoid,
+                                      const float *quats, const float *opacities,
+                                      const float *sh_dc, const float *sh_rest,
+                                      const float *world_to_camera, const float *intrinsic,
+                                      const float *camera_pos, int width, int height,
+                                      int sh_sigmoid, int activate, int accumulate,
                                       const uint8_t *mask, const float *grad_points_img,
                                       int gp_stride, const float *grad_splat, int gs_stride,
                                       float *grad_means, float *grad_scales, float *grad_quats,
@@ -655,13 +721,15 @@ extern "C" int gs_preprocess_backward(int n, const float *means, const float *sc
                                       void *stream) {
   if (n < 0 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
     return GS_ERR_INVALID_ARGUMENT;
+  if (activate && opacities == nullptr) return GS_ERR_INVALID_ARGUMENT;
   if (n == 0) return GS_OK;
   cudaStream_t st = as_stream(stream);
-  PreBwdArgs A{means, scales, quats, sh_dc, sh_rest, world_to_camera, intrinsic, camera_pos,
-               width, height, sh_sigmoid, mask, grad_points_img, gp_stride, grad_splat,
-               gs_stride, grad_means, grad_scales, grad_quats, grad_opacities, grad_dc,
-               grad_rest};
+  PreBwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
+               camera_pos, width, height, sh_sigmoid, activate, accumulate, mask,
+               grad_points_img, gp_stride, grad_splat, gs_stride, grad_means, grad_scales,
+               grad_quats, grad_opacities, grad_dc, grad_rest};
   const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
+                       (!activate || aligned16(opacities)) &&
                        aligned16(sh_dc) && aligned16(sh_rest) && aligned16(grad_means) &&
                        aligned16(grad_scales) && aligned16(grad_quats) && aligned16(grad_dc) &&
                        aligned16(grad_rest);

@@ -1,0 +1,173 @@
+"""Native data-parallel training step.
+
+The reference's training step (scripts/train.py:133-222) is, per view:
+activations in Torch (exp scales, normalised quaternions, sigmoid
+opacities), render(), L1 loss against the target image, backward through
+the rasterizer and the activations, Adam on the six parameter groups. This
+module runs the same step entirely in this library's kernels, for a batch of
+views sharded across ranks:
+
+* activations fused into the preprocess kernels (their Jacobians in the
+  preprocess backward), so gradients come out w.r.t. the raw parameters;
+* every view's preprocess is queued before one host synchronisation that
+  reads all the views' pair counts (the reference synchronises once per
+  view, rasterizer.cpp:322);
+* the clamp*255 of render() and the L1 loss with its gradient in one kernel;
+* each view's raw-parameter gradients added straight into the flat gradient
+  buffer by the preprocess backward (TMA bulk reduce-add), so neither
+  autograd nor a per-view gradient copy is involved;
+* one NCCL all-reduce of the flat gradient (world > 1) and the one-launch
+  Adam of dp.FlatParams.
+
+The renders are the same as render()'s (same kernels); tests compare one step
+of this trainer with the autograd path (render() + Torch activations +
+torch.nn.functional.l1_loss).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from . import cuda_rasterizer
+from .dp import GROUPS, FlatParams
+
+RENDER_DEFAULTS = dict(near_plane=0.01, far_plane=100.0, min_opacity=1 / 255, min_radius=0.5,
+                       max_radius=128.0, alpha_threshold=1e-4, transmittance_threshold=1e-4,
+                       chi_squared_threshold=9.21)
+
+
+class NativeTrainer:
+    """Gaussians as raw parameters (means, log-scales, raw quaternions,
+    opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
+
+    def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
+                 **render_opts):
+        self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs)
+        self.device = self.fp.device
+        if self.device.type != "cuda":
+            raise RuntimeError("NativeTrainer needs the parameters on a CUDA device")
+        self.width, self.height = int(width), int(height)
+        self.opts = dict(RENDER_DEFAULTS)
+        self.opts.update(render_opts)
+        self.n = self.fp.shapes["means"][0]
+        self.tx = (self.width + 15) // 16
+        self.ty = (self.height + 15) // 16
+
+    @property
+    def params(self):
+        return self.fp.params
+
+    def _ptr(self, name):
+        return self.fp.params[name].data_ptr()
+
+    def _gptr(self, name):
+        a, _ = self.fp.spans[name]
+        return self.fp.grad.data_ptr() + 4 * a
+
+    def forward_views(self, world_to_cameras, intrinsics):
+        """Render the views (forward only). Returns the per-view state list;
+        state["image"] is the raw blended image (H, W, 3) before clamp * 255."""
+        o = self.opts
+        dev = self.device
+        st = nat.stream_ptr(dev)
+        n, W, H = self.n, self.width, self.height
+        w2c = world_to_cameras.to(dev, torch.float32).contiguous()
+        Ks = intrinsics.to(dev, torch.float32)
+        if Ks.dim() == 2:
+            Ks = Ks.unsqueeze(0).expand(w2c.shape[0], 3, 3)
+        Ks = Ks.contiguous()
+        V = w2c.shape[0]
+        campos = (-(w2c[:, :3, :3].transpose(1, 2) @ w2c[:, :3, 3:4])).squeeze(-1).contiguous()
+        totals = torch.empty(V, dtype=torch.int64, device=dev)
+        f = dict(device=dev, dtype=torch.float32)
+        views = []
+        for v in range(V):
+            s = dict(points=torch.empty((n, 2), **f), depths=torch.empty((n,), **f),
+                     radii=torch.empty((n, 2), **f),
+                     mask=torch.empty((n,), device=dev, dtype=torch.uint8),
+                     splat=torch.empty((n, 8), **f),
+                     counts=torch.empty((max(n, 1),), device=dev, dtype=torch.int32),
+                     w2c=w2c[v], K=Ks[v], campos=campos[v])
+            nat.call("gs_preprocess_forward", n, self._ptr("means"), self._ptr("scales"),
+                     self._ptr("quaternions"), self._ptr("opacities"), self._ptr("sh_coeffs_dc"),
+                     self._ptr("sh_coeffs_rest"), s["w2c"].data_ptr(), s["K"].data_ptr(),
+                     s["campos"].data_ptr(), o["near_plane"], o["far_plane"], o["min_opacity"],
+                     o["min_radius"], o["max_radius"], W, H, 0, 1, s["points"].data_ptr(),
+                     s["depths"].data_ptr(), s["radii"].data_ptr(), s["mask"].data_ptr(),
+                     s["splat"].data_ptr(), s["counts"].data_ptr(), totals[v:].data_ptr(), st)
+            views.append(s)
+        # one host synchronisation for every view's pair count
+        host_totals = totals.cpu()
+        rc = nat.query("gs_check_status", st)
+        if rc:
+            raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+        for v, s in enumerate(views):
+            total = int(host_totals[v])
+            s["total"] = total
+            s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
+                s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
+            s["image"] = torch.empty((H, W, 3), **f)
+            s["final_t"] = torch.empty((H * W,), **f)
+            s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
+            nat.call("gs_blend_forward", s["offsets"].shape[0], s["offsets"].data_ptr(), total,
+                     s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(), W, H,
+                     o["alpha_threshold"], o["transmittance_threshold"],
+                     o["chi_squared_threshold"], s["image"].data_ptr(), s["final_t"].data_ptr(),
+                     s["pixel_end"].data_ptr(), st)
+        return views
+
+    def loss_and_backward(self, views, targets, accumulate=False):
+        """L1 loss of every view against its target (H, W, 3; float in
+        [0, 255] or uint8) and the backward into the flat gradient buffer.
+        The first view's gradients overwrite the buffer (every element is
+        written, zeros for Gaussians it culled) unless `accumulate`; later
+        views add to it. Returns the per-view losses (device tensor)."""
+        o = self.opts
+        dev = self.device
+        st = nat.stream_ptr(dev)
+        n, W, H = self.n, self.width, self.height
+        npx = H * W * 3
+        V = len(views)
+        loss_sums = torch.zeros(V, dtype=torch.float64, device=dev)
+        grad_img = torch.empty((H, W, 3), device=dev, dtype=torch.float32)
+        g_points = torch.empty((n, 2), device=dev, dtype=torch.float32)
+        g_splat = torch.empty((n, 8), device=dev, dtype=torch.float32)
+        for v, s in enumerate(views):
+            tgt = targets[v]
+            if tgt.device != dev or not tgt.is_contiguous():
+                tgt = tgt.to(dev).contiguous()
+            if tgt.dtype not in (torch.uint8, torch.float32):
+                tgt = tgt.float()
+            nat.call("gs_l1_loss_grad", npx, s["image"].data_ptr(), tgt.data_ptr(),
+                     int(tgt.dtype == torch.uint8), grad_img.data_ptr(), loss_sums[v:].data_ptr(),
+                     st)
+            g_points.zero_()
+            g_splat.zero_()
+            nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
+                     s["total"], s["ids"].data_ptr(), n, s["points"].data_ptr(),
+                     s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
+                     s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
+                     o["transmittance_threshold"], o["chi_squared_threshold"],
+                     g_points.data_ptr(), g_splat.data_ptr(), st)
+            nat.call("gs_preprocess_backward", n, self._ptr("means"), self._ptr("scales"),
+                     self._ptr("quaternions"), self._ptr("opacities"),
+                     self._ptr("sh_coeffs_dc"), self._ptr("sh_coeffs_rest"), s["w2c"].data_ptr(),
+                     s["K"].data_ptr(), s["campos"].data_ptr(), W, H, 0, 1,
+                     int(accumulate or v > 0),
+                     s["mask"].data_ptr(), g_points.data_ptr(), 2, g_splat.data_ptr(), 8,
+                     self._gptr("means"), self._gptr("scales"), self._gptr("quaternions"),
+                     self._gptr("opacities"), self._gptr("sh_coeffs_dc"),
+                     self._gptr("sh_coeffs_rest"), st)
+        return loss_sums / npx
+
+    def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True):
+        """One training step over this rank's views: render, L1 loss,
+        backward (the first view overwrites the flat gradient, so no zeroing
+        is needed between steps), gradient all-reduce (when a process group
+        is initialised with world > 1), Adam. Returns the losses."""
+        views = self.forward_views(world_to_cameras, intrinsics)
+        losses = self.loss_and_backward(views, targets)
+        if optimizer_step:
+            self.fp.allreduce_grads()
+            self.fp.adam_step()
+        return losses

@@ -144,7 +144,7 @@ class _Preprocess(torch.autograd.Function):
                  sh_rest.data_ptr(), world_to_camera.data_ptr(), intrinsic.data_ptr(),
                  camera_pos.data_ptr(), opts["near_plane"], opts["far_plane"],
                  opts["min_opacity"], opts["min_radius"], opts["max_radius"], opts["width"],
-                 opts["height"], int(opts["sh_sigmoid"]), points.data_ptr(), depths.data_ptr(),
+                 opts["height"], int(opts["sh_sigmoid"]), 0, points.data_ptr(), depths.data_ptr(),
                  radii.data_ptr(), mask.view(torch.uint8).data_ptr(), splat.data_ptr(),
                  counts.data_ptr(), total_dev.data_ptr(), nat.stream_ptr(dev))
         ctx.save_for_backward(means, scales, quaternions, sh_dc, sh_rest, world_to_camera,
@@ -175,9 +175,9 @@ class _Preprocess(torch.autograd.Function):
         gdc = torch.empty((n, 3), **f)
         grest = torch.empty((n, 15, 3), **f)
         nat.call("gs_preprocess_backward", n, means.data_ptr(), scales.data_ptr(),
-                 quats.data_ptr(), sh_dc.data_ptr(), sh_rest.data_ptr(), w2c.data_ptr(),
+                 quats.data_ptr(), None, sh_dc.data_ptr(), sh_rest.data_ptr(), w2c.data_ptr(),
                  K.data_ptr(), campos.data_ptr(), o["width"], o["height"], int(o["sh_sigmoid"]),
-                 mask.view(torch.uint8).data_ptr(), g_points.data_ptr(),
+                 0, 0, mask.view(torch.uint8).data_ptr(), g_points.data_ptr(),
                  g_points.stride(0) if n > 0 else 2, g_splat.data_ptr(),
                  g_splat.stride(0) if n > 0 else 8, gm.data_ptr(), gs.data_ptr(), gq.data_ptr(),
                  go.data_ptr(), gdc.data_ptr(), grest.data_ptr(), nat.stream_ptr(dev))

@@ -13,6 +13,12 @@ value = views/s over all ranks, device-timed with CUDA events, max over
 ranks. e2e = the same step through render() with each step's target images
 (uint8) and cameras copied from pinned host memory and the loss read back,
 wall-clock timed. See DESIGN.md for the roofline definitions.
+
+--trainer native (default) runs the step with trainer.NativeTrainer: the same
+math with the activations fused into the preprocess kernels, one host
+synchronisation per step, the L1 loss and its gradient in one kernel, and
+gradients accumulated straight into the flat buffer. --trainer autograd runs
+it through the public render() with Torch activations, loss and autograd.
 """
 from __future__ import annotations
 
@@ -35,6 +41,7 @@ sys.path.insert(0, HERE)
 gs = importlib.import_module("3dgs_from_scratch_b200")
 nat = importlib.import_module("3dgs_from_scratch_b200._native")
 dp = importlib.import_module("3dgs_from_scratch_b200.dp")
+trainer_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
 scenes = gs.scenes
 
 METRIC = "fwd+bwd ms/view (1M SH3 Gauss, 1080p); train views/s at 1/2/4/8 B200"
@@ -68,6 +75,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-sample-views", type=int, default=2)
+    p.add_argument("--trainer", choices=["native", "autograd"], default="native",
+                   help="native: NativeTrainer (fused activations/loss, flat-buffer gradients); "
+                        "autograd: render() + Torch activations/loss + autograd")
     return p.parse_args()
 
 
@@ -285,7 +295,8 @@ def workload_config(args, cfg, views_per_rank):
             "global_batch": views_per_rank * max(args.gpus, 1), "views_per_rank": views_per_rank,
             "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
-            "optimizer": "Adam, six groups in one flat buffer, one native launch"}
+            "optimizer": "Adam, six groups in one flat buffer, one native launch",
+            "trainer": args.trainer}
 
 
 # ---------------------------------------------------------------------------
@@ -340,6 +351,43 @@ class Trainer:
         return total
 
 
+class NativeBenchTrainer:
+    """The same step as Trainer, run by trainer.NativeTrainer."""
+
+    def __init__(self, cfg, n, views, world, rank, device):
+        self.cfg = cfg
+        self.world = world
+        self.device = device
+        raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
+        self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height)
+        self.fp = self.nt.fp
+        self.params = self.fp.params
+        cams = scenes.orbit_cameras(cfg, views * world)
+        mine = dp.shard_views(views * world, rank, world)
+        self.cams = cams[mine].to(device)
+        self.K = scenes.intrinsic_for(cfg).to(device)
+        g = torch.Generator(device=device).manual_seed(1234 + rank)
+        self.targets = [torch.rand((cfg.height, cfg.width, 3), device=device, generator=g) * 255.0
+                        for _ in range(views)]
+        self.host_targets = [(t.cpu().round().clamp(0, 255).to(torch.uint8)).pin_memory()
+                             for t in self.targets]
+        self.host_cams = self.cams.cpu().pin_memory()
+        self.host_K = self.K.cpu().pin_memory()
+        self.host_loss = torch.zeros(len(self.targets), dtype=torch.float64).pin_memory()
+
+    def step(self, e2e=False):
+        if e2e:
+            cams = self.host_cams.to(self.device, non_blocking=True)
+            K = self.host_K.to(self.device, non_blocking=True)
+            tg = [t.to(self.device, non_blocking=True) for t in self.host_targets]
+        else:
+            cams, K, tg = self.cams, self.K, self.targets
+        losses = self.nt.step(cams, K, tg)
+        if e2e:
+            self.host_loss.copy_(losses, non_blocking=True)
+        return losses
+
+
 def count_pairs(tr, view=0):
     """Evaluated (pixel, Gaussian) pairs of one view, in the reference's
     counting: list entries visited before the transmittance break."""
@@ -386,7 +434,8 @@ def main():
     device = torch.device("cuda", local)
     cfg = scenes.CONFIGS[args.config]
     V = args.views_per_rank
-    tr = Trainer(cfg, args.n, V, world, rank, device)
+    tr = (NativeBenchTrainer if args.trainer == "native" else Trainer)(cfg, args.n, V, world, rank,
+                                                                        device)
     n = tr.params["means"].shape[0]
 
     for _ in range(args.warmup):

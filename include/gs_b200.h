@@ -189,15 +189,19 @@ GS_API int gs_rasterize_backward(int num_tiles, const int32_t *indexing_offset, 
  * *total_dev (int64; zeroed by this call before the kernel). The splat record
  * is float[8] per Gaussian: conic (a, b, c), opacity, colour (r, g, b), 0.
  * Every output element is written (zeros for culled Gaussians). camera_pos is
- * the device float[3] -R^T t (wrapper.py:260). */
+ * the device float[3] -R^T t (wrapper.py:260). With activate = 1 the
+ * parameters are the raw ones of the reference's training loop (log-scales,
+ * unnormalised quaternions, opacity logits) and the kernel applies exp,
+ * q / max(|q|, 1e-12) and sigmoid itself (scripts/train.py:135-140); the
+ * splat record then holds the activated opacity. */
 GS_API int gs_preprocess_forward(int n, const float *means, const float *scales, const float *quats,
                           const float *opacities, const float *sh_dc, const float *sh_rest,
                           const float *world_to_camera, const float *intrinsic,
                           const float *camera_pos, float near_plane, float far_plane,
                           float min_opacity, float min_radius, float max_radius, int width,
-                          int height, int sh_sigmoid, float *points_img, float *depths,
-                          float *radii, uint8_t *mask, float *splat, int32_t *tile_counts,
-                          int64_t *total_dev, void *stream);
+                          int height, int sh_sigmoid, int activate, float *points_img,
+                          float *depths, float *radii, uint8_t *mask, float *splat,
+                          int32_t *tile_counts, int64_t *total_dev, void *stream);
 
 /* Blend forward over the splat records; also writes each pixel's final
  * transmittance and end index (one past its last contributing list entry).
@@ -223,11 +227,16 @@ GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int6
  * upstream gradients are read with element strides (so column views of a
  * packed buffer work): grad_points_img at gp[i*gp_stride + {0,1}], the splat
  * gradient at gs[i*gs_stride + {0..6}] (conic a,b,c, opacity, r, g, b).
- * grad_opacities receives the opacity gradient (may be NULL). */
+ * grad_opacities receives the opacity gradient (may be NULL). With activate = 1
+ * the parameters are raw (as for gs_preprocess_forward; opacities required)
+ * and the gradients are w.r.t. the raw parameters (exp, normalisation and
+ * sigmoid backward applied). With accumulate = 1 the gradients are added into
+ * the outputs (the TMA engine's bulk reduce-add in L2) instead of written. */
 GS_API int gs_preprocess_backward(int n, const float *means, const float *scales,
-                           const float *quats, const float *sh_dc, const float *sh_rest,
-                           const float *world_to_camera, const float *intrinsic,
-                           const float *camera_pos, int width, int height, int sh_sigmoid,
+                           const float *quats, const float *opacities, const float *sh_dc,
+                           const float *sh_rest, const float *world_to_camera,
+                           const float *intrinsic, const float *camera_pos, int width,
+                           int height, int sh_sigmoid, int activate, int accumulate,
                            const uint8_t *mask, const float *grad_points_img, int gp_stride,
                            const float *grad_splat, int gs_stride, float *grad_means,
                            float *grad_scales, float *grad_quats, float *grad_opacities,
@@ -245,6 +254,15 @@ GS_API int gs_adam_step(int64_t n, float *params, const float *grads, float *exp
                         float *exp_avg_sq, int num_groups, const int64_t *group_ends,
                         const float *lrs, const float *eps, float beta1, float beta2,
                         int64_t step, void *stream);
+
+/* The reference's per-view training loss on the raw blended image (H*W*3 =
+ * n floats): rendered = clamp(raw, 0, 1) * 255 (wrapper.py:294),
+ * l1 = mean(|rendered / 255 - target / 255|) (scripts/train.py:187-191).
+ * Adds sum |.| into *loss_sum (device double; divide by n for the mean) and
+ * writes d l1 / d raw into grad_raw. target is float [0, 255] or, with
+ * target_is_u8 = 1, uint8. */
+GS_API int gs_l1_loss_grad(int64_t n, const float *raw_image, const void *target,
+                           int target_is_u8, float *grad_raw, double *loss_sum, void *stream);
 
 #ifdef __cplusplus
 }
