@@ -387,9 +387,26 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
 
 // ---- tile layout kernels -------------------------------------------------------
 
-// Pairs in depth order: thread i takes the i-th Gaussian of the depth sort
-// and writes its tile ids (row-major over its rectangle) and its id at
-// offsets[i] (exclusive scan of the counts in depth order).
+// Pairs in depth order. Thread i takes the i-th Gaussian of the depth sort
+// and its output range at offsets[i] (exclusive scan of the counts in depth
+// order). Rectangles of up to kSmallRect tiles are written by their own
+// thread; larger ones by the whole warp, one Gaussian at a time, lane q
+// writing the rectangle's q-th tile in row-major order (contiguous stores). The digit
+// histograms of the following tile-id sort (passes of 8 bits over tbits bits)
+// are counted on the way (per-block shared counters, one global atomic per
+// non-zero bin per block), which saves the sort a read of the keys.
+constexpr int kSmallRect = 8;
+
+template <typename KT>
+__device__ __forceinline__ void emit_one(int64_t o, int tile, int g, KT *keys, int32_t *vals,
+                                         uint32_t *s_hist, int tpasses) {
+  keys[o] = (KT)tile;
+  vals[o] = g;
+  atomicAdd(&s_hist[tile & 255], 1u);
+  if (tpasses > 1) atomicAdd(&s_hist[256 + ((tile >> 8) & 255)], 1u);
+  if (tpasses > 2) atomicAdd(&s_hist[512 + ((tile >> 16) & 255)], 1u);
+}
+
 template <typename KT>
 __global__ void __launch_bounds__(256) emit_pairs_kernel(int n, const int32_t *__restrict__ order,
                                                          const int32_t *__restrict__ counts,
@@ -397,39 +414,90 @@ __global__ void __launch_bounds__(256) emit_pairs_kernel(int n, const int32_t *_
                                                          const float2 *__restrict__ points,
                                                          const float2 *__restrict__ radii,
                                                          int width, int height, int64_t total,
-                                                         KT *__restrict__ keys,
-                                                         int32_t *__restrict__ vals) {
+                                                         int tpasses, KT *__restrict__ keys,
+                                                         int32_t *__restrict__ vals,
+                                                         uint32_t *__restrict__ hist) {
+  __shared__ uint32_t s_hist[3 * 256];
+  for (int k = threadIdx.x; k < tpasses * 256; k += blockDim.x) s_hist[k] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int g = order[i];
-  if (g < 0 || g >= n || counts[g] <= 0) return;
-  const float2 p = points[g], r = radii[g];
-  const TileRect tr = tile_rect(p.x, p.y, r.x, r.y, width, height);
-  if (tr.empty) return;
   const int tx = tiles_x_of(width);
-  int64_t o = offsets[i];
-  if (o < 0) return;
-  for (int y = tr.y0; y <= tr.y1; ++y)
-    for (int x = tr.x0; x <= tr.x1; ++x) {
-      if (o >= total) return;  // only reachable if the offsets were corrupted
-      keys[o] = (KT)(y * tx + x);
-      vals[o] = g;
-      ++o;
+  int g = -1, x0 = 0, y0 = 0, w = 0, h = 0;
+  int64_t base = 0;
+  if (i < n) {
+    const int gg = order[i];
+    if (gg >= 0 && gg < n && counts[gg] > 0) {
+      const float2 p = points[gg], r = radii[gg];
+      const TileRect tr = tile_rect(p.x, p.y, r.x, r.y, width, height);
+      base = offsets[i];
+      w = tr.x1 - tr.x0 + 1;
+      h = tr.y1 - tr.y0 + 1;
+      if (!tr.empty && base >= 0 && base + (int64_t)w * h <= total) {  // else: corrupted offsets
+        g = gg;
+        x0 = tr.x0;
+        y0 = tr.y0;
+      }
     }
+  }
+  const bool big = g >= 0 && w * h > kSmallRect;
+  if (g >= 0 && !big) {
+    int64_t o = base;
+    for (int y = y0; y < y0 + h; ++y)
+      for (int x = x0; x < x0 + w; ++x) emit_one<KT>(o++, y * tx + x, g, keys, vals, s_hist, tpasses);
+  }
+  uint32_t todo = __ballot_sync(0xffffffffu, big);
+  while (todo) {
+    const int j = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const int gj = __shfl_sync(0xffffffffu, g, j);
+    const int xj = __shfl_sync(0xffffffffu, x0, j), yj = __shfl_sync(0xffffffffu, y0, j);
+    const int wj = __shfl_sync(0xffffffffu, w, j), hj = __shfl_sync(0xffffffffu, h, j);
+    const int64_t bj = __shfl_sync(0xffffffffu, base, j);
+    const int area = wj * hj;
+    for (int q = lane; q < area; q += 32) {
+      const int r = q / wj, c = q - r * wj;
+      emit_one<KT>(bj + q, (yj + r) * tx + xj + c, gj, keys, vals, s_hist, tpasses);
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < tpasses * 256; k += blockDim.x)
+    if (s_hist[k]) atomicAdd(&hist[k], s_hist[k]);
 }
 
-// Per-tile start offsets from the sorted tile ids (kernel.cu:875-914).
+// Per-tile start offsets from the sorted tile ids (kernel.cu:875-914): one
+// thread per 8 consecutive ids (a 16-byte load for 16-bit ids), comparing
+// each id with its predecessor and filling the offsets of the tiles in
+// between.
 template <typename KT>
 __global__ void __launch_bounds__(256) ranges_kernel(const KT *__restrict__ tiles_sorted,
                                                      int64_t n, int num_tiles,
                                                      int32_t *__restrict__ offsets) {
-  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= n) return;
-  const int tile = min((int)tiles_sorted[k], num_tiles - 1);
-  const int prev = (k == 0) ? -1 : min((int)tiles_sorted[k - 1], num_tiles - 1);
-  for (int g = prev + 1; g <= tile; ++g) offsets[g] = (int32_t)k;
-  if (k == n - 1)
-    for (int g = tile + 1; g < num_tiles; ++g) offsets[g] = (int32_t)n;
+  constexpr int kPer = 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kPer;
+  for (int64_t k0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPer; k0 < n; k0 += stride) {
+    KT v[kPer];
+    if (k0 + kPer <= n && sizeof(KT) * kPer == 16) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(tiles_sorted + k0);
+      const KT *pv = reinterpret_cast<const KT *>(&raw);
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) v[q] = pv[q];
+    } else {
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) v[q] = (k0 + q < n) ? tiles_sorted[k0 + q] : (KT)0;
+    }
+    int prev = (k0 == 0) ? -1 : min((int)tiles_sorted[k0 - 1], num_tiles - 1);
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int64_t k = k0 + q;
+      if (k >= n) break;
+      const int tile = min((int)v[q], num_tiles - 1);
+      for (int t = prev + 1; t <= tile; ++t) offsets[t] = (int32_t)k;
+      prev = tile;
+      if (k == n - 1)
+        for (int t = tile + 1; t < num_tiles; ++t) offsets[t] = (int32_t)n;
+    }
+  }
 }
 
 // The reference's 64-bit keys (tile << 32 | depth bits) of the sorted pairs,
@@ -485,7 +553,7 @@ static int sm_count() {
 template <typename KT>
 static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *vals_alt,
                     int end_bit, void *scratch, cudaStream_t st, const int32_t *vals_first = nullptr,
-                    bool identity_first = false) {
+                    bool identity_first = false, const uint32_t *hist_given = nullptr) {
   constexpr int ITEMS = SortItems<KT>::value;
   const int passes = (end_bit + 7) / 8;
   if (n <= 0 || passes <= 0) return GS_OK;
@@ -497,10 +565,14 @@ static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *v
   uint32_t *tickets = reinterpret_cast<uint32_t *>(base + L.tickets);
   int rc = cuda_status(cudaMemsetAsync(scratch, 0, L.total, st));
   if (rc) return rc;
-  const int64_t hb = (n + 255) / 256;
-  const int hblocks = (int)(hb < (int64_t)sm_count() * 4 ? hb : (int64_t)sm_count() * 4);
-  sort_histogram_kernel<KT><<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
-  count_launch();
+  if (hist_given) {
+    hist = const_cast<uint32_t *>(hist_given);  // digit counts known in advance
+  } else {
+    const int64_t hb = (n + 255) / 256;
+    const int hblocks = (int)(hb < (int64_t)sm_count() * 4 ? hb : (int64_t)sm_count() * 4);
+    sort_histogram_kernel<KT><<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
+    count_launch();
+  }
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -537,7 +609,8 @@ static int bits_for(int64_t count) {
 
 // Scratch of the tile layout, carved in this order.
 struct LayoutScratch {
-  size_t dkeys_a, dkeys_b, dvals_a, dvals_b, offs, total8, tkeys_a, tkeys_b, tvals_b, sort, total;
+  size_t dkeys_a, dkeys_b, dvals_a, dvals_b, offs, total8, thist, tkeys_a, tkeys_b, tvals_b, sort,
+      total;
 };
 
 static LayoutScratch layout_scratch(int n, int64_t total, int num_tiles) {
@@ -550,7 +623,8 @@ static LayoutScratch layout_scratch(int n, int64_t total, int num_tiles) {
   L.dvals_b = align_up(L.dvals_a + 4 * nn, 256);
   L.offs = align_up(L.dvals_b + 4 * nn, 256);
   L.total8 = align_up(L.offs + 4 * nn, 256);  // the scan's int64 total (8-byte aligned)
-  L.tkeys_a = align_up(L.total8 + 8, 256);
+  L.thist = align_up(L.total8 + 8, 256);
+  L.tkeys_a = align_up(L.thist + kMaxPasses * 256 * 4, 256);
   L.tkeys_b = align_up(L.tkeys_a + tk * kk, 256);
   L.tvals_b = align_up(L.tkeys_b + tk * kk, 256);
   L.sort = align_up(L.tvals_b + 4 * kk, 256);
@@ -596,24 +670,30 @@ static int tile_layout_impl(int n, const float2 *points, const float2 *radii, co
                                                device_status_word());
   count_launch();
 
-  // 3. pairs in depth order, 4. stable sort by tile id
+  // 3. pairs in depth order (with the tile sort's digit histograms)
   const int tbits = bits_for(num_tiles) > 0 ? bits_for(num_tiles) : 1;
   const int tpasses = (tbits + 7) / 8;
+  uint32_t *thist = reinterpret_cast<uint32_t *>(p + L.thist);
+  rc = cuda_status(cudaMemsetAsync(thist, 0, kMaxPasses * 256 * 4, st));
+  if (rc) return rc;
   KT *k0 = (tpasses & 1) ? tk_b : tk_a;
   int32_t *v0 = (tpasses & 1) ? tv_b : ids_sorted;
   KT *k1 = (tpasses & 1) ? tk_a : tk_b;
   int32_t *v1 = (tpasses & 1) ? ids_sorted : tv_b;
   emit_pairs_kernel<KT><<<(n + 255) / 256, 256, 0, st>>>(n, order, counts, offs, points, radii,
-                                                         width, height, total, k0, v0);
+                                                         width, height, total, tpasses, k0, v0,
+                                                         thist);
   count_launch();
-  rc = run_sort<KT>(total, k0, v0, k1, v1, tbits, sort_scratch, st);
+  // 4. stable sort by tile id; the sorted ids land in (tk_a, ids_sorted)
+  rc = run_sort<KT>(total, k0, v0, k1, v1, tbits, sort_scratch, st, nullptr, false, thist);
   if (rc) return rc;
-  // the sorted tile ids are in tk_a, the ids in ids_sorted
-
   // 5. tile ranges
-  ranges_kernel<KT><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(tk_a, total, num_tiles,
-                                                                     indexing_offset);
-  count_launch();
+  {
+    const int64_t want = (total + 256 * 8 - 1) / (256 * 8);
+    const int grid = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
+    ranges_kernel<KT><<<grid, 256, 0, st>>>(tk_a, total, num_tiles, indexing_offset);
+    count_launch();
+  }
   if (keys_sorted) {
     full_keys_kernel<KT><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(tk_a, ids_sorted, depths,
                                                                           total, keys_sorted);
@@ -699,6 +779,7 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
   if (total >= (int64_t)kLbValue) return GS_ERR_CAPACITY;
   cudaStream_t st = as_stream(stream);
   const int num_tiles = tiles_x_of(width) * tiles_y_of(height);
+  if (num_tiles > (1 << 24)) return GS_ERR_CAPACITY;  // tile ids sorted in at most 3 passes
   // rasterizer.cpp:352: offsets start at zero; with no pairs they stay zero.
   int rc = cuda_status(cudaMemsetAsync(indexing_offset, 0, (size_t)num_tiles * sizeof(int32_t), st));
   if (rc || total == 0 || n == 0) return rc;

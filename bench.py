@@ -75,6 +75,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--cpu-sample-views", type=int, default=2)
+    p.add_argument("--mode", choices=["train", "render"], default="train",
+                   help="render: forward-only novel-view rendering (config 4), frames/s")
     p.add_argument("--trainer", choices=["native", "autograd"], default="native",
                    help="native: NativeTrainer (fused activations/loss, flat-buffer gradients); "
                         "autograd: render() + Torch activations/loss + autograd")
@@ -289,9 +291,11 @@ def run_reference(args, world, rank):
 
 
 def workload_config(args, cfg, views_per_rank):
+    what = ("forward-only rendering to uint8 frames, replicas (no communication)"
+            if getattr(args, "mode", "train") == "render" else "L1 vs uniform target, Adam step")
     return {"workload": f"config {args.config}: {cfg.n if args.n is None else args.n} SH3 "
                         f"Gaussians, {cfg.width}x{cfg.height}, {views_per_rank} view(s)/rank per "
-                        f"step, orbit r={cfg.camera_distance}, L1 vs uniform target, Adam step",
+                        f"step, orbit r={cfg.camera_distance}, {what}",
             "global_batch": views_per_rank * max(args.gpus, 1), "views_per_rank": views_per_rank,
             "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
@@ -387,6 +391,24 @@ class NativeBenchTrainer:
             self.host_loss.copy_(losses, non_blocking=True)
         return losses
 
+    def render_step(self, e2e=False):
+        """Forward-only rendering of this rank's views into uint8 frames
+        (configuration 4); with e2e the frames are copied to pinned host
+        memory."""
+        if e2e:
+            cams = self.host_cams.to(self.device, non_blocking=True)
+            K = self.host_K.to(self.device, non_blocking=True)
+        else:
+            cams, K = self.cams, self.K
+        views = self.nt.forward_views(cams, K)
+        frames = [(v["image"].clamp(0, 1) * 255).round().to(torch.uint8) for v in views]
+        if e2e:
+            if not hasattr(self, "host_frames"):
+                self.host_frames = [torch.empty_like(f, device="cpu").pin_memory() for f in frames]
+            for h, f in zip(self.host_frames, frames):
+                h.copy_(f, non_blocking=True)
+        return frames
+
 
 def count_pairs(tr, view=0):
     """Evaluated (pixel, Gaussian) pairs of one view, in the reference's
@@ -437,9 +459,13 @@ def main():
     tr = (NativeBenchTrainer if args.trainer == "native" else Trainer)(cfg, args.n, V, world, rank,
                                                                         device)
     n = tr.params["means"].shape[0]
+    render_mode = args.mode == "render"
+    if render_mode and args.trainer != "native":
+        raise SystemExit("--mode render uses the native path")
+    run_step = tr.render_step if render_mode else tr.step
 
     for _ in range(args.warmup):
-        tr.step()
+        run_step()
     torch.cuda.synchronize()
     barrier(world)
 
@@ -452,7 +478,7 @@ def main():
         torch.cuda.synchronize()
         start.record()
         for _ in range(args.steps):
-            tr.step()
+            run_step()
         end.record()
         torch.cuda.synchronize()
         barrier(world)
@@ -461,23 +487,29 @@ def main():
     ms_total = max_over_ranks(start.elapsed_time(end), world)
     ms_step = ms_total / args.steps
     value = world * V * args.steps / (ms_total / 1000.0)
+    unit = "frames/s" if render_mode else "views/s"
     stage_ms = stages.mean_ms()
 
     e2e = None
     if not args.no_e2e:
         for _ in range(2):
-            tr.step(e2e=True)
+            run_step(e2e=True)
         torch.cuda.synchronize()
         barrier(world)
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            tr.step(e2e=True)
-            torch.cuda.current_stream().synchronize()  # loss is on the host
+            run_step(e2e=True)
+            torch.cuda.current_stream().synchronize()  # the step's result is on the host
         barrier(world)
         sec = max_over_ranks(time.perf_counter() - t0, world)
-        h2d = sum(t.numel() for t in tr.host_targets) + V * (16 + 9) * 4
-        e2e = {"value": world * V * args.steps / sec, "unit": "views/s",
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(V * 4),
+        if render_mode:
+            h2d = V * (16 + 9) * 4
+            d2h = V * cfg.width * cfg.height * 3
+        else:
+            h2d = sum(t.numel() for t in tr.host_targets) + V * (16 + 9) * 4
+            d2h = V * 8
+        e2e = {"value": world * V * args.steps / sec, "unit": unit,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "timing": "wall clock, max over ranks"}
 
     # roofline of the dominant stage
@@ -522,7 +554,7 @@ def main():
                                         else "see DESIGN.md")}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not render_mode:
         act, cams, tg, threads = cpu_setup(cfg, args.n, args.cpu_sample_views)
         sec = cpu_fwd_bwd_views(cfg, act, cams, tg)
         cpu = {"value": args.cpu_sample_views / sec, "unit": "views/s", "cores": threads,
@@ -532,9 +564,11 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world,
+            "metric": METRIC if not render_mode else "inference frames/s (config 4)",
+            "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "ms_per_view": ms_step / V, "higher_is_better": True, "scaling": "weak",
+            "mode": args.mode,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, cfg, V), "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks, "roofline": roofline, "stages": roof,

@@ -161,3 +161,49 @@ def test_render_end_to_end_vs_reference(gs, ref, cfg_id, n, W, H):
     for k in rg:
         assert_close_metric(k, og[k], rg[k], 0.999, 1e-3)
     assert_close_metric("points_img.grad", op, rp, 0.999, 1e-3)
+
+
+def test_cfg3_stress_layout_and_image_vs_reference(gs, ref):
+    """Configuration 3 (2M Gaussians in 64 clusters, ~50 tiles per Gaussian,
+    3840x2160, ~10^8 pairs): the reference's layout and image, bit for bit."""
+    _, a, w2c, K, W, H = scene(gs, 3)
+    r = ref.project_points(a["means"], a["scales"], a["quaternions"], a["opacities"], w2c, K, *ARGS,
+                           W, H)
+    o = gs.cuda_rasterizer.project_points(a["means"], a["scales"], a["quaternions"],
+                                          a["opacities"], w2c, K, *ARGS, W, H)
+    assert torch.equal(r[5], o[5])
+    for x, y in zip(o[:5], r[:5]):
+        assert torch.equal(x, y)
+    pts, depths, conic, radii, mask = r[0], r[1], r[3], r[4], r[5]
+    r_off, r_ids = ref.compute_tile_intersection(pts, radii, depths, mask, W, H, 16)
+    off, ids = gs.cuda_rasterizer.compute_tile_intersection(pts, radii, depths, mask, W, H, 16)
+    print("cfg3 pairs:", ids.numel())
+    assert ids.numel() > 50_000_000
+    assert torch.equal(off, r_off)
+    assert torch.equal(ids, r_ids)
+    del r_ids
+    colors = torch.rand((pts.shape[0], 3), device=DEV, generator=torch.Generator(DEV).manual_seed(4))
+    args = (off, ids, pts, conic, a["opacities"], colors, W, H, 16, 1e-4, 1e-4, 9.21)
+    ri = ref.rasterize(*args)
+    oi = gs.cuda_rasterizer.rasterize(*args)
+    assert torch.equal(ri, oi)
+
+
+def test_cfg3_fused_render_forward_vs_reference(gs, ref):
+    """render()'s fused path on configuration 3 against the reference
+    composition (forward)."""
+    raw, a, w2c, K, W, H = scene(gs, 3)
+    with torch.no_grad():
+        img, pts, radii = gs.render(w2c, K, W, H, a["means"], a["scales"], a["quaternions"],
+                                    a["opacities"], a["sh_coeffs_dc"], a["sh_coeffs_rest"])
+        r = ref.project_points(a["means"], a["scales"], a["quaternions"], a["opacities"], w2c, K,
+                               *ARGS, W, H)
+        campos = -w2c[:3, :3].t() @ w2c[:3, 3]
+        colors = torch.clamp_min(ref.evaluate_spherical_harmonics(
+            campos, a["means"], a["sh_coeffs_dc"], a["sh_coeffs_rest"], r[5], False) + 0.5, 0.0)
+        off, ids = ref.compute_tile_intersection(r[0], r[4], r[1], r[5], W, H, 16)
+        ri = ref.rasterize(off, ids, r[0], r[3], a["opacities"], colors, W, H, 16, 1e-4, 1e-4, 9.21)
+        ri = ri.clamp(0, 1) * 255
+    assert torch.equal(radii, r[4]) and torch.equal(pts, r[0])
+    d = (img - ri).abs() / 255.0
+    assert float(d.max()) <= 1e-4, float(d.max())
