@@ -61,6 +61,10 @@ SIGNATURES = {
     "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P]),
     "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
+    "gs_ssim_scratch_bytes": (SZ, [I, I, I]),
+    "gs_ssim_forward": (I, [I, I, I, P, P, I, P, SZ, P, P]),
+    "gs_ssim_backward": (I, [I, I, I, P, P, P, P, P, P]),
+    "gs_l1_ssim_loss_grad": (I, [I, I, P, P, I, F, P, P, P, SZ, P]),
     "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P, I, P, I, P,
                                    P, P, P, P, P, P]),
 }

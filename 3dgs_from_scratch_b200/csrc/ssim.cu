@@ -1,0 +1,384 @@
+// ssim.cu -- SSIM (11x11 Gaussian window, sigma 1.5) with its gradient, and the
+// reference's training loss (1 - lambda) * L1 + lambda * (1 - SSIM) fused with
+// the clamp * 255 / 255 of the rendered image (scripts/train.py:183-203).
+//
+// The reference takes SSIM from the external package fused_ssim (pinned as
+// fused-ssim==0.0.0 in environment.yml:56, not vendored), called at
+// scripts/train.py:193-197 and scripts/evaluate.py:57-61. What is restated
+// here is the published definition of Wang et al. (2004) that package
+// implements: per channel, Gaussian-weighted local statistics
+//   mu_x = G*x, mu_y = G*y, s_xx = G*(x^2) - mu_x^2, s_yy = ..., s_xy = G*(xy) - mu_x mu_y
+// (G the normalised 11-tap Gaussian, sigma 1.5, outer product; zero padding),
+// S = (2 mu_x mu_y + C1)(2 s_xy + C2) / ((mu_x^2 + mu_y^2 + C1)(s_xx + s_yy + C2)),
+// C1 = 0.01^2, C2 = 0.03^2, and the loss value is the mean of S over every
+// channel and pixel ("same") or over the pixels at least 5 from every border
+// ("valid", the reference's choice).
+//
+// Two kernels, both tiled 32 x 16 output pixels per block with the 5-pixel
+// halo staged in shared memory and the window applied separably:
+//   ssim_fwd_kernel  local statistics -> S (summed into a double) and the
+//                    three partial derivatives of S at each pixel,
+//                    dS/dmu_x, dS/dE[x^2], dS/dE[xy], already multiplied by
+//                    the loss weight of that pixel (zero where not counted);
+//   ssim_bwd_kernel  the same window applied to those three maps gives
+//                    dL/dx(p) = G*m0 + 2 x(p) G*m1 + y(p) G*m2;
+//                    in the fused-loss form it adds the L1 term, sums |d|,
+//                    and chains through clamp * 255 / 255 to the raw image.
+// Inputs are either planar (N, C, H, W) fp32 (the fused_ssim interface) or
+// the rasterizer's (H, W, 3) raw image with an (H, W, 3) uint8 or fp32 target
+// in [0, 255] (the training loss).
+#include "gs_common.cuh"
+
+namespace gs {
+
+constexpr int kSsimTW = 32;           // output tile width
+constexpr int kSsimTH = 16;           // output tile height
+constexpr int kSsimR = 5;             // window radius
+constexpr int kSsimWin = 2 * kSsimR + 1;
+constexpr int kSsimHW = kSsimTW + 2 * kSsimR;  // 42 staged columns
+constexpr int kSsimHH = kSsimTH + 2 * kSsimR;  // 26 staged rows
+constexpr int kSsimThreads = 256;
+constexpr float kSsimC1 = 0.01f * 0.01f;
+constexpr float kSsimC2 = 0.03f * 0.03f;
+
+__constant__ float c_ssim_win[kSsimWin];
+
+// Where the two images of one plane come from.
+//   HWC = false: planar fp32, plane p = n * C + c at offset p * H * W.
+//   HWC = true : raw rendered (H, W, C) fp32 -> clamp(r, 0, 1) * 255 / 255,
+//                target (H, W, C) of type TT -> t / 255; plane = channel.
+template <bool HWC, typename TT>
+struct SsimSrc {
+  const float *a;
+  const TT *b;
+  int C, H, W;
+
+  __device__ __forceinline__ int64_t index(int plane, int y, int x) const {
+    if (HWC) return ((int64_t)y * W + x) * C + plane;
+    return (int64_t)plane * H * W + (int64_t)y * W + x;
+  }
+  __device__ __forceinline__ void load(int plane, int y, int x, float &xv, float &yv) const {
+    const int64_t i = index(plane, y, x);
+    if (HWC) {
+      const float c = fminf(fmaxf(a[i], 0.0f), 1.0f);
+      xv = (c * 255.0f) / 255.0f;
+      yv = (float)b[i] / 255.0f;
+    } else {
+      xv = a[i];
+      yv = (float)b[i];
+    }
+  }
+};
+
+__device__ __forceinline__ double block_sum_double(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __shared__ double s_part[kSsimThreads / 32];
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kSsimThreads / 32; ++w) t += s_part[w];
+  return t;  // valid in thread 0
+}
+
+// Grid: x = tiles_x * planes (plane fastest, so the blocks of the three
+// channels of one tile run together and share the tile's cache lines),
+// y = tiles_y.
+template <bool HWC, typename TT>
+__global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT> src, int planes,
+                                                                int valid, float wscale,
+                                                                float *__restrict__ m0,
+                                                                float *__restrict__ m1,
+                                                                float *__restrict__ m2,
+                                                                double *__restrict__ ssim_sum) {
+  __shared__ float sx[kSsimHH][kSsimHW + 1];
+  __shared__ float sy[kSsimHH][kSsimHW + 1];
+  __shared__ float hs[5][kSsimHH][kSsimTW + 1];
+  const int H = src.H, W = src.W;
+  const int plane = blockIdx.x % planes;
+  const int tx = blockIdx.x / planes;
+  const int gx0 = tx * kSsimTW, gy0 = blockIdx.y * kSsimTH;
+  for (int k = threadIdx.x; k < kSsimHH * kSsimHW; k += kSsimThreads) {
+    const int r = k / kSsimHW, c = k - r * kSsimHW;
+    const int gy = gy0 - kSsimR + r, gx = gx0 - kSsimR + c;
+    float xv = 0.0f, yv = 0.0f;
+    if (gy >= 0 && gy < H && gx >= 0 && gx < W) src.load(plane, gy, gx, xv, yv);
+    sx[r][c] = xv;
+    sy[r][c] = yv;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < kSsimHH * kSsimTW; k += kSsimThreads) {
+    const int r = k / kSsimTW, c = k - r * kSsimTW;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+    for (int t = 0; t < kSsimWin; ++t) {
+      const float g = c_ssim_win[t];
+      const float xv = sx[r][c + t], yv = sy[r][c + t];
+      a0 = fmaf(g, xv, a0);
+      a1 = fmaf(g, yv, a1);
+      a2 = fmaf(g, xv * xv, a2);
+      a3 = fmaf(g, yv * yv, a3);
+      a4 = fmaf(g, xv * yv, a4);
+    }
+    hs[0][r][c] = a0;
+    hs[1][r][c] = a1;
+    hs[2][r][c] = a2;
+    hs[3][r][c] = a3;
+    hs[4][r][c] = a4;
+  }
+  __syncthreads();
+  double acc = 0.0;
+  for (int k = threadIdx.x; k < kSsimTH * kSsimTW; k += kSsimThreads) {
+    const int r = k / kSsimTW, c = k - r * kSsimTW;
+    const int gy = gy0 + r, gx = gx0 + c;
+    if (gy >= H || gx >= W) continue;
+    float mx = 0.f, my = 0.f, exx = 0.f, eyy = 0.f, exy = 0.f;
+#pragma unroll
+    for (int t = 0; t < kSsimWin; ++t) {
+      const float g = c_ssim_win[t];
+      mx = fmaf(g, hs[0][r + t][c], mx);
+      my = fmaf(g, hs[1][r + t][c], my);
+      exx = fmaf(g, hs[2][r + t][c], exx);
+      eyy = fmaf(g, hs[3][r + t][c], eyy);
+      exy = fmaf(g, hs[4][r + t][c], exy);
+    }
+    const bool counted =
+        !valid || (gy >= kSsimR && gy < H - kSsimR && gx >= kSsimR && gx < W - kSsimR);
+    float d_mu = 0.f, d_xx = 0.f, d_xy = 0.f;
+    if (counted) {
+      const float sxx = exx - mx * mx, syy = eyy - my * my, sxy = exy - mx * my;
+      const float a1 = 2.f * mx * my + kSsimC1, a2 = 2.f * sxy + kSsimC2;
+      const float b1 = mx * mx + my * my + kSsimC1, b2 = sxx + syy + kSsimC2;
+      const float inv_b = 1.0f / (b1 * b2);
+      const float s = a1 * a2 * inv_b;
+      acc += (double)s;
+      d_xy = 2.f * a1 * inv_b;                     // dS/dE[xy]
+      d_xx = -s / b2;                              // dS/dE[x^2]
+      d_mu = 2.f * my * a2 * inv_b - 2.f * mx * s / b1 - 2.f * mx * d_xx - my * d_xy;
+      d_mu *= wscale;
+      d_xx *= wscale;
+      d_xy *= wscale;
+    }
+    const int64_t o = (int64_t)plane * H * W + (int64_t)gy * W + gx;
+    m0[o] = d_mu;
+    m1[o] = d_xx;
+    m2[o] = d_xy;
+  }
+  const double t = block_sum_double(acc);
+  if (threadIdx.x == 0 && t != 0.0) atomicAdd(ssim_sum, t);
+}
+
+// FUSED = true: the training loss form (HWC only): grad_raw = chain of
+// l1_weight * sign(x - y) / numel + (G*m0 + 2x G*m1 + y G*m2) through the
+// / 255, * 255 and the clamp mask, and sum |x - y| into l1_sum.
+// FUSED = false: grad (planar) = upstream * (G*m0 + 2x G*m1 + y G*m2).
+template <bool HWC, typename TT, bool FUSED>
+__global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
+    SsimSrc<HWC, TT> src, int planes, const float *__restrict__ m0, const float *__restrict__ m1,
+    const float *__restrict__ m2, const float *__restrict__ upstream, float l1_weight,
+    float inv_numel, float *__restrict__ grad, double *__restrict__ l1_sum) {
+  __shared__ float sm[3][kSsimHH][kSsimHW + 1];
+  __shared__ float hs[3][kSsimHH][kSsimTW + 1];
+  const int H = src.H, W = src.W;
+  const int plane = blockIdx.x % planes;
+  const int tx = blockIdx.x / planes;
+  const int gx0 = tx * kSsimTW, gy0 = blockIdx.y * kSsimTH;
+  const int64_t pbase = (int64_t)plane * H * W;
+  for (int k = threadIdx.x; k < kSsimHH * kSsimHW; k += kSsimThreads) {
+    const int r = k / kSsimHW, c = k - r * kSsimHW;
+    const int gy = gy0 - kSsimR + r, gx = gx0 - kSsimR + c;
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+    if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
+      const int64_t o = pbase + (int64_t)gy * W + gx;
+      v0 = m0[o];
+      v1 = m1[o];
+      v2 = m2[o];
+    }
+    sm[0][r][c] = v0;
+    sm[1][r][c] = v1;
+    sm[2][r][c] = v2;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < kSsimHH * kSsimTW; k += kSsimThreads) {
+    const int r = k / kSsimTW, c = k - r * kSsimTW;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+    for (int t = 0; t < kSsimWin; ++t) {
+      const float g = c_ssim_win[t];
+      a0 = fmaf(g, sm[0][r][c + t], a0);
+      a1 = fmaf(g, sm[1][r][c + t], a1);
+      a2 = fmaf(g, sm[2][r][c + t], a2);
+    }
+    hs[0][r][c] = a0;
+    hs[1][r][c] = a1;
+    hs[2][r][c] = a2;
+  }
+  __syncthreads();
+  const float up = upstream ? *upstream : 1.0f;
+  double acc = 0.0;
+  for (int k = threadIdx.x; k < kSsimTH * kSsimTW; k += kSsimThreads) {
+    const int r = k / kSsimTW, c = k - r * kSsimTW;
+    const int gy = gy0 + r, gx = gx0 + c;
+    if (gy >= H || gx >= W) continue;
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+#pragma unroll
+    for (int t = 0; t < kSsimWin; ++t) {
+      const float g = c_ssim_win[t];
+      c0 = fmaf(g, hs[0][r + t][c], c0);
+      c1 = fmaf(g, hs[1][r + t][c], c1);
+      c2 = fmaf(g, hs[2][r + t][c], c2);
+    }
+    float xv, yv;
+    src.load(plane, gy, gx, xv, yv);
+    const float gs = c0 + 2.f * xv * c1 + yv * c2;
+    if (FUSED) {
+      const int64_t i = src.index(plane, gy, gx);
+      const float d = xv - yv;
+      acc += (double)fabsf(d);
+      const float sgn = (d > 0.0f) ? 1.0f : ((d < 0.0f) ? -1.0f : 0.0f);
+      const float gn = l1_weight * sgn * inv_numel + gs;  // d loss / d rendered_norm
+      float g = gn / 255.0f;                             // rendered_norm = rendered / 255
+      g = g * 255.0f;                                    // rendered = clamp(raw) * 255
+      const float raw = src.a[i];
+      grad[i] = (raw >= 0.0f && raw <= 1.0f) ? g : 0.0f;
+    } else {
+      grad[pbase + (int64_t)gy * W + gx] = up * gs;
+    }
+  }
+  if (FUSED) {
+    const double t = block_sum_double(acc);
+    if (threadIdx.x == 0 && t != 0.0) atomicAdd(l1_sum, t);
+  }
+}
+
+static int g_win_ready[64] = {0};
+
+// The normalised window exp(-(i - 5)^2 / (2 * 1.5^2)) / sum, computed in
+// double and rounded to fp32, uploaded once per device.
+static int ensure_window() {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev));
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return GS_ERR_INVALID_ARGUMENT;
+  if (g_win_ready[dev]) return GS_OK;
+  double w[kSsimWin], sum = 0.0;
+  for (int i = 0; i < kSsimWin; ++i) {
+    const double d = (double)(i - kSsimR);
+    w[i] = exp(-d * d / (2.0 * 1.5 * 1.5));
+    sum += w[i];
+  }
+  float wf[kSsimWin];
+  for (int i = 0; i < kSsimWin; ++i) wf[i] = (float)(w[i] / sum);
+  rc = cuda_status(cudaMemcpyToSymbol(c_ssim_win, wf, sizeof(wf)));
+  if (rc) return rc;
+  g_win_ready[dev] = 1;
+  return GS_OK;
+}
+
+static dim3 ssim_grid(int planes, int H, int W) {
+  return dim3((unsigned)(((W + kSsimTW - 1) / kSsimTW) * planes),
+              (unsigned)((H + kSsimTH - 1) / kSsimTH));
+}
+
+static bool ssim_grid_ok(int planes, int H, int W) {
+  return (int64_t)((W + kSsimTW - 1) / kSsimTW) * planes < (int64_t)INT32_MAX &&
+         (H + kSsimTH - 1) / kSsimTH <= 65535;
+}
+
+static int64_t ssim_count(int planes, int H, int W, int valid) {
+  if (!valid) return (int64_t)planes * H * W;
+  return (int64_t)planes * (H - 2 * kSsimR) * (W - 2 * kSsimR);
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" size_t gs_ssim_scratch_bytes(int planes, int height, int width) {
+  if (planes <= 0 || height <= 0 || width <= 0) return 0;
+  return (size_t)3 * planes * height * width * sizeof(float);
+}
+
+extern "C" int gs_ssim_forward(int planes, int height, int width, const float *img1,
+                               const float *img2, int valid, float *scratch,
+                               size_t scratch_bytes, double *ssim_sum, void *stream) {
+  if (planes <= 0 || height <= 0 || width <= 0 || img1 == nullptr || img2 == nullptr ||
+      ssim_sum == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (valid && (height <= 2 * kSsimR || width <= 2 * kSsimR)) return GS_ERR_INVALID_ARGUMENT;
+  if (!ssim_grid_ok(planes, height, width)) return GS_ERR_CAPACITY;
+  if (scratch == nullptr || scratch_bytes < gs_ssim_scratch_bytes(planes, height, width))
+    return GS_ERR_CAPACITY;
+  int rc = ensure_window();
+  if (rc) return rc;
+  const int64_t plane_px = (int64_t)height * width;
+  const float wscale = (float)(1.0 / (double)ssim_count(planes, height, width, valid));
+  SsimSrc<false, float> src{img1, img2, 1, height, width};
+  ssim_fwd_kernel<false, float><<<ssim_grid(planes, height, width), kSsimThreads, 0,
+                                  reinterpret_cast<cudaStream_t>(stream)>>>(
+      src, planes, valid, wscale, scratch, scratch + planes * plane_px,
+      scratch + 2 * planes * plane_px, ssim_sum);
+  count_launch();
+  return launch_status();
+}
+
+extern "C" int gs_ssim_backward(int planes, int height, int width, const float *img1,
+                                const float *img2, const float *scratch, const float *grad_out,
+                                float *grad_img1, void *stream) {
+  if (planes <= 0 || height <= 0 || width <= 0 || img1 == nullptr || img2 == nullptr ||
+      scratch == nullptr || grad_img1 == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!ssim_grid_ok(planes, height, width)) return GS_ERR_CAPACITY;
+  int rc = ensure_window();
+  if (rc) return rc;
+  const int64_t plane_px = (int64_t)height * width;
+  SsimSrc<false, float> src{img1, img2, 1, height, width};
+  ssim_bwd_kernel<false, float, false><<<ssim_grid(planes, height, width), kSsimThreads, 0,
+                                         reinterpret_cast<cudaStream_t>(stream)>>>(
+      src, planes, scratch, scratch + planes * plane_px, scratch + 2 * planes * plane_px,
+      grad_out, 0.0f, 0.0f, grad_img1, nullptr);
+  count_launch();
+  return launch_status();
+}
+
+extern "C" int gs_l1_ssim_loss_grad(int height, int width, const float *raw_image,
+                                    const void *target, int target_is_u8, float ssim_lambda,
+                                    float *grad_raw, double *sums, float *scratch,
+                                    size_t scratch_bytes, void *stream) {
+  if (height <= 2 * kSsimR || width <= 2 * kSsimR || raw_image == nullptr || target == nullptr ||
+      grad_raw == nullptr || sums == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (!(ssim_lambda >= 0.0f && ssim_lambda <= 1.0f)) return GS_ERR_INVALID_ARGUMENT;
+  if (scratch == nullptr || scratch_bytes < gs_ssim_scratch_bytes(3, height, width))
+    return GS_ERR_CAPACITY;
+  if (!ssim_grid_ok(3, height, width)) return GS_ERR_CAPACITY;
+  int rc = ensure_window();
+  if (rc) return rc;
+  const int planes = 3;
+  const int64_t plane_px = (int64_t)height * width;
+  const int64_t numel = 3 * plane_px;
+  const float wscale = (float)(-(double)ssim_lambda / (double)ssim_count(3, height, width, 1));
+  const float l1_weight = 1.0f - ssim_lambda;
+  const float inv_numel = (float)(1.0 / (double)numel);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float *m0 = scratch, *m1 = scratch + planes * plane_px, *m2 = scratch + 2 * planes * plane_px;
+  const dim3 grid = ssim_grid(planes, height, width);
+  if (target_is_u8) {
+    SsimSrc<true, uint8_t> src{raw_image, reinterpret_cast<const uint8_t *>(target), 3, height,
+                               width};
+    ssim_fwd_kernel<true, uint8_t><<<grid, kSsimThreads, 0, st>>>(src, planes, 1, wscale, m0, m1,
+                                                                  m2, sums + 1);
+    ssim_bwd_kernel<true, uint8_t, true><<<grid, kSsimThreads, 0, st>>>(
+        src, planes, m0, m1, m2, nullptr, l1_weight, inv_numel, grad_raw, sums);
+  } else {
+    SsimSrc<true, float> src{raw_image, reinterpret_cast<const float *>(target), 3, height, width};
+    ssim_fwd_kernel<true, float><<<grid, kSsimThreads, 0, st>>>(src, planes, 1, wscale, m0, m1, m2,
+                                                                sums + 1);
+    ssim_bwd_kernel<true, float, true><<<grid, kSsimThreads, 0, st>>>(
+        src, planes, m0, m1, m2, nullptr, l1_weight, inv_numel, grad_raw, sums);
+  }
+  count_launch();
+  count_launch();
+  return launch_status();
+}

@@ -12,7 +12,9 @@ views sharded across ranks:
 * every view's preprocess is queued before one host synchronisation that
   reads all the views' pair counts (the reference synchronises once per
   view, rasterizer.cpp:322);
-* the clamp*255 of render() and the L1 loss with its gradient in one kernel;
+* the clamp*255 of render() and the loss with its gradient in one kernel
+  (L1, or with ssim_lambda > 0 the reference's (1 - lambda) L1 +
+  lambda (1 - SSIM) of scripts/train.py:186-203, in two kernels);
 * each view's raw-parameter gradients added straight into the flat gradient
   buffer by the preprocess backward (TMA bulk reduce-add), so neither
   autograd nor a per-view gradient copy is involved;
@@ -41,8 +43,12 @@ class NativeTrainer:
     opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
-                 **render_opts):
+                 ssim_lambda: float = 0.0, **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs)
+        if not 0.0 <= float(ssim_lambda) <= 1.0:
+            raise ValueError("ssim_lambda must lie in [0, 1]")
+        self.ssim_lambda = float(ssim_lambda)
+        self._ssim_scratch = None
         self.device = self.fp.device
         if self.device.type != "cuda":
             raise RuntimeError("NativeTrainer needs the parameters on a CUDA device")
@@ -117,8 +123,9 @@ class NativeTrainer:
         return views
 
     def loss_and_backward(self, views, targets, accumulate=False):
-        """L1 loss of every view against its target (H, W, 3; float in
-        [0, 255] or uint8) and the backward into the flat gradient buffer.
+        """Loss of every view against its target (H, W, 3; float in [0, 255]
+        or uint8) -- L1, or (1 - ssim_lambda) L1 + ssim_lambda (1 - SSIM)
+        when ssim_lambda > 0 -- and the backward into the flat gradient buffer.
         The first view's gradients overwrite the buffer (every element is
         written, zeros for Gaussians it culled) unless `accumulate`; later
         views add to it. Returns the per-view losses (device tensor)."""
@@ -128,8 +135,12 @@ class NativeTrainer:
         n, W, H = self.n, self.width, self.height
         npx = H * W * 3
         V = len(views)
-        loss_sums = torch.zeros(V, dtype=torch.float64, device=dev)
+        lam = self.ssim_lambda
+        loss_sums = torch.zeros((V, 2), dtype=torch.float64, device=dev)
         grad_img = torch.empty((H, W, 3), device=dev, dtype=torch.float32)
+        if lam > 0 and self._ssim_scratch is None:
+            self._ssim_scratch = torch.empty(nat.query("gs_ssim_scratch_bytes", 3, H, W) // 4,
+                                             device=dev, dtype=torch.float32)
         g_points = torch.empty((n, 2), device=dev, dtype=torch.float32)
         g_splat = torch.empty((n, 8), device=dev, dtype=torch.float32)
         for v, s in enumerate(views):
@@ -138,9 +149,15 @@ class NativeTrainer:
                 tgt = tgt.to(dev).contiguous()
             if tgt.dtype not in (torch.uint8, torch.float32):
                 tgt = tgt.float()
-            nat.call("gs_l1_loss_grad", npx, s["image"].data_ptr(), tgt.data_ptr(),
-                     int(tgt.dtype == torch.uint8), grad_img.data_ptr(), loss_sums[v:].data_ptr(),
-                     st)
+            if lam > 0:
+                nat.call("gs_l1_ssim_loss_grad", H, W, s["image"].data_ptr(), tgt.data_ptr(),
+                         int(tgt.dtype == torch.uint8), lam, grad_img.data_ptr(),
+                         loss_sums[v].data_ptr(), self._ssim_scratch.data_ptr(),
+                         self._ssim_scratch.numel() * 4, st)
+            else:
+                nat.call("gs_l1_loss_grad", npx, s["image"].data_ptr(), tgt.data_ptr(),
+                         int(tgt.dtype == torch.uint8), grad_img.data_ptr(),
+                         loss_sums[v].data_ptr(), st)
             g_points.zero_()
             g_splat.zero_()
             nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
@@ -158,7 +175,11 @@ class NativeTrainer:
                      self._gptr("means"), self._gptr("scales"), self._gptr("quaternions"),
                      self._gptr("opacities"), self._gptr("sh_coeffs_dc"),
                      self._gptr("sh_coeffs_rest"), st)
-        return loss_sums / npx
+        l1 = loss_sums[:, 0] / npx
+        if lam == 0:
+            return l1
+        ssim = loss_sums[:, 1] / (3 * (H - 10) * (W - 10))
+        return (1 - lam) * l1 + lam * (1 - ssim)
 
     def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True):
         """One training step over this rank's views: render, L1 loss,

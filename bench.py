@@ -42,6 +42,7 @@ gs = importlib.import_module("3dgs_from_scratch_b200")
 nat = importlib.import_module("3dgs_from_scratch_b200._native")
 dp = importlib.import_module("3dgs_from_scratch_b200.dp")
 trainer_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
+gs_ssim = importlib.import_module("3dgs_from_scratch_b200.ssim")
 scenes = gs.scenes
 
 METRIC = "fwd+bwd ms/view (1M SH3 Gauss, 1080p); train views/s at 1/2/4/8 B200"
@@ -69,7 +70,13 @@ def parse():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--views-per-rank", type=int, default=4)
+    p.add_argument("--views-per-rank", type=int, default=None,
+                   help="views each rank renders per step (weak scaling; default 4)")
+    p.add_argument("--global-views", type=int, default=None,
+                   help="views per step over all ranks, sharded (strong scaling); "
+                        "config 2 defaults to its batch of 32")
+    p.add_argument("--ssim-lambda", type=float, default=None,
+                   help="loss = (1 - l) L1 + l (1 - SSIM); default 0.2 for config 2, else 0")
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--n", type=int, default=None, help="override Gaussian count (tests/profiling)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -224,9 +231,11 @@ def max_over_ranks(x, world):
 # CPU leg: the oracle port (the reference's algorithm restated in C)
 # ---------------------------------------------------------------------------
 
-def cpu_fwd_bwd_views(cfg, raw_np, views, targets):
+def cpu_fwd_bwd_views(cfg, raw_np, views, targets, ssim_lambda=0.0):
     from oracle import oracle as orc
+    from oracle import ssim_oracle
 
+    ssim_oracle.set_separable(True)
     a = raw_np
     K = scenes.intrinsic_for(cfg).numpy()
     t0 = time.perf_counter()
@@ -234,7 +243,11 @@ def cpu_fwd_bwd_views(cfg, raw_np, views, targets):
         img, st = orc.render_forward(w2c, K, cfg.width, cfg.height, a["means"], a["scales"],
                                      a["quaternions"], a["opacities"], a["sh_coeffs_dc"],
                                      a["sh_coeffs_rest"])
-        g = (np.sign(img - tgt) / img.size).astype(np.float32)
+        if ssim_lambda > 0:  # image is clamp(raw) * 255: the loss's clamp is then the identity
+            _, g = ssim_oracle.l1_ssim_loss(img / 255.0, tgt, ssim_lambda)
+            g = (g / 255.0).astype(np.float32)
+        else:
+            g = (np.sign(img - tgt) / img.size).astype(np.float32)
         orc.render_backward(g, st, w2c, K, cfg.width, cfg.height, a["means"], a["scales"],
                             a["quaternions"], a["opacities"], a["sh_coeffs_dc"],
                             a["sh_coeffs_rest"])
@@ -268,10 +281,11 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     cfg = scenes.CONFIGS[args.config]
+    _, _, lam = view_plan(args, 1, 0)
     act, cams, tg, threads = cpu_setup(cfg, args.n, 1)
     for _ in range(args.warmup):
-        cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1])
-    times = [cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1]) for _ in range(args.steps)]
+        cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1], lam)
+    times = [cpu_fwd_bwd_views(cfg, act, cams[:1], tg[:1], lam) for _ in range(args.steps)]
     sec = statistics.median(times)
     value = 1.0 / sec
     sample = (f"1 full view per step (N={act['means'].shape[0]}, {cfg.width}x{cfg.height}), "
@@ -280,7 +294,7 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "views/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sec * 1000.0, "ms_per_view": sec * 1000.0, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, cfg, 1),
         "cpu_baseline": {"value": value, "unit": "views/s", "cores": threads, "kind": "port",
                          "sample": sample, "cpu": cpu_model()},
@@ -290,13 +304,40 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def view_plan(args, world, rank):
+    """(views per step over all ranks, this rank's views, SSIM lambda).
+    Config 2 is a fixed batch of 32 views sharded over the ranks (strong
+    scaling) with the L1 + 0.2 (1 - SSIM) loss; the others render
+    --views-per-rank views on every rank (weak scaling) with L1."""
+    gv = args.global_views
+    if gv is None and args.config == 2 and args.views_per_rank is None:
+        gv = 32
+    if gv is not None:
+        total = int(gv)
+        if total < world:
+            raise SystemExit("--global-views must be at least the number of ranks")
+    else:
+        total = (args.views_per_rank or 4) * world
+    args.global_views_resolved = total
+    args.strong = gv is not None
+    lam = args.ssim_lambda
+    if lam is None:
+        lam = 0.2 if args.config == 2 else 0.0
+    args.ssim_lambda_resolved = float(lam)
+    return total, len(dp.shard_views(total, rank, world)), float(lam)
+
+
 def workload_config(args, cfg, views_per_rank):
+    lam = getattr(args, "ssim_lambda_resolved", 0.0)
+    loss = f"{1 - lam:g} L1 + {lam:g} (1 - SSIM valid)" if lam > 0 else "L1"
     what = ("forward-only rendering to uint8 frames, replicas (no communication)"
-            if getattr(args, "mode", "train") == "render" else "L1 vs uniform target, Adam step")
+            if getattr(args, "mode", "train") == "render"
+            else f"{loss} vs uniform target, Adam step")
+    total = getattr(args, "global_views_resolved", views_per_rank * max(args.gpus, 1))
     return {"workload": f"config {args.config}: {cfg.n if args.n is None else args.n} SH3 "
                         f"Gaussians, {cfg.width}x{cfg.height}, {views_per_rank} view(s)/rank per "
                         f"step, orbit r={cfg.camera_distance}, {what}",
-            "global_batch": views_per_rank * max(args.gpus, 1), "views_per_rank": views_per_rank,
+            "global_batch": total, "views_per_rank": views_per_rank,
             "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
             "optimizer": "Adam, six groups in one flat buffer, one native launch",
@@ -308,15 +349,17 @@ def workload_config(args, cfg, views_per_rank):
 # ---------------------------------------------------------------------------
 
 class Trainer:
-    def __init__(self, cfg, n, views, world, rank, device):
+    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0):
         self.cfg = cfg
         self.world = world
         self.device = device
+        self.ssim_lambda = float(ssim_lambda)
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
         self.fp = dp.FlatParams(raw)  # replicas: identical on every rank
         self.params = self.fp.params
-        cams = scenes.orbit_cameras(cfg, views * world)
-        mine = dp.shard_views(views * world, rank, world)
+        cams = scenes.orbit_cameras(cfg, total_views)
+        mine = dp.shard_views(total_views, rank, world)
+        views = len(mine)
         self.cams = cams[mine].to(device)
         self.K = scenes.intrinsic_for(cfg).to(device)
         g = torch.Generator(device=device).manual_seed(1234 + rank)
@@ -342,7 +385,13 @@ class Trainer:
             img, pts, radii = gs.render(w2c, K, self.cfg.width, self.cfg.height, act["means"],
                                         act["scales"], act["quaternions"], act["opacities"],
                                         act["sh_coeffs_dc"], act["sh_coeffs_rest"])
-            losses.append(torch.nn.functional.l1_loss(img / 255.0, tgt / 255.0))
+            rn, tn = img / 255.0, tgt / 255.0
+            loss = torch.nn.functional.l1_loss(rn, tn)
+            if self.ssim_lambda > 0:  # scripts/train.py:193-203
+                ss = gs_ssim.fused_ssim(rn.permute(2, 0, 1).unsqueeze(0),
+                                        tn.permute(2, 0, 1).unsqueeze(0), padding="valid")
+                loss = (1 - self.ssim_lambda) * loss + self.ssim_lambda * (1 - ss)
+            losses.append(loss)
         # one backward per step: the views' gradients meet at the activated
         # parameters, so the activation backward runs once
         torch.stack(losses).sum().backward()
@@ -358,16 +407,17 @@ class Trainer:
 class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
-    def __init__(self, cfg, n, views, world, rank, device):
+    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0):
         self.cfg = cfg
         self.world = world
         self.device = device
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
-        self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height)
+        self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda)
         self.fp = self.nt.fp
         self.params = self.fp.params
-        cams = scenes.orbit_cameras(cfg, views * world)
-        mine = dp.shard_views(views * world, rank, world)
+        cams = scenes.orbit_cameras(cfg, total_views)
+        mine = dp.shard_views(total_views, rank, world)
+        views = len(mine)
         self.cams = cams[mine].to(device)
         self.K = scenes.intrinsic_for(cfg).to(device)
         g = torch.Generator(device=device).manual_seed(1234 + rank)
@@ -455,9 +505,9 @@ def main():
         return
     device = torch.device("cuda", local)
     cfg = scenes.CONFIGS[args.config]
-    V = args.views_per_rank
-    tr = (NativeBenchTrainer if args.trainer == "native" else Trainer)(cfg, args.n, V, world, rank,
-                                                                        device)
+    total_views, V, lam = view_plan(args, world, rank)
+    tr = (NativeBenchTrainer if args.trainer == "native" else Trainer)(
+        cfg, args.n, total_views, world, rank, device, ssim_lambda=lam)
     n = tr.params["means"].shape[0]
     render_mode = args.mode == "render"
     if render_mode and args.trainer != "native":
@@ -486,7 +536,7 @@ def main():
     launches = nat.launch_count() - launches0
     ms_total = max_over_ranks(start.elapsed_time(end), world)
     ms_step = ms_total / args.steps
-    value = world * V * args.steps / (ms_total / 1000.0)
+    value = total_views * args.steps / (ms_total / 1000.0)
     unit = "frames/s" if render_mode else "views/s"
     stage_ms = stages.mean_ms()
 
@@ -508,7 +558,7 @@ def main():
         else:
             h2d = sum(t.numel() for t in tr.host_targets) + V * (16 + 9) * 4
             d2h = V * 8
-        e2e = {"value": world * V * args.steps / sec, "unit": unit,
+        e2e = {"value": total_views * args.steps / sec, "unit": unit,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "timing": "wall clock, max over ranks"}
 
@@ -556,7 +606,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not render_mode:
         act, cams, tg, threads = cpu_setup(cfg, args.n, args.cpu_sample_views)
-        sec = cpu_fwd_bwd_views(cfg, act, cams, tg)
+        sec = cpu_fwd_bwd_views(cfg, act, cams, tg, lam)
         cpu = {"value": args.cpu_sample_views / sec, "unit": "views/s", "cores": threads,
                "kind": "port",
                "sample": f"{args.cpu_sample_views} full views fwd+bwd of the same scene "
@@ -567,7 +617,8 @@ def main():
             "metric": METRIC if not render_mode else "inference frames/s (config 4)",
             "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "ms_per_view": ms_step / V, "higher_is_better": True, "scaling": "weak",
+            "ms_per_view": ms_step / V, "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak",
             "mode": args.mode,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, cfg, V), "e2e": e2e, "gpu_launches": int(launches),

@@ -264,6 +264,42 @@ GS_API int gs_adam_step(int64_t n, float *params, const float *grads, float *exp
 GS_API int gs_l1_loss_grad(int64_t n, const float *raw_image, const void *target,
                            int target_is_u8, float *grad_raw, double *loss_sum, void *stream);
 
+/* ---- SSIM and the L1 + SSIM training loss ------------------------------
+ * No counterpart in the reference's native module: the reference calls the
+ * external fused_ssim package (scripts/train.py:193-197, evaluate.py:57-61).
+ * SSIM with the 11x11 Gaussian window (sigma 1.5), C1 = 0.01^2,
+ * C2 = 0.03^2, zero padding; valid = 1 averages only over the pixels at
+ * least 5 from every border (fused_ssim's padding="valid"). */
+
+/* Scratch for gs_ssim_forward / gs_ssim_backward / gs_l1_ssim_loss_grad
+ * (planes = 3 for the loss): three fp32 maps of planes * height * width. */
+GS_API size_t gs_ssim_scratch_bytes(int planes, int height, int width);
+
+/* SSIM of planar fp32 images (planes = N * C, each height x width): adds the
+ * sum of the SSIM map over the counted pixels into *ssim_sum (device double;
+ * divide by planes * H * W, or planes * (H - 10) * (W - 10) when valid),
+ * and keeps in scratch what gs_ssim_backward needs. */
+GS_API int gs_ssim_forward(int planes, int height, int width, const float *img1,
+                           const float *img2, int valid, float *scratch, size_t scratch_bytes,
+                           double *ssim_sum, void *stream);
+
+/* d mean-SSIM / d img1, times *grad_out (a device float; NULL means 1), from
+ * the scratch a gs_ssim_forward on the same images filled. */
+GS_API int gs_ssim_backward(int planes, int height, int width, const float *img1,
+                            const float *img2, const float *scratch, const float *grad_out,
+                            float *grad_img1, void *stream);
+
+/* The reference's training loss on one raw blended (height, width, 3) image
+ * (scripts/train.py:183-203): rendered = clamp(raw, 0, 1) * 255 / 255,
+ * target / 255, loss = (1 - lambda) * L1 + lambda * (1 - SSIM_valid).
+ * Adds sum |rendered - target| into sums[0] and the sum of the valid SSIM map
+ * into sums[1] (device doubles), and writes d loss / d raw into grad_raw.
+ * height and width must exceed 10. */
+GS_API int gs_l1_ssim_loss_grad(int height, int width, const float *raw_image,
+                                const void *target, int target_is_u8, float ssim_lambda,
+                                float *grad_raw, double *sums, float *scratch,
+                                size_t scratch_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_close_metric, golden, metric
+from conftest import assert_close_metric, golden, metric, torch_ssim
 
 pytestmark = pytest.mark.gpu
 
@@ -492,11 +492,12 @@ def test_flat_adam_matches_torch_adam(gs):
         torch.testing.assert_close(fp[k].detach(), ref[k].detach(), rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("u8", [False, True])
-def test_native_trainer_step_matches_autograd_path(gs, u8):
-    """One NativeTrainer step (fused activations, fused L1 loss, gradients
+@pytest.mark.parametrize("u8,lam", [(False, 0.0), (True, 0.0), (True, 0.2), (False, 1.0)])
+def test_native_trainer_step_matches_autograd_path(gs, u8, lam):
+    """One NativeTrainer step (fused activations, fused loss, gradients
     accumulated in the flat buffer) against render() + Torch activations +
-    torch l1_loss + autograd, on two views."""
+    the reference's loss expression (scripts/train.py:186-203, SSIM as a
+    Torch conv2d restatement) + autograd, on two views."""
     tr_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
     W, H, f = 160, 120, 170.0
     cfg = gs.scenes.CONFIGS[0]
@@ -517,16 +518,22 @@ def test_native_trainer_step_matches_autograd_path(gs, u8):
                               act["quaternions"], act["opacities"], act["sh_coeffs_dc"],
                               act["sh_coeffs_rest"])
         imgs.append(img.detach())
-        losses.append(torch.nn.functional.l1_loss(img / 255.0, targets[v].to(DEV).float() / 255.0))
+        rn, tn = img / 255.0, targets[v].to(DEV).float() / 255.0
+        loss = torch.nn.functional.l1_loss(rn, tn)
+        if lam > 0:
+            ss = torch_ssim(rn.permute(2, 0, 1).unsqueeze(0), tn.permute(2, 0, 1).unsqueeze(0),
+                            True)
+            loss = (1 - lam) * loss + lam * (1 - ss)
+        losses.append(loss)
     torch.stack(losses).sum().backward()
     # native path
-    tr = tr_mod.NativeTrainer({k: v.to(DEV) for k, v in raw.items()}, W, H)
+    tr = tr_mod.NativeTrainer({k: v.to(DEV) for k, v in raw.items()}, W, H, ssim_lambda=lam)
     views = tr.forward_views(w2cs, K)
     nl = tr.loss_and_backward(views, [t.to(DEV) for t in targets])
     for v in range(2):
         native_img = views[v]["image"].clamp(0, 1) * 255
         assert float((native_img - imgs[v]).abs().max()) / 255.0 < 1e-4
-    torch.testing.assert_close(nl.float(), torch.stack(losses).detach(), rtol=1e-5, atol=1e-7)
+    torch.testing.assert_close(nl.float(), torch.stack(losses).detach(), rtol=1e-5, atol=2e-7)
     for k in p:
         a, n = tr.fp.spans[k]
         assert_close_metric(k, np_(tr.fp.grad[a:a + n]), np_(p[k].grad).ravel(), 0.9999, 1e-3)
