@@ -141,7 +141,7 @@ __device__ __forceinline__ void fwd_step(FwdPx &p, const float4 &g0, const float
 // Forward blend. With ACCUM = false only the transmittance bookkeeping is
 // done (the replay used by the reference-API backward).
 template <bool PACKED, bool ACCUM>
-__global__ void __launch_bounds__(kBlendThreads) blend_forward_kernel(
+__global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
     int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
     const int32_t *__restrict__ ids, int n, const float2 *__restrict__ points,
     const float4 *__restrict__ splat, const float *__restrict__ conic,
@@ -256,9 +256,22 @@ struct BwdPx {
 };
 
 // One list entry for one pixel, back to front (kernel.cu:1068-1109). Adds the
-// pixel's 9 gradient terms into acc; returns whether it contributed. The two
-// divisions of the reference (kernel.cu:1088,1094) become one correctly
-// rounded reciprocal and two products.
+// pixel's gradient terms into acc and returns whether it contributed. The
+// terms that are a per-Gaussian constant times a per-pixel quantity are
+// summed without the constant, which is applied once per (tile, Gaussian) in
+// the flush: acc[0..4] = sum of du*ag, dv*ag, du*du*ag, du*dv*ag, dv*dv*ag
+// (ag = alpha * dL/dalpha), from which d(u,v) = conic * (acc0, acc1) and
+// d conic = (-acc2 / 2, -acc3, -acc4 / 2). The skip decisions (chi-square
+// cut, alpha threshold) use the forward's expressions operation for
+// operation; the two divisions by (1 - alpha) of the reference
+// (kernel.cu:1088,1094) become one approximate reciprocal (rcp.approx, at
+// most 1 ulp) and two products.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float4 &g1, float c2,
                                          float alpha_thr, float chi_thr, float acc[9]) {
   const float du = p.fu - g0.x;
@@ -270,24 +283,23 @@ __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float
   float alpha = density * g1.y;
   if (alpha < alpha_thr) return false;
   float one_minus_alpha = 1.0f - alpha + kTransEps;
-  float rcp = __frcp_rn(one_minus_alpha);
+  float rcp = rcp_approx(one_minus_alpha);
   float prefix_t = p.Ta * rcp;
   float weight = alpha * prefix_t;
   const float c0 = g1.z, c1 = g1.w;
   float grad_rgb = p.gr * c0 + p.gg * c1 + p.gb * c2;
   float grad_alpha = prefix_t * grad_rgb - p.suffix * rcp;
-  float grad_u = inv00 * du + inv01 * dv;
-  float grad_v = inv01 * du + inv11 * dv;
   float ag = alpha * grad_alpha;
-  acc[0] += grad_u * ag;
-  acc[1] += grad_v * ag;
-  acc[2] += -0.5f * du * du * ag;
-  acc[3] += -du * dv * ag;
-  acc[4] += -0.5f * dv * dv * ag;
-  acc[5] += density * grad_alpha;
-  acc[6] += weight * p.gr;
-  acc[7] += weight * p.gg;
-  acc[8] += weight * p.gb;
+  const float au = du * ag, av = dv * ag;
+  acc[0] += au;
+  acc[1] += av;
+  acc[2] = fmaf(au, du, acc[2]);
+  acc[3] = fmaf(au, dv, acc[3]);
+  acc[4] = fmaf(av, dv, acc[4]);
+  acc[5] = fmaf(density, grad_alpha, acc[5]);
+  acc[6] = fmaf(weight, p.gr, acc[6]);
+  acc[7] = fmaf(weight, p.gg, acc[7]);
+  acc[8] = fmaf(weight, p.gb, acc[8]);
   p.suffix += weight * grad_rgb;
   p.Ta = prefix_t;
   return true;
@@ -407,6 +419,16 @@ __global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(
         float a[9];
 #pragma unroll
         for (int q = 0; q < 9; ++q) a[q] = s_acc[slot * 9 + q];
+        {  // apply the per-Gaussian constants factored out of bwd_step's sums
+          const float4 g0 = s_g0[slot];
+          const float inv00 = g0.z, inv01 = g0.w, inv11 = s_g1[slot].x;
+          const float su = a[0], sv = a[1];
+          a[0] = inv00 * su + inv01 * sv;
+          a[1] = inv01 * su + inv11 * sv;
+          a[2] = -0.5f * a[2];
+          a[3] = -a[3];
+          a[4] = -0.5f * a[4];
+        }
         if (a[0] != 0.f || a[1] != 0.f)
           atomicAdd(reinterpret_cast<float2 *>(g_points) + id, make_float2(a[0], a[1]));
         if (PACKED) {
