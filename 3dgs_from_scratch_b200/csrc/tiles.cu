@@ -285,6 +285,8 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
 
   // Stable warp-local ranks: running per-warp digit counts in shared memory.
   uint32_t rank[ITEMS];
+  uint32_t lead_old[ITEMS];
+  uint8_t leader_of[ITEMS];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
   for (int k = 0; k < ITEMS; ++k) {
@@ -293,15 +295,18 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
     const uint32_t d = valid ? digit_of(key[k], shift, dmask) : 0x100u;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const uint32_t leader = 31 - __clz(peers);
+    // One shared-memory atomic per digit group: the returned count is only
+    // needed in the scatter below, so the ITEMS atomics of a thread are
+    // independent instructions that pipeline (a load/store pair per item
+    // would serialise on the possible aliasing of consecutive items).
     uint32_t old = 0;
-    if (valid && lane == leader) {
-      old = S.whist[warp][d];
-      S.whist[warp][d] = old + (uint32_t)__popc(peers);
-    }
-    old = __shfl_sync(0xffffffffu, old, leader);
-    rank[k] = old + (uint32_t)__popc(peers & lt_mask);
-    __syncwarp();
+    if (valid && lane == leader) old = atomicAdd(&S.whist[warp][d], (uint32_t)__popc(peers));
+    rank[k] = (uint32_t)__popc(peers & lt_mask);
+    lead_old[k] = old;
+    leader_of[k] = (uint8_t)leader;
   }
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) rank[k] += __shfl_sync(0xffffffffu, lead_old[k], leader_of[k]);
   __syncthreads();
 
   // Thread t owns digit t: warp offsets, block count, look-back.
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
   }
   const uint32_t gdig = block_scan_256(hist[d], S.tmp);
   const uint32_t ldig = block_scan_256(cnt, S.tmp);
-  S.gbase[d] = gdig + excl;
+  S.gbase[d] = gdig + excl - ldig;  // output index = gbase[digit] + position in the tile
   S.lstart[d] = ldig;
   __syncthreads();
 
@@ -374,13 +379,16 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
 
   const int64_t tile_base = (int64_t)tile * kTileItems;
   const int valid_count = (int)min((int64_t)kTileItems, n - tile_base);
-  for (int p = t; p < valid_count; p += kSortThreads) {
-    const KT kk = S.keys[p];
-    const uint32_t dk = digit_of(kk, shift, dmask);
-    const uint32_t out = S.gbase[dk] + ((uint32_t)p - S.lstart[dk]);
-    if ((int64_t)out < n) {  // always true unless a look-back gave up
-      keys_out[out] = kk;
-      vals_out[out] = S.vals[p];
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    const int p = t + k * kSortThreads;
+    if (p < valid_count) {
+      const KT kk = S.keys[p];
+      const uint32_t out = S.gbase[digit_of(kk, shift, dmask)] + (uint32_t)p;
+      if ((int64_t)out < n) {  // always true unless a look-back gave up
+        keys_out[out] = kk;
+        vals_out[out] = S.vals[p];
+      }
     }
   }
 }
