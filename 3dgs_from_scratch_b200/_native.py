@@ -62,6 +62,10 @@ SIGNATURES = {
     "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
     "gs_ssim_scratch_bytes": (SZ, [I, I, I]),
+    "gs_dp_flag_words": (SZ, [I]),
+    "gs_dp_max_blocks": (I, []),
+    "gs_dp_adam_step": (I, [I, I, P, P, P, P, P, I64, P, P, I, P, P, P, F, F, I64, ctypes.c_uint32,
+                            I, P, P]),
     "gs_ssim_forward": (I, [I, I, I, P, P, I, P, SZ, P, P]),
     "gs_ssim_backward": (I, [I, I, I, P, P, P, P, P, P]),
     "gs_l1_ssim_loss_grad": (I, [I, I, P, P, I, F, P, P, P, SZ, P]),

@@ -11,48 +11,48 @@
 // torch.optim.Adam's default (non-amsgrad, no weight decay) update:
 //   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2
 //   p -= lr / (1 - b1^t) * m / (sqrt(v) / sqrt(1 - b2^t) + eps)
-#include "gs_common.cuh"
+#include "adam.cuh"
 
 namespace gs {
-
-constexpr int kAdamMaxGroups = 8;
-
-struct AdamGroups {
-  int64_t end[kAdamMaxGroups];  // exclusive end (in elements) of each group, multiples of 4
-  float step_size[kAdamMaxGroups];   // lr / (1 - b1^t)
-  float inv_bc2_sqrt[kAdamMaxGroups];  // 1 / sqrt(1 - b2^t)
-  float eps[kAdamMaxGroups];
-  int count;
-};
-
-__device__ __forceinline__ float adam_one(float &p, float g, float &m, float &v, float b1,
-                                          float b2, float step, float ibc2, float eps) {
-  m = b1 * m + (1.0f - b1) * g;
-  v = b2 * v + (1.0f - b2) * g * g;
-  const float denom = sqrtf(v) * ibc2 + eps;
-  p = p - step * (m / denom);
-  return p;
-}
 
 __global__ void __launch_bounds__(256) adam_kernel(float4 *__restrict__ p, const float4 *__restrict__ g,
                                                    float4 *__restrict__ m, float4 *__restrict__ v,
                                                    int64_t n4, AdamGroups G, float b1, float b2) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-    const int64_t e = 4 * i;
-    int grp = 0;
-#pragma unroll
-    for (int k = 0; k < kAdamMaxGroups - 1; ++k) grp += (k < G.count - 1 && e >= G.end[k]) ? 1 : 0;
-    const float st = G.step_size[grp], ib = G.inv_bc2_sqrt[grp], ep = G.eps[grp];
     float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
-    adam_one(pp.x, gg.x, mm.x, vv.x, b1, b2, st, ib, ep);
-    adam_one(pp.y, gg.y, mm.y, vv.y, b1, b2, st, ib, ep);
-    adam_one(pp.z, gg.z, mm.z, vv.z, b1, b2, st, ib, ep);
-    adam_one(pp.w, gg.w, mm.w, vv.w, b1, b2, st, ib, ep);
+    adam_float4(G, 4 * i, pp, gg, mm, vv, b1, b2);
     p[i] = pp;
     m[i] = mm;
     v[i] = vv;
   }
+}
+
+int build_adam_groups(int64_t n, int num_groups, const int64_t *group_ends, const float *lrs,
+                      const float *eps, float beta1, float beta2, int64_t step, AdamGroups *G) {
+  if (num_groups < 1 || num_groups > kAdamMaxGroups || step < 1 || group_ends == nullptr ||
+      lrs == nullptr || eps == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  G->count = num_groups;
+  const double bc1 = 1.0 - pow((double)beta1, (double)step);
+  const double bc2 = 1.0 - pow((double)beta2, (double)step);
+  int64_t prev = 0;
+  for (int k = 0; k < kAdamMaxGroups; ++k) {
+    if (k < num_groups) {
+      if (group_ends[k] < prev || (group_ends[k] & 3)) return GS_ERR_INVALID_ARGUMENT;
+      prev = group_ends[k];
+      G->end[k] = group_ends[k];
+      G->step_size[k] = (float)((double)lrs[k] / bc1);
+      G->inv_bc2_sqrt[k] = (float)(1.0 / sqrt(bc2));
+      G->eps[k] = eps[k];
+    } else {
+      G->end[k] = n;
+      G->step_size[k] = 0.f;
+      G->inv_bc2_sqrt[k] = 1.f;
+      G->eps[k] = 1.f;
+    }
+  }
+  return prev == n ? GS_OK : GS_ERR_INVALID_ARGUMENT;
 }
 
 }  // namespace gs
@@ -69,26 +69,8 @@ extern "C" int gs_adam_step(int64_t n, float *params, const float *grads, float 
     return GS_ERR_INVALID_ARGUMENT;
   if (n == 0) return GS_OK;
   AdamGroups G;
-  G.count = num_groups;
-  const double bc1 = 1.0 - pow((double)beta1, (double)step);
-  const double bc2 = 1.0 - pow((double)beta2, (double)step);
-  int64_t prev = 0;
-  for (int k = 0; k < kAdamMaxGroups; ++k) {
-    if (k < num_groups) {
-      if (group_ends[k] < prev || (group_ends[k] & 3)) return GS_ERR_INVALID_ARGUMENT;
-      prev = group_ends[k];
-      G.end[k] = group_ends[k];
-      G.step_size[k] = (float)((double)lrs[k] / bc1);
-      G.inv_bc2_sqrt[k] = (float)(1.0 / sqrt(bc2));
-      G.eps[k] = eps[k];
-    } else {
-      G.end[k] = n;
-      G.step_size[k] = 0.f;
-      G.inv_bc2_sqrt[k] = 1.f;
-      G.eps[k] = 1.f;
-    }
-  }
-  if (prev != n) return GS_ERR_INVALID_ARGUMENT;
+  const int rc = build_adam_groups(n, num_groups, group_ends, lrs, eps, beta1, beta2, step, &G);
+  if (rc) return rc;
   const int64_t n4 = n / 4;
   int dev = 0;
   cudaGetDevice(&dev);

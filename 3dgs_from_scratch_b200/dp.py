@@ -40,10 +40,20 @@ def shard_views(num_views: int, rank: int, world: int) -> list[int]:
 class FlatParams:
     """Gaussian parameters as views into one flat buffer, with a matching flat
     gradient buffer (each parameter's .grad is a view of it, so autograd
-    accumulates in place) and flat Adam state."""
+    accumulates in place) and flat Adam state.
+
+    With `fused_dp` set and a process group of world > 1 on CUDA, the two
+    flat buffers live in symmetric memory (every rank can address every
+    other rank's buffers, and the NVSwitch multicast mapping is used when
+    the system has one) and `step()` runs the fused data-parallel optimizer
+    step (gs_dp_adam_step: reduce-scatter of the gradient, Adam on this
+    rank's 1/world shard, all-gather of the parameters, in one kernel);
+    each rank then keeps only its shard of the Adam moments. fused_dp is
+    "auto" (multicast when available, else peer loads and stores), "p2p"
+    (always peer loads and stores) or False (NCCL all-reduce + full Adam)."""
 
     def __init__(self, tensors: dict, lrs: dict | None = None, eps: float = 1e-15,
-                 betas=(0.9, 0.999)):
+                 betas=(0.9, 0.999), group=None, fused_dp=False):
         first = tensors[GROUPS[0]]
         self.device = first.device
         self.shapes = {k: tuple(tensors[k].shape) for k in GROUPS}
@@ -54,9 +64,20 @@ class FlatParams:
             self.spans[k] = (off, n)
             off += (n + 3) // 4 * 4
         self.numel = off
+        self.group = group
+        self.world, self.rank = _world_rank(group)
+        self.fused = bool(fused_dp) and self.world > 1 and self.device.type == "cuda"
+        if fused_dp and fused_dp not in (True, "auto", "p2p"):
+            raise ValueError("fused_dp must be False, True, 'auto' or 'p2p'")
+        self._force_p2p = fused_dp == "p2p"
         f = dict(device=self.device, dtype=torch.float32)
-        self.data = torch.zeros(off, **f)
-        self.grad = torch.zeros(off, **f)
+        if self.fused:
+            self.padded = padded_numel(off, self.world)
+            self._setup_symmetric()
+        else:
+            self.padded = off
+            self.data = torch.zeros(off, **f)
+            self.grad = torch.zeros(off, **f)
         self.params = {}
         for k in GROUPS:
             a, n = self.spans[k]
@@ -70,6 +91,50 @@ class FlatParams:
         self.exp_avg = None
         self.exp_avg_sq = None
         self.step_count = 0
+        self._epoch = 0
+
+    # ---- symmetric-memory set-up (fused data-parallel step) -----------------
+
+    def _setup_symmetric(self):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        gname = (self.group if self.group is not None else dist.group.WORLD).group_name
+        self.data = symm.empty(self.padded, dtype=torch.float32, device=self.device)
+        self.grad = symm.empty(self.padded, dtype=torch.float32, device=self.device)
+        self.data.zero_()
+        self.grad.zero_()
+        self.num_blocks = max(1, min(int(nat.query("gs_dp_max_blocks")),
+                                     -(-self.padded // (self.world * 4 * 512))))
+        words = int(nat.query("gs_dp_flag_words", self.num_blocks))
+        self.flags = symm.empty(words, dtype=torch.int32, device=self.device)
+        self.flags.zero_()
+        torch.cuda.synchronize(self.device)
+        self._h_data = symm.rendezvous(self.data, gname)
+        self._h_grad = symm.rendezvous(self.grad, gname)
+        self._h_flags = symm.rendezvous(self.flags, gname)
+        vp = ctypes.c_void_p * self.world
+        g_ptrs, mc_g = self._peer_ptrs(self.grad, self._h_grad)
+        p_ptrs, mc_p = self._peer_ptrs(self.data, self._h_data)
+        f_ptrs, _ = self._peer_ptrs(self.flags, self._h_flags)
+        self._grad_ptrs, self._param_ptrs, self._flag_ptrs = vp(*g_ptrs), vp(*p_ptrs), vp(*f_ptrs)
+        self.multicast = (not self._force_p2p) and mc_g != 0 and mc_p != 0
+        self._mc = (mc_g, mc_p) if self.multicast else (None, None)
+        dist.barrier(group=self.group)
+
+    def _peer_ptrs(self, t, h):
+        """Every rank's address of tensor t and its multicast address (0 if
+        none), from the rendezvous handle of t. The handle must address t
+        itself on this rank (anything else is refused rather than guessed)."""
+        ptrs = [int(x) for x in h.buffer_ptrs]
+        if len(ptrs) != self.world or ptrs[self.rank] != t.data_ptr():
+            raise RuntimeError("symmetric-memory handle does not address the tensor")
+        if any(x % 16 for x in ptrs):
+            raise RuntimeError("symmetric buffers must be 16-byte aligned")
+        mc = int(getattr(h, "multicast_ptr", 0) or 0)
+        if mc % 16:
+            mc = 0
+        return ptrs, mc
 
     def __getitem__(self, k):
         return self.params[k]
@@ -84,26 +149,77 @@ class FlatParams:
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
             dist.all_reduce(self.grad, op=dist.ReduceOp.SUM, group=group)
 
-    def adam_step(self):
-        """One Adam step over every group with the native one-launch kernel."""
-        if self.device.type != "cuda":
-            raise RuntimeError("adam_step runs on the GPU kernel only")
-        if self.exp_avg is None:
-            self.exp_avg = torch.zeros_like(self.data)
-            self.exp_avg_sq = torch.zeros_like(self.data)
-        self.step_count += 1
-        ends = []
-        lrs = []
+    def _group_table(self):
+        ends, lrs = [], []
         for i, k in enumerate(GROUPS):
-            a, n = self.spans[k]
-            nxt = self.spans[GROUPS[i + 1]][0] if i + 1 < len(GROUPS) else self.numel
+            nxt = self.spans[GROUPS[i + 1]][0] if i + 1 < len(GROUPS) else self.padded
             ends.append(nxt)
             lrs.append(self.lrs[k])
         ends_c = (ctypes.c_int64 * len(GROUPS))(*ends)
         lrs_c = (ctypes.c_float * len(GROUPS))(*lrs)
         eps_c = (ctypes.c_float * len(GROUPS))(*([self.eps] * len(GROUPS)))
-        nat.call("gs_adam_step", self.numel, self.data.data_ptr(), self.grad.data_ptr(),
+        return ends_c, lrs_c, eps_c
+
+    def adam_step(self):
+        """One Adam step over every group with the native one-launch kernel
+        (on this rank's full buffer; the gradient must already be summed)."""
+        if self.device.type != "cuda":
+            raise RuntimeError("adam_step runs on the GPU kernel only")
+        if self.fused:
+            raise RuntimeError("with fused_dp the optimizer runs in step()")
+        if self.exp_avg is None:
+            self.exp_avg = torch.zeros_like(self.data)
+            self.exp_avg_sq = torch.zeros_like(self.data)
+        self.step_count += 1
+        ends_c, lrs_c, eps_c = self._group_table()
+        nat.call("gs_adam_step", self.padded, self.data.data_ptr(), self.grad.data_ptr(),
                  self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), len(GROUPS),
                  ctypes.cast(ends_c, ctypes.c_void_p), ctypes.cast(lrs_c, ctypes.c_void_p),
                  ctypes.cast(eps_c, ctypes.c_void_p), self.betas[0], self.betas[1],
                  self.step_count, nat.stream_ptr(self.device))
+
+    def fused_step(self, grad_shard_out=None):
+        """The fused data-parallel optimizer step (see the class docstring).
+        grad_shard_out, if given, receives this rank's shard of the summed
+        gradient (padded // world floats)."""
+        if not self.fused:
+            raise RuntimeError("fused_step needs fused_dp and world > 1")
+        shard = self.padded // self.world
+        if self.exp_avg is None:
+            self.exp_avg = torch.zeros(shard, device=self.device, dtype=torch.float32)
+            self.exp_avg_sq = torch.zeros(shard, device=self.device, dtype=torch.float32)
+        self.step_count += 1
+        self._epoch = (self._epoch + 1) & 0x7FFFFFFF
+        ends_c, lrs_c, eps_c = self._group_table()
+        out = 0 if grad_shard_out is None else grad_shard_out.data_ptr()
+        nat.call("gs_dp_adam_step", self.world, self.rank, self._grad_ptrs, self._param_ptrs,
+                 self._flag_ptrs, self._mc[0], self._mc[1], self.padded,
+                 self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), len(GROUPS),
+                 ctypes.cast(ends_c, ctypes.c_void_p), ctypes.cast(lrs_c, ctypes.c_void_p),
+                 ctypes.cast(eps_c, ctypes.c_void_p), self.betas[0], self.betas[1],
+                 self.step_count, self._epoch, self.num_blocks, out,
+                 nat.stream_ptr(self.device))
+
+    def step(self):
+        """The step's gradient sum over the ranks and the Adam update: the
+        fused kernel with fused_dp, else NCCL all-reduce + one-launch Adam."""
+        if self.fused:
+            self.fused_step()
+        else:
+            self.allreduce_grads(self.group)
+            self.adam_step()
+
+
+def padded_numel(numel: int, world: int) -> int:
+    """Flat length rounded up so that each of `world` shards is a whole
+    number of float4s (the fused step's unit of work)."""
+    q = 4 * max(int(world), 1)
+    return -(-int(numel) // q) * q
+
+
+def _world_rank(group):
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(group), dist.get_rank(group)
+    return 1, 0

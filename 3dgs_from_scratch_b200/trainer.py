@@ -18,8 +18,10 @@ views sharded across ranks:
 * each view's raw-parameter gradients added straight into the flat gradient
   buffer by the preprocess backward (TMA bulk reduce-add), so neither
   autograd nor a per-view gradient copy is involved;
-* one NCCL all-reduce of the flat gradient (world > 1) and the one-launch
-  Adam of dp.FlatParams.
+* the optimizer step of dp.FlatParams: one NCCL all-reduce of the flat
+  gradient (world > 1) and the one-launch Adam, or with fused_dp one kernel
+  that reduce-scatters the gradient over NVLink / NVSwitch, applies Adam to
+  the rank's shard and all-gathers the parameters.
 
 The renders are the same as render()'s (same kernels); tests compare one step
 of this trainer with the autograd path (render() + Torch activations +
@@ -43,8 +45,8 @@ class NativeTrainer:
     opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
-                 ssim_lambda: float = 0.0, **render_opts):
-        self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs)
+                 ssim_lambda: float = 0.0, group=None, fused_dp=False, **render_opts):
+        self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
         self.ssim_lambda = float(ssim_lambda)
@@ -182,13 +184,14 @@ class NativeTrainer:
         return (1 - lam) * l1 + lam * (1 - ssim)
 
     def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True):
-        """One training step over this rank's views: render, L1 loss,
-        backward (the first view overwrites the flat gradient, so no zeroing
-        is needed between steps), gradient all-reduce (when a process group
-        is initialised with world > 1), Adam. Returns the losses."""
+        """One training step over this rank's views: render, loss, backward
+        (the first view overwrites the flat gradient, so no zeroing is needed
+        between steps), then the gradient sum over the ranks and Adam
+        (FlatParams.step: NCCL all-reduce + one-launch Adam, or with
+        fused_dp the one-kernel reduce-scatter / sharded Adam / all-gather).
+        Returns the losses."""
         views = self.forward_views(world_to_cameras, intrinsics)
         losses = self.loss_and_backward(views, targets)
         if optimizer_step:
-            self.fp.allreduce_grads()
-            self.fp.adam_step()
+            self.fp.step()
         return losses

@@ -75,6 +75,10 @@ def parse():
     p.add_argument("--global-views", type=int, default=None,
                    help="views per step over all ranks, sharded (strong scaling); "
                         "config 2 defaults to its batch of 32")
+    p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="nccl",
+                   help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
+                        "reduce-scatter / sharded Adam / all-gather kernel (multicast when "
+                        "available, or peer stores only)")
     p.add_argument("--ssim-lambda", type=float, default=None,
                    help="loss = (1 - l) L1 + l (1 - SSIM); default 0.2 for config 2, else 0")
     p.add_argument("--config", type=int, default=1)
@@ -338,7 +342,11 @@ def workload_config(args, cfg, views_per_rank):
                         f"Gaussians, {cfg.width}x{cfg.height}, {views_per_rank} view(s)/rank per "
                         f"step, orbit r={cfg.camera_distance}, {what}",
             "global_batch": total, "views_per_rank": views_per_rank,
-            "parallelism": f"dp{max(args.gpus, 1)} (views sharded, NCCL all-reduce of grads)",
+            "parallelism": f"dp{max(args.gpus, 1)} (views sharded; " + (
+                "NCCL all-reduce of grads + Adam)" if getattr(args, "dp", "nccl") == "nccl" else
+                "fused reduce-scatter / sharded Adam / all-gather kernel, "
+                + ("NVSwitch multicast when available)" if args.dp == "fused" else
+                   "peer loads and stores)")),
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
             "optimizer": "Adam, six groups in one flat buffer, one native launch",
             "trainer": args.trainer}
@@ -407,12 +415,14 @@ class Trainer:
 class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
-    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0):
+    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl"):
         self.cfg = cfg
         self.world = world
         self.device = device
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
-        self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda)
+        fused = {"nccl": False, "fused": "auto", "fused-p2p": "p2p"}[dp_mode]
+        self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda,
+                                            fused_dp=fused)
         self.fp = self.nt.fp
         self.params = self.fp.params
         cams = scenes.orbit_cameras(cfg, total_views)
@@ -506,8 +516,13 @@ def main():
     device = torch.device("cuda", local)
     cfg = scenes.CONFIGS[args.config]
     total_views, V, lam = view_plan(args, world, rank)
-    tr = (NativeBenchTrainer if args.trainer == "native" else Trainer)(
-        cfg, args.n, total_views, world, rank, device, ssim_lambda=lam)
+    if args.trainer == "native":
+        tr = NativeBenchTrainer(cfg, args.n, total_views, world, rank, device, ssim_lambda=lam,
+                                dp_mode=args.dp)
+    else:
+        if args.dp != "nccl":
+            raise SystemExit("--dp fused needs --trainer native")
+        tr = Trainer(cfg, args.n, total_views, world, rank, device, ssim_lambda=lam)
     n = tr.params["means"].shape[0]
     render_mode = args.mode == "render"
     if render_mode and args.trainer != "native":
@@ -630,7 +645,9 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        torch.cuda.synchronize()
         barrier(world)
+        del tr  # symmetric-memory buffers go before the process group
         dist.destroy_process_group()
 
 

@@ -300,6 +300,36 @@ GS_API int gs_l1_ssim_loss_grad(int height, int width, const float *raw_image,
                                 float *grad_raw, double *sums, float *scratch,
                                 size_t scratch_bytes, void *stream);
 
+/* ---- data-parallel optimizer step over NVLink / NVSwitch -----------------
+ * No counterpart in the reference, which trains on one GPU with one view
+ * per step (scripts/train.py:160-221); this is the multi-GPU extension of its
+ * optimizer step (scripts/train.py:17-44,219-221).
+ * One kernel per rank: every rank's flat gradient (n floats) is summed,
+ * Adam is applied to this rank's shard [rank * n / world, (rank + 1) * n /
+ * world) with this rank's shard of the Adam moments, and the new parameters
+ * are written into every rank's flat parameter buffer. grad_ptrs, param_ptrs
+ * and flag_ptrs are HOST arrays of `world` device pointers: every rank's
+ * gradient buffer, parameter buffer and flag buffer (gs_dp_flag_words(
+ * num_blocks) zero-initialised uint32 words), all addressable from this GPU
+ * (peer mappings). mc_grad / mc_param are the NVSwitch multicast addresses
+ * of the gradient and parameter buffers (then the sum is one
+ * multimem.ld_reduce and the write one multimem.st per float4), or both NULL
+ * (peer loads and stores). Every rank calls this with the same n, world,
+ * num_blocks (<= gs_dp_max_blocks()) and epoch, a value larger (mod 2^31)
+ * than at the previous call. n must be a multiple of 4 * world and all
+ * buffers 16-byte aligned. grad_shard_out (n / world floats, or NULL)
+ * receives this rank's shard of the summed gradient. Waits for other ranks
+ * are bounded (4 s); a rank that never arrives makes gs_check_status report
+ * GS_ERR_DEVICE_TIMEOUT. */
+GS_API size_t gs_dp_flag_words(int num_blocks);
+GS_API int gs_dp_max_blocks(void);
+GS_API int gs_dp_adam_step(int world, int rank, void *const *grad_ptrs, void *const *param_ptrs,
+                           void *const *flag_ptrs, void *mc_grad, void *mc_param, int64_t n,
+                           float *exp_avg_shard, float *exp_avg_sq_shard, int num_groups,
+                           const int64_t *group_ends, const float *lrs, const float *eps,
+                           float beta1, float beta2, int64_t step, uint32_t epoch, int num_blocks,
+                           float *grad_shard_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
