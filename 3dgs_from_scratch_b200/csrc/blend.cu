@@ -41,37 +41,58 @@ struct Rec {
 
 // Bitmask of the tile's 4 warp blocks (8x8 pixels each) that may hold a pixel
 // with q <= q_cut, where q_cut = min(chi2, 2 ln(opacity / alpha_thr)) bounds
-// both of the reference's skip tests (q > chi2, alpha < alpha_thr). The
-// ellipse {d : d^T Q d <= qc} lies in the box |dx| <= sqrt(qc C / det),
-// |dy| <= sqrt(qc A / det). The float evaluation of q at a pixel has a
-// relative error below 3e-7 * R with R = 2 (A + C)^2 / det (the ratio of the
-// summed term magnitudes to q); conics with R >= 2000 reach everything, and
-// for the rest qc = 1.01 q_cut + 0.05 exceeds q_cut by far more than that
-// error, so a skipped record fails one of the reference's tests at every
-// pixel of the block. Non-finite input reaches everything.
+// both of the reference's skip tests (q > chi2, alpha < alpha_thr). A block
+// is reached when the minimum m of the quadratic form q(d) = d^T Q d over the
+// box of offsets d = pixel - mean spanned by the block's pixel centres is at
+// most qc = 1.01 q_cut + 0.05: q is convex with its minimum at d = 0, so m is
+// 0 if the box holds the origin and otherwise lies on one of the box's four
+// edges, where it is a clamped 1-D quadratic minimum. The box contains every
+// pixel offset of the block, so m bounds q at each of them from below.
+// Rounding: with R = 2 (A + C)^2 / det (the ratio of the summed term
+// magnitudes to q), both the kernels' float q at a pixel and the float m
+// here are within 5e-4 R/2000 of exact (relative); an error in the clamped
+// minimiser changes m only to second order. Conics with R >= 2000 reach
+// everything; for the rest, m > qc implies the pixel's float q exceeds
+// (1.01 q_cut + 0.05)(1 - 1e-3) > q_cut, so a skipped record fails one of the
+// reference's tests at every pixel of the block. Non-finite input reaches
+// everything.
+__device__ __forceinline__ float box_min_q(float a, float b, float c, float dx0, float dx1,
+                                           float dy0, float dy1, float inv_a, float inv_c) {
+  if (dx0 <= 0.0f && dx1 >= 0.0f && dy0 <= 0.0f && dy1 >= 0.0f) return 0.0f;
+  float best = INFINITY;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float X = e ? dx1 : dx0;
+    const float dy = fminf(fmaxf(-b * X * inv_c, dy0), dy1);
+    best = fminf(best, a * X * X + 2.0f * b * X * dy + c * dy * dy);
+    const float Y = e ? dy1 : dy0;
+    const float dx = fminf(fmaxf(-b * Y * inv_a, dx0), dx1);
+    best = fminf(best, a * dx * dx + 2.0f * b * dx * Y + c * Y * Y);
+  }
+  return best;
+}
+
 __device__ __forceinline__ uint32_t reach_mask(float u, float v, float A, float B, float C,
                                                float opac, float alpha_thr, float chi_thr,
                                                int tile_x0, int tile_y0) {
-  double q_cut = (double)chi_thr;
+  float q_cut = chi_thr;
   if (alpha_thr > 0.0f) {
     if (!(opac > 0.0f)) return 0xfu;  // degenerate opacity: evaluate normally
-    double qa = 2.0 * log((double)opac / (double)alpha_thr);
-    q_cut = fmin(q_cut, qa);
+    q_cut = fminf(q_cut, 2.0f * logf(opac / alpha_thr));
   }
-  double a = A, c = C, b = B;
-  double det = a * c - b * b;
-  if (!(A > 0.0f) || !(C > 0.0f) || !(det > 0.0) || !isfinite(u) || !isfinite(v) ||
-      !isfinite(q_cut) || !(2.0 * (a + c) * (a + c) < 2000.0 * det))
+  const float det = A * C - B * B;
+  if (!(A > 0.0f) || !(C > 0.0f) || !(det > 0.0f) || !isfinite(u) || !isfinite(v) ||
+      !isfinite(q_cut) || !(2.0f * (A + C) * (A + C) < 2000.0f * det))
     return 0xfu;
-  if (q_cut < -0.05) return 0u;  // opacity below the alpha threshold: alpha < thr everywhere
-  double qc = fmax(q_cut, 0.0) * 1.01 + 0.05;
-  double hx = sqrt(qc * c / det);
-  double hy = sqrt(qc * a / det);
+  if (q_cut < -0.05f) return 0u;  // opacity below the alpha threshold: alpha < thr everywhere
+  const float qc = fmaxf(q_cut, 0.0f) * 1.01f + 0.05f;
+  const float inv_a = 1.0f / A, inv_c = 1.0f / C;
   uint32_t m = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
-    double bx0 = tile_x0 + 8 * (w & 1), by0 = tile_y0 + 8 * (w >> 1);
-    bool hit = (u + hx >= bx0) && (u - hx <= bx0 + 7.0) && (v + hy >= by0) && (v - hy <= by0 + 7.0);
+    const float dx0 = (float)(tile_x0 + 8 * (w & 1)) - u;
+    const float dy0 = (float)(tile_y0 + 8 * (w >> 1)) - v;
+    const bool hit = box_min_q(A, B, C, dx0, dx0 + 7.0f, dy0, dy0 + 7.0f, inv_a, inv_c) <= qc;
     m |= hit ? (1u << w) : 0u;
   }
   return m;
@@ -308,7 +329,7 @@ __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float
 // Backward blend. Gradient slot order per Gaussian: 0,1 = d(u,v);
 // 2,3,4 = d(conic a,b,c); 5 = d opacity; 6,7,8 = d colour.
 template <bool PACKED>
-__global__ void __launch_bounds__(kBlendThreads) blend_backward_kernel(
+__global__ void __launch_bounds__(kBlendThreads, 8) blend_backward_kernel(
     int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
     const int32_t *__restrict__ ids, int n, const float2 *__restrict__ points,
     const float4 *__restrict__ splat, const float *__restrict__ conic,
