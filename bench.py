@@ -75,7 +75,7 @@ def parse():
     p.add_argument("--global-views", type=int, default=None,
                    help="views per step over all ranks, sharded (strong scaling); "
                         "config 2 defaults to its batch of 32")
-    p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="nccl",
+    p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="fused",
                    help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
                         "reduce-scatter / sharded Adam / all-gather kernel (multicast when "
                         "available, or peer stores only)")
