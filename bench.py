@@ -54,14 +54,18 @@ FALLBACK_BF16_TFLOPS = 1590.0
 PRE_FWD_BYTES_PER_G = 281
 PRE_BWD_BYTES_PER_G = 504
 LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
+# 8-rank NCCL all-reduce bus bandwidth at 1 GiB measured on this pool's B200s (GB/s): the
+# reference figure for the fused data-parallel optimizer step
+NVLINK_ALLREDUCE_BUS_GBS = 725.0
 BLEND_FWD_FLOP_PER_PAIR = 22
 BLEND_BWD_FLOP_PER_PAIR = 60
 
 # DRAM bytes (read + write) per launch at config 1, from the ncu --set full
 # capture summarised in profiles/kernels_cfg1_full.md (dram__bytes_read.sum +
 # dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = {"preprocess_fwd": 274.4e6, "preprocess_bwd": 459.5e6,
-                     "blend_fwd": 58.3e6, "blend_bwd": 110.0e6}
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 277.0e6, "preprocess_bwd": 463.4e6,
+                     "blend_fwd": 56.6e6, "blend_bwd": 111.1e6, "optimizer": 1598.3e6,
+                     "loss": 51.2e6}
 
 
 def parse():
@@ -162,7 +166,8 @@ class StageTimer:
     """CUDA events around each C-ABI call of interest, on the launching stream."""
 
     WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_blend_forward", "gs_blend_backward",
-             "gs_preprocess_backward")
+             "gs_preprocess_backward", "gs_l1_loss_grad", "gs_l1_ssim_loss_grad", "gs_adam_step",
+             "gs_dp_adam_step")
 
     def __init__(self):
         self.events = {k: [] for k in self.WATCH}
@@ -603,6 +608,33 @@ def main():
             tf = fl * E / (stage_ms[nm] * 1e-3) / 1e12
             roof[key] = {"bound": "fp32", "ms": stage_ms[nm], "achieved": tf, "peak": fp32_peak,
                          "unit": "TFLOP/s", "frac": tf / fp32_peak}
+    npx = cfg.width * cfg.height * 3
+    tgt_bytes = 4  # float targets in the device-timed loop
+    if stage_ms.get("gs_l1_loss_grad"):  # raw + target read, gradient written
+        gbs = npx * (4 + tgt_bytes + 4) / (stage_ms["gs_l1_loss_grad"] * 1e-3) / 1e9
+        roof["loss"] = {"bound": "hbm", "ms": stage_ms["gs_l1_loss_grad"], "achieved": gbs,
+                        "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_l1_ssim_loss_grad"):
+        # two kernels: raw + target read, three fp32 maps written; maps + raw + target read,
+        # gradient written
+        b = npx * ((4 + tgt_bytes + 12) + (12 + 4 + tgt_bytes + 4))
+        gbs = b / (stage_ms["gs_l1_ssim_loss_grad"] * 1e-3) / 1e9
+        roof["loss"] = {"bound": "hbm", "ms": stage_ms["gs_l1_ssim_loss_grad"], "achieved": gbs,
+                        "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    numel = tr.fp.padded
+    if stage_ms.get("gs_adam_step"):  # param, grad, m, v read; param, m, v written
+        gbs = 28 * numel / (stage_ms["gs_adam_step"] * 1e-3) / 1e9
+        roof["optimizer"] = {"bound": "hbm", "ms": stage_ms["gs_adam_step"], "achieved": gbs,
+                             "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_dp_adam_step"):
+        # all-reduce-equivalent bus bytes per rank, 2 (w - 1) / w * 4 B * numel, against the
+        # measured 8-rank NCCL all-reduce bus bandwidth of this pool
+        bus = 2 * (world - 1) / world * 4 * numel
+        gbs = bus / (stage_ms["gs_dp_adam_step"] * 1e-3) / 1e9
+        roof["optimizer"] = {"bound": "nvlink", "ms": stage_ms["gs_dp_adam_step"],
+                             "achieved": gbs, "peak": NVLINK_ALLREDUCE_BUS_GBS, "unit": "GB/s",
+                             "frac": gbs / NVLINK_ALLREDUCE_BUS_GBS,
+                             "multicast": bool(getattr(tr.fp, "multicast", False))}
     dom = max(roof, key=lambda k: roof[k]["ms"]) if roof else None
     roofline = None
     if dom:
