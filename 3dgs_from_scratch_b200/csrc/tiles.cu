@@ -5,7 +5,8 @@
 // templated on the key width. One upfront kernel histograms every pass's
 // digits in a single read of the keys. In a pass, each 256-thread block
 // takes a tile of pairs (ticketed in start order), ranks its digits warp by
-// warp with match.any (the warp-striped layout keeps the ranking stable),
+// warp (lanes with equal digits found with one ballot per digit bit; the
+// warp-striped layout keeps the ranking stable),
 // publishes its per-digit counts, obtains the global per-digit prefix from
 // its predecessors by decoupled look-back (bounded spins), shuffles the tile
 // into digit order in shared memory and writes it out in coalesced runs.
@@ -169,17 +170,27 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
 // ---- onesweep radix sort -----------------------------------------------------
 
 constexpr int kSortThreads = 256;
+#ifndef GS_SORT_LOOKBACK
+#define GS_SORT_LOOKBACK 16  // predecessors inspected per look-back round trip
+#endif
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kMaxPasses = 8;
 constexpr uint32_t kLbAgg = 1u << 30;
 constexpr uint32_t kLbPrefix = 2u << 30;
 constexpr uint32_t kLbValue = (1u << 30) - 1;
 
-// Items per thread by key width (shared memory per tile: items * 256 * (key + 4) B).
+// Items per thread and resident blocks per SM by key width (shared memory per
+// tile: items * 256 * (key + 4) B; registers capped at 65536 / (256 * blocks)).
 template <typename KT> struct SortItems;
-template <> struct SortItems<uint64_t> { static constexpr int value = 14; };
-template <> struct SortItems<uint32_t> { static constexpr int value = 16; };
-template <> struct SortItems<uint16_t> { static constexpr int value = 20; };
+template <> struct SortItems<uint64_t> {
+  static constexpr int value = 14, min_blocks = 2;
+};
+template <> struct SortItems<uint32_t> {
+  static constexpr int value = 10, min_blocks = 3;
+};
+template <> struct SortItems<uint16_t> {
+  static constexpr int value = 12, min_blocks = 3;
+};
 
 template <typename KT>
 __device__ __forceinline__ uint32_t digit_of(KT key, int shift, uint32_t dmask) {
@@ -256,7 +267,7 @@ struct SortSmem {
 
 // One digit pass. vals_in == nullptr means the identity (value = index).
 template <typename KT, int ITEMS>
-__global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
+__global__ void __launch_bounds__(kSortThreads, SortItems<KT>::min_blocks) onesweep_pass_kernel(
     const KT *__restrict__ keys_in, const int32_t *__restrict__ vals_in,
     KT *__restrict__ keys_out, int32_t *__restrict__ vals_out, int64_t n, int shift,
     uint32_t dmask, const uint32_t *__restrict__ hist, uint32_t *__restrict__ lookback,
@@ -293,7 +304,16 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
     const int64_t idx = base + k * 32 + lane;
     const bool valid = idx < n;
     const uint32_t d = valid ? digit_of(key[k], shift, dmask) : 0x100u;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    // Lanes with the same digit (and validity): one ballot per digit bit,
+    // which issues faster than match.any.
+    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+    if (!valid) peers = ~peers;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const bool bit = (d >> b) & 1u;
+      const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+      peers &= bit ? bal : ~bal;
+    }
     const uint32_t leader = 31 - __clz(peers);
     // One shared-memory atomic per digit group: the returned count is only
     // needed in the scatter below, so the ITEMS atomics of a thread are
@@ -329,7 +349,7 @@ __global__ void __launch_bounds__(kSortThreads, 2) onesweep_pass_kernel(
     // nearest first, re-polling (bounded) only those not yet published.
     // Inspecting many predecessors per round trip keeps the first wave of
     // tiles from forming a chain of one L2 round trip per tile.
-    constexpr int kLookback = 16;
+    constexpr int kLookback = GS_SORT_LOOKBACK;
     int top = tile - 1;
     bool found = false;
     while (!found && top >= 0) {
