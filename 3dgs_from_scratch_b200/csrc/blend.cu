@@ -7,9 +7,11 @@
 // shared memory, together with a 4-bit mask of the warp blocks whose pixels
 // that Gaussian can reach (a conservative bound; see reach_mask), and then
 // every warp walks the batch from shared memory, skipping records its block
-// cannot see as one uniform branch. Per pixel the arithmetic is the reference's, operation for
-// operation (ruguangyou/3dgs_from_scratch src/cuda/kernel.cu:954-982 forward,
-// 1066-1110 backward), so images and per-pixel gradient terms match it.
+// cannot see as one uniform branch. Per pixel the forward arithmetic is the
+// reference's, operation for operation (ruguangyou/3dgs_from_scratch
+// src/cuda/kernel.cu:954-982), so images match it bit for bit; the backward
+// (kernel.cu:1066-1110) keeps the forward's skip tests and reorganises the
+// gradient sums (see bwd_step).
 //
 // The forward records each pixel's final transmittance and the index one past
 // its last contributing list entry, so the backward needs no forward replay.
@@ -283,10 +285,12 @@ struct BwdPx {
 // the flush: acc[0..4] = sum of du*ag, dv*ag, du*du*ag, du*dv*ag, dv*dv*ag
 // (ag = alpha * dL/dalpha), from which d(u,v) = conic * (acc0, acc1) and
 // d conic = (-acc2 / 2, -acc3, -acc4 / 2). The skip decisions (chi-square
-// cut, alpha threshold) use the forward's expressions operation for
-// operation; the two divisions by (1 - alpha) of the reference
-// (kernel.cu:1088,1094) become one approximate reciprocal (rcp.approx, at
-// most 1 ulp) and two products.
+// cut, alpha threshold) use the forward's expressions, with the fast
+// exponential (__expf, a few 1e-7 relative): a pair whose alpha lies within
+// that of the threshold may be decided differently from the forward, which
+// changes the pixel's gradient by about alpha_thr relative; the two
+// divisions by (1 - alpha) of the reference (kernel.cu:1088,1094) become one
+// approximate reciprocal (rcp.approx, at most 1 ulp) and two products.
 __device__ __forceinline__ float rcp_approx(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
@@ -300,7 +304,7 @@ __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float
   const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
   float exponent = inv00 * du * du + 2.0f * inv01 * du * dv + inv11 * dv * dv;
   if (exponent > chi_thr) return false;
-  float density = expf(-0.5f * exponent);
+  float density = __expf(-0.5f * exponent);
   float alpha = density * g1.y;
   if (alpha < alpha_thr) return false;
   float one_minus_alpha = 1.0f - alpha + kTransEps;

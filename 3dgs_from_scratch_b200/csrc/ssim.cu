@@ -14,8 +14,11 @@
 // channel and pixel ("same") or over the pixels at least 5 from every border
 // ("valid", the reference's choice).
 //
-// Two kernels, both tiled 32 x 16 output pixels per block with the 5-pixel
-// halo staged in shared memory and the window applied separably:
+// Two kernels, both tiled 32 x 32 output pixels per block with the 5-pixel
+// halo staged in shared memory and the window applied separably, register
+// blocked (a thread produces 8 consecutive outputs of a row, then 4 of a
+// column, from a sliding window of loaded values, instead of one shared-memory
+// load per multiply-add):
 //   ssim_fwd_kernel  local statistics -> S (summed into a double) and the
 //                    three partial derivatives of S at each pixel,
 //                    dS/dmu_x, dS/dE[x^2], dS/dE[xy], already multiplied by
@@ -31,12 +34,16 @@
 
 namespace gs {
 
-constexpr int kSsimTW = 32;           // output tile width
-constexpr int kSsimTH = 16;           // output tile height
-constexpr int kSsimR = 5;             // window radius
+constexpr int kSsimTW = 32;                    // output tile width
+constexpr int kSsimTH = 32;                    // output tile height
+constexpr int kSsimR = 5;                      // window radius
 constexpr int kSsimWin = 2 * kSsimR + 1;
 constexpr int kSsimHW = kSsimTW + 2 * kSsimR;  // 42 staged columns
-constexpr int kSsimHH = kSsimTH + 2 * kSsimR;  // 26 staged rows
+constexpr int kSsimHH = kSsimTH + 2 * kSsimR;  // 42 staged rows
+constexpr int kSsimStride = kSsimHW + 1;       // 43: conflict-free row starts
+constexpr int kSsimHRow = kSsimTW + 1;         // 33: conflict-free horizontal-pass stores
+constexpr int kSsimRunH = 8;                   // outputs per thread, horizontal pass
+constexpr int kSsimRunV = 4;                   // outputs per thread, vertical pass
 constexpr int kSsimThreads = 256;
 constexpr float kSsimC1 = 0.01f * 0.01f;
 constexpr float kSsimC2 = 0.03f * 0.03f;
@@ -85,6 +92,67 @@ __device__ __forceinline__ double block_sum_double(double v) {
 // Grid: x = tiles_x * planes (plane fastest, so the blocks of the three
 // channels of one tile run together and share the tile's cache lines),
 // y = tiles_y.
+// Horizontal pass of NQ quantities over one staged row: thread item = (row,
+// group of kSsimRunH columns). val(k, q) gives quantity q at staged column
+// c0 + k; the kSsimRunH window sums go to out[q][row][c0 + o].
+template <int NQ, typename Val>
+__device__ __forceinline__ void hpass_run(Val val, float (*out)[kSsimHH][kSsimHRow], int row,
+                                          int c0) {
+  float acc[kSsimRunH][NQ];
+#pragma unroll
+  for (int o = 0; o < kSsimRunH; ++o)
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) acc[o][q] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kSsimRunH + kSsimWin - 1; ++k) {
+    float v[NQ];
+    val(k, v);
+#pragma unroll
+    for (int o = 0; o < kSsimRunH; ++o) {
+      const int t = k - o;
+      if (t >= 0 && t < kSsimWin) {
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) acc[o][q] = fmaf(c_ssim_win[t], v[q], acc[o][q]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < kSsimRunH; ++o)
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) out[q][row][c0 + o] = acc[o][q];
+}
+
+// Vertical pass: kSsimRunV consecutive output rows r0.. of column c.
+template <int NQ>
+__device__ __forceinline__ void vpass_run(const float (*hs)[kSsimHH][kSsimHRow], int r0, int c,
+                                          float (&acc)[kSsimRunV][NQ]) {
+#pragma unroll
+  for (int o = 0; o < kSsimRunV; ++o)
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) acc[o][q] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kSsimRunV + kSsimWin - 1; ++k) {
+    float v[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) v[q] = hs[q][r0 + k][c];
+#pragma unroll
+    for (int o = 0; o < kSsimRunV; ++o) {
+      const int t = k - o;
+      if (t >= 0 && t < kSsimWin) {
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) acc[o][q] = fmaf(c_ssim_win[t], v[q], acc[o][q]);
+      }
+    }
+  }
+}
+
+constexpr int kSsimHItems = kSsimHH * (kSsimTW / kSsimRunH);  // 168
+constexpr int kSsimVItems = kSsimTW * (kSsimTH / kSsimRunV);  // 256
+static_assert(kSsimVItems == kSsimThreads, "one vertical run per thread");
+
+// Grid: x = tiles_x * planes (plane fastest, so the blocks of the three
+// channels of one tile run together and share the tile's cache lines),
+// y = tiles_y.
 template <bool HWC, typename TT>
 __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT> src, int planes,
                                                                 int valid, float wscale,
@@ -92,9 +160,9 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
                                                                 float *__restrict__ m1,
                                                                 float *__restrict__ m2,
                                                                 double *__restrict__ ssim_sum) {
-  __shared__ float sx[kSsimHH][kSsimHW + 1];
-  __shared__ float sy[kSsimHH][kSsimHW + 1];
-  __shared__ float hs[5][kSsimHH][kSsimTW + 1];
+  __shared__ float sx[kSsimHH * kSsimStride];
+  __shared__ float sy[kSsimHH * kSsimStride];
+  __shared__ float hs[5][kSsimHH][kSsimHRow];
   const int H = src.H, W = src.W;
   const int plane = blockIdx.x % planes;
   const int tx = blockIdx.x / planes;
@@ -104,45 +172,36 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
     const int gy = gy0 - kSsimR + r, gx = gx0 - kSsimR + c;
     float xv = 0.0f, yv = 0.0f;
     if (gy >= 0 && gy < H && gx >= 0 && gx < W) src.load(plane, gy, gx, xv, yv);
-    sx[r][c] = xv;
-    sy[r][c] = yv;
+    sx[r * kSsimStride + c] = xv;
+    sy[r * kSsimStride + c] = yv;
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < kSsimHH * kSsimTW; k += kSsimThreads) {
-    const int r = k / kSsimTW, c = k - r * kSsimTW;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
-#pragma unroll
-    for (int t = 0; t < kSsimWin; ++t) {
-      const float g = c_ssim_win[t];
-      const float xv = sx[r][c + t], yv = sy[r][c + t];
-      a0 = fmaf(g, xv, a0);
-      a1 = fmaf(g, yv, a1);
-      a2 = fmaf(g, xv * xv, a2);
-      a3 = fmaf(g, yv * yv, a3);
-      a4 = fmaf(g, xv * yv, a4);
-    }
-    hs[0][r][c] = a0;
-    hs[1][r][c] = a1;
-    hs[2][r][c] = a2;
-    hs[3][r][c] = a3;
-    hs[4][r][c] = a4;
+  if (threadIdx.x < kSsimHItems) {
+    const int row = threadIdx.x >> 2, c0 = (threadIdx.x & 3) * kSsimRunH;
+    const float *px = sx + row * kSsimStride + c0;
+    const float *py = sy + row * kSsimStride + c0;
+    hpass_run<5>(
+        [&](int k, float *v) {
+          const float x = px[k], y = py[k];
+          v[0] = x;
+          v[1] = y;
+          v[2] = x * x;
+          v[3] = y * y;
+          v[4] = x * y;
+        },
+        hs, row, c0);
   }
   __syncthreads();
+  const int c = threadIdx.x & 31, r0 = (threadIdx.x >> 5) * kSsimRunV;
+  float st[kSsimRunV][5];
+  vpass_run<5>(hs, r0, c, st);
   double acc = 0.0;
-  for (int k = threadIdx.x; k < kSsimTH * kSsimTW; k += kSsimThreads) {
-    const int r = k / kSsimTW, c = k - r * kSsimTW;
-    const int gy = gy0 + r, gx = gx0 + c;
-    if (gy >= H || gx >= W) continue;
-    float mx = 0.f, my = 0.f, exx = 0.f, eyy = 0.f, exy = 0.f;
+  const int gx = gx0 + c;
 #pragma unroll
-    for (int t = 0; t < kSsimWin; ++t) {
-      const float g = c_ssim_win[t];
-      mx = fmaf(g, hs[0][r + t][c], mx);
-      my = fmaf(g, hs[1][r + t][c], my);
-      exx = fmaf(g, hs[2][r + t][c], exx);
-      eyy = fmaf(g, hs[3][r + t][c], eyy);
-      exy = fmaf(g, hs[4][r + t][c], exy);
-    }
+  for (int o = 0; o < kSsimRunV; ++o) {
+    const int gy = gy0 + r0 + o;
+    if (gy >= H || gx >= W) continue;
+    const float mx = st[o][0], my = st[o][1], exx = st[o][2], eyy = st[o][3], exy = st[o][4];
     const bool counted =
         !valid || (gy >= kSsimR && gy < H - kSsimR && gx >= kSsimR && gx < W - kSsimR);
     float d_mu = 0.f, d_xx = 0.f, d_xy = 0.f;
@@ -153,17 +212,17 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
       const float inv_b = 1.0f / (b1 * b2);
       const float s = a1 * a2 * inv_b;
       acc += (double)s;
-      d_xy = 2.f * a1 * inv_b;                     // dS/dE[xy]
-      d_xx = -s / b2;                              // dS/dE[x^2]
+      d_xy = 2.f * a1 * inv_b;  // dS/dE[xy]
+      d_xx = -s / b2;           // dS/dE[x^2]
       d_mu = 2.f * my * a2 * inv_b - 2.f * mx * s / b1 - 2.f * mx * d_xx - my * d_xy;
       d_mu *= wscale;
       d_xx *= wscale;
       d_xy *= wscale;
     }
-    const int64_t o = (int64_t)plane * H * W + (int64_t)gy * W + gx;
-    m0[o] = d_mu;
-    m1[o] = d_xx;
-    m2[o] = d_xy;
+    const int64_t oi = (int64_t)plane * H * W + (int64_t)gy * W + gx;
+    m0[oi] = d_mu;
+    m1[oi] = d_xx;
+    m2[oi] = d_xy;
   }
   const double t = block_sum_double(acc);
   if (threadIdx.x == 0 && t != 0.0) atomicAdd(ssim_sum, t);
@@ -178,8 +237,8 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
     SsimSrc<HWC, TT> src, int planes, const float *__restrict__ m0, const float *__restrict__ m1,
     const float *__restrict__ m2, const float *__restrict__ upstream, float l1_weight,
     float inv_numel, float *__restrict__ grad, double *__restrict__ l1_sum) {
-  __shared__ float sm[3][kSsimHH][kSsimHW + 1];
-  __shared__ float hs[3][kSsimHH][kSsimTW + 1];
+  __shared__ float sm[3][kSsimHH * kSsimStride];
+  __shared__ float hs[3][kSsimHH][kSsimHRow];
   const int H = src.H, W = src.W;
   const int plane = blockIdx.x % planes;
   const int tx = blockIdx.x / planes;
@@ -195,43 +254,36 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
       v1 = m1[o];
       v2 = m2[o];
     }
-    sm[0][r][c] = v0;
-    sm[1][r][c] = v1;
-    sm[2][r][c] = v2;
+    sm[0][r * kSsimStride + c] = v0;
+    sm[1][r * kSsimStride + c] = v1;
+    sm[2][r * kSsimStride + c] = v2;
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < kSsimHH * kSsimTW; k += kSsimThreads) {
-    const int r = k / kSsimTW, c = k - r * kSsimTW;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-#pragma unroll
-    for (int t = 0; t < kSsimWin; ++t) {
-      const float g = c_ssim_win[t];
-      a0 = fmaf(g, sm[0][r][c + t], a0);
-      a1 = fmaf(g, sm[1][r][c + t], a1);
-      a2 = fmaf(g, sm[2][r][c + t], a2);
-    }
-    hs[0][r][c] = a0;
-    hs[1][r][c] = a1;
-    hs[2][r][c] = a2;
+  if (threadIdx.x < kSsimHItems) {
+    const int row = threadIdx.x >> 2, c0 = (threadIdx.x & 3) * kSsimRunH;
+    const int base = row * kSsimStride + c0;
+    hpass_run<3>(
+        [&](int k, float *v) {
+          v[0] = sm[0][base + k];
+          v[1] = sm[1][base + k];
+          v[2] = sm[2][base + k];
+        },
+        hs, row, c0);
   }
   __syncthreads();
+  const int c = threadIdx.x & 31, r0 = (threadIdx.x >> 5) * kSsimRunV;
+  float cv[kSsimRunV][3];
+  vpass_run<3>(hs, r0, c, cv);
   const float up = upstream ? *upstream : 1.0f;
   double acc = 0.0;
-  for (int k = threadIdx.x; k < kSsimTH * kSsimTW; k += kSsimThreads) {
-    const int r = k / kSsimTW, c = k - r * kSsimTW;
-    const int gy = gy0 + r, gx = gx0 + c;
-    if (gy >= H || gx >= W) continue;
-    float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+  const int gx = gx0 + c;
 #pragma unroll
-    for (int t = 0; t < kSsimWin; ++t) {
-      const float g = c_ssim_win[t];
-      c0 = fmaf(g, hs[0][r + t][c], c0);
-      c1 = fmaf(g, hs[1][r + t][c], c1);
-      c2 = fmaf(g, hs[2][r + t][c], c2);
-    }
+  for (int o = 0; o < kSsimRunV; ++o) {
+    const int gy = gy0 + r0 + o;
+    if (gy >= H || gx >= W) continue;
     float xv, yv;
     src.load(plane, gy, gx, xv, yv);
-    const float gs = c0 + 2.f * xv * c1 + yv * c2;
+    const float gs = cv[o][0] + 2.f * xv * cv[o][1] + yv * cv[o][2];
     if (FUSED) {
       const int64_t i = src.index(plane, gy, gx);
       const float d = xv - yv;
