@@ -62,6 +62,11 @@ SIGNATURES = {
     "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
     "gs_ssim_scratch_bytes": (SZ, [I, I, I]),
+    "gs_densify_accumulate": (I, [I, P, P, I, I, P, P, P]),
+    "gs_densify_plan": (I, [I, P, P, P, P, F, I, F, F, F, P, P, P, P, P]),
+    "gs_densify_apply": (I, [I, P, P, P, P, I64, I64, I64, P, P, P, P, P, P, P, P, P,
+                             ctypes.c_uint64, F, P]),
+    "gs_reset_opacities": (I, [I, P, P, P, F, P]),
     "gs_dp_flag_words": (SZ, [I]),
     "gs_dp_max_blocks": (I, []),
     "gs_dp_adam_step": (I, [I, I, P, P, P, P, P, I64, P, P, I, P, P, P, F, F, I64, ctypes.c_uint32,

@@ -56,35 +56,18 @@ class FlatParams:
                  betas=(0.9, 0.999), group=None, fused_dp=False):
         first = tensors[GROUPS[0]]
         self.device = first.device
-        self.shapes = {k: tuple(tensors[k].shape) for k in GROUPS}
-        self.spans = {}
-        off = 0
-        for k in GROUPS:
-            n = tensors[k].numel()
-            self.spans[k] = (off, n)
-            off += (n + 3) // 4 * 4
-        self.numel = off
         self.group = group
         self.world, self.rank = _world_rank(group)
         self.fused = bool(fused_dp) and self.world > 1 and self.device.type == "cuda"
         if fused_dp and fused_dp not in (True, "auto", "p2p"):
             raise ValueError("fused_dp must be False, True, 'auto' or 'p2p'")
         self._force_p2p = fused_dp == "p2p"
-        f = dict(device=self.device, dtype=torch.float32)
-        if self.fused:
-            self.padded = padded_numel(off, self.world)
-            self._setup_symmetric()
-        else:
-            self.padded = off
-            self.data = torch.zeros(off, **f)
-            self.grad = torch.zeros(off, **f)
-        self.params = {}
+        self._set_layout({k: tuple(tensors[k].shape) for k in GROUPS})
+        self._alloc_buffers()
         for k in GROUPS:
             a, n = self.spans[k]
             self.data[a:a + n].copy_(tensors[k].reshape(-1))
-            p = torch.nn.Parameter(self.data[a:a + n].view(self.shapes[k]))
-            p.grad = self.grad[a:a + n].view(self.shapes[k])
-            self.params[k] = p
+        self._make_params()
         self.lrs = dict(DEFAULT_LRS if lrs is None else lrs)
         self.eps = float(eps)
         self.betas = (float(betas[0]), float(betas[1]))
@@ -92,6 +75,83 @@ class FlatParams:
         self.exp_avg_sq = None
         self.step_count = 0
         self._epoch = 0
+
+    def _set_layout(self, shapes):
+        self.shapes = dict(shapes)
+        self.spans = {}
+        off = 0
+        for k in GROUPS:
+            n = 1
+            for d in self.shapes[k]:
+                n *= d
+            self.spans[k] = (off, n)
+            off += (n + 3) // 4 * 4
+        self.numel = off
+        self.padded = padded_numel(off, self.world) if self.fused else off
+
+    def _alloc_buffers(self):
+        if self.fused:
+            self._setup_symmetric()
+        else:
+            f = dict(device=self.device, dtype=torch.float32)
+            self.data = torch.zeros(self.padded, **f)
+            self.grad = torch.zeros(self.padded, **f)
+
+    def _make_params(self):
+        self.params = {}
+        for k in GROUPS:
+            a, n = self.spans[k]
+            p = torch.nn.Parameter(self.data[a:a + n].view(self.shapes[k]))
+            p.grad = self.grad[a:a + n].view(self.shapes[k])
+            self.params[k] = p
+
+    @property
+    def num_gaussians(self) -> int:
+        return self.shapes[GROUPS[0]][0]
+
+    def group_offsets(self):
+        """Element offset of each group in the flat buffers (host int64 array)."""
+        return (ctypes.c_int64 * len(GROUPS))(*[self.spans[k][0] for k in GROUPS])
+
+    def full_moments(self):
+        """The Adam moments over the whole flat buffer (gathered from the
+        ranks' shards with the fused step), or (None, None) before the first
+        step."""
+        if self.exp_avg is None:
+            return None, None
+        if not self.fused:
+            return self.exp_avg, self.exp_avg_sq
+        import torch.distributed as dist
+
+        full = []
+        for t in (self.exp_avg, self.exp_avg_sq):
+            out = torch.empty(self.padded, device=self.device, dtype=torch.float32)
+            dist.all_gather_into_tensor(out, t, group=self.group)
+            full.append(out)
+        return full[0], full[1]
+
+    def rebuild(self, num_gaussians: int, fill):
+        """Re-lay the buffers out for `num_gaussians` Gaussians. fill(old_data,
+        old_offsets, new_data, new_offsets, old_m, old_v, new_m, new_v) writes
+        the new parameters (and, when the moments exist, the new moments) from
+        the old; the gradient buffer comes back zeroed. With the fused step
+        this is a collective (new symmetric buffers, re-sharded moments)."""
+        old_data, old_offsets = self.data, self.group_offsets()
+        old_m, old_v = self.full_moments()
+        self._set_layout({k: (int(num_gaussians),) + tuple(self.shapes[k][1:]) for k in GROUPS})
+        self._alloc_buffers()
+        new_m = new_v = None
+        if old_m is not None:
+            new_m = torch.zeros(self.padded, device=self.device, dtype=torch.float32)
+            new_v = torch.zeros(self.padded, device=self.device, dtype=torch.float32)
+        fill(old_data, old_offsets, self.data, self.group_offsets(), old_m, old_v, new_m, new_v)
+        if new_m is not None:
+            if self.fused:
+                shard = self.padded // self.world
+                sl = slice(self.rank * shard, (self.rank + 1) * shard)
+                new_m, new_v = new_m[sl].clone(), new_v[sl].clone()
+            self.exp_avg, self.exp_avg_sq = new_m, new_v
+        self._make_params()
 
     # ---- symmetric-memory set-up (fused data-parallel step) -----------------
 

@@ -45,7 +45,8 @@ class NativeTrainer:
     opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
-                 ssim_lambda: float = 0.0, group=None, fused_dp=False, **render_opts):
+                 ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
+                 **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -57,13 +58,17 @@ class NativeTrainer:
         self.width, self.height = int(width), int(height)
         self.opts = dict(RENDER_DEFAULTS)
         self.opts.update(render_opts)
-        self.n = self.fp.shapes["means"][0]
+        self.strategy = strategy  # a densify.DeviceStrategy, or None
         self.tx = (self.width + 15) // 16
         self.ty = (self.height + 15) // 16
 
     @property
     def params(self):
         return self.fp.params
+
+    @property
+    def n(self) -> int:
+        return self.fp.num_gaussians
 
     def _ptr(self, name):
         return self.fp.params[name].data_ptr()
@@ -168,6 +173,8 @@ class NativeTrainer:
                      s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
                      o["transmittance_threshold"], o["chi_squared_threshold"],
                      g_points.data_ptr(), g_splat.data_ptr(), st)
+            if self.strategy is not None:  # strategy.py:48-72, per view
+                self.strategy.accumulate(g_points, s["radii"], W, H)
             nat.call("gs_preprocess_backward", n, self._ptr("means"), self._ptr("scales"),
                      self._ptr("quaternions"), self._ptr("opacities"),
                      self._ptr("sh_coeffs_dc"), self._ptr("sh_coeffs_rest"), s["w2c"].data_ptr(),
@@ -183,15 +190,19 @@ class NativeTrainer:
         ssim = loss_sums[:, 1] / (3 * (H - 10) * (W - 10))
         return (1 - lam) * l1 + lam * (1 - ssim)
 
-    def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True):
+    def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True, step_index=None):
         """One training step over this rank's views: render, loss, backward
         (the first view overwrites the flat gradient, so no zeroing is needed
         between steps), then the gradient sum over the ranks and Adam
         (FlatParams.step: NCCL all-reduce + one-launch Adam, or with
         fused_dp the one-kernel reduce-scatter / sharded Adam / all-gather).
-        Returns the losses."""
+        With a strategy and step_index, the densification schedule of
+        scripts/train.py:224-227 runs after the optimizer step (it may change
+        the number of Gaussians). Returns the losses."""
         views = self.forward_views(world_to_cameras, intrinsics)
         losses = self.loss_and_backward(views, targets)
         if optimizer_step:
             self.fp.step()
+            if self.strategy is not None and step_index is not None:
+                self.strategy.adjust(self.fp, int(step_index))
         return losses

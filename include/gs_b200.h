@@ -330,6 +330,51 @@ GS_API int gs_dp_adam_step(int world, int rank, void *const *grad_ptrs, void *co
                            float beta1, float beta2, int64_t step, uint32_t epoch, int num_blocks,
                            float *grad_shard_out, void *stream);
 
+/* ---- adaptive density control on the flat buffers -------------------------
+ * The reference's Strategy (src/strategy.py:5-250) on the device. Flat
+ * layout: six groups (means, log-scales, raw quaternions, opacity logits,
+ * sh_dc, sh_rest: 3, 3, 4, 1, 3, 45 floats per Gaussian) at the element
+ * offsets group_offsets[0..5] (HOST array) of one fp32 buffer; Adam moments
+ * in the same layout. */
+
+/* strategy.py:48-72 for one view: where both radii are positive,
+ * grad_accum[i] += |(g_u * width / 2, g_v * height / 2)|, count[i] += 1. */
+GS_API int gs_densify_accumulate(int n, const float *grad_points, const float *radii, int width,
+                                 int height, float *grad_accum, float *count, void *stream);
+
+/* strategy.py:74-80,118-128: per Gaussian codes[i] = 0 pruned (sigmoid
+ * opacity < prune_opacity, or with prune_by_scale max exp(log-scale) >
+ * prune_scale), 1 kept, 2 kept and cloned (mean gradient grad_accum /
+ * max(count, 1) > grow_grad and max scale < split_scale), 3 split (high
+ * gradient, larger); and 0/1 flags (kept: codes 1, 2; cloned: 2; split: 3)
+ * whose exclusive scans give the output slots of gs_densify_apply. */
+GS_API int gs_densify_plan(int n, const float *params, const int64_t *group_offsets,
+                           const float *grad_accum, const float *count, float prune_opacity,
+                           int prune_by_scale, float prune_scale, float grow_grad,
+                           float split_scale, uint8_t *codes, int32_t *keep_flags,
+                           int32_t *clone_flags, int32_t *split_flags, void *stream);
+
+/* strategy.py:83-233: writes the new flat buffer of n_keep + n_clone +
+ * 2 n_split Gaussians, ordered [kept and not split][clones][split sample
+ * 0][split sample 1], from the codes and the scanned slots (pos_*). Split
+ * samples: mean + R(q / |q|) (exp(s) * z), log-scale log(exp(s) / scale_div),
+ * the rest repeated; z from noise (2 x n_split x 3 floats, sample-major) or,
+ * when noise is NULL, from Philox keyed by (seed, split slot). New Adam
+ * moments (when the new_exp_avg* pointers are given): copied for kept
+ * Gaussians, zero for clones and split samples. */
+GS_API int gs_densify_apply(int n, const uint8_t *codes, const int32_t *pos_keep,
+                            const int32_t *pos_clone, const int32_t *pos_split, int64_t n_keep,
+                            int64_t n_clone, int64_t n_split, const float *params,
+                            const int64_t *group_offsets, float *new_params,
+                            const int64_t *new_group_offsets, const float *exp_avg,
+                            const float *exp_avg_sq, float *new_exp_avg, float *new_exp_avg_sq,
+                            const float *noise, uint64_t seed, float scale_div, void *stream);
+
+/* strategy.py:235-250: opacity_logits = min(opacity_logits, threshold) and
+ * the group's Adam moments (if given) zeroed. */
+GS_API int gs_reset_opacities(int n, float *opacity_logits, float *exp_avg, float *exp_avg_sq,
+                              float threshold, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
