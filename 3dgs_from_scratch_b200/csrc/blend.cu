@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
   const int tile = blockIdx.x;
   const int tx = tiles_x_of(width);
   const int tile_x0 = (tile % tx) * GS_TILE, tile_y0 = (tile / tx) * GS_TILE;
-  const int t = threadIdx.x, warp = t >> 5;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int2 pp = pixel_in_tile(t);
   const int u = tile_x0 + pp.x, v0 = tile_y0 + pp.y, v1 = v0 + 4;
   const bool in0 = (u < width) && (v0 < height);
@@ -209,10 +209,15 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
     }
     __syncthreads();
     const int cnt = min(kBatch, e - base);
-    if (!__all_sync(0xffffffffu, p0.done && p1.done)) {
-      for (int j = 0; j < cnt; ++j) {
-        if (!((s_mask[j] >> warp) & 1u)) continue;  // uniform across the warp
-        if (p0.done && p1.done) break;
+    // 32 entries at a time: one ballot of the reach masks, then only the
+    // entries this warp's block can see, in list order
+    for (int j0 = 0; j0 < cnt; j0 += 32) {
+      if (__all_sync(0xffffffffu, p0.done && p1.done)) break;
+      const int jl = j0 + lane;
+      uint32_t todo = __ballot_sync(0xffffffffu, jl < cnt && ((s_mask[jl] >> warp) & 1u));
+      while (todo) {
+        const int j = j0 + __ffs(todo) - 1;
+        todo &= todo - 1;
         const float4 g0 = s_g0[j];
         const float4 g1 = s_g1[j];
         const float cb = ACCUM ? s_b[j] : 0.f;
@@ -416,24 +421,31 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_backward_kernel(
     }
     __syncthreads();
     const int jmax = min(cnt, warp_end - bstart);  // entries beyond every lane's end are idle
-    for (int j = jmax - 1; j >= 0; --j) {
-      if (!((s_mask[j] >> warp) & 1u)) continue;  // uniform across the warp
-      const int k = bstart + j;
-      const float4 g0 = s_g0[j];
-      const float4 g1 = s_g1[j];
-      const float c2 = s_b[j];
-      float acc[9];
+    // 32 entries at a time, back to front: one ballot of the reach masks
+    // (bit b <-> entry j1 - 1 - b), then the visible entries highest first
+    for (int j1 = jmax; j1 > 0; j1 -= 32) {
+      const int jl = j1 - 1 - (int)lane;
+      uint32_t todo = __ballot_sync(0xffffffffu, jl >= 0 && ((s_mask[jl] >> warp) & 1u));
+      while (todo) {
+        const int j = j1 - __ffs(todo);
+        todo &= todo - 1;
+        const int k = bstart + j;
+        const float4 g0 = s_g0[j];
+        const float4 g1 = s_g1[j];
+        const float c2 = s_b[j];
+        float acc[9];
 #pragma unroll
-      for (int q = 0; q < 9; ++q) acc[q] = 0.f;
-      bool contrib = false;
-      if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc);
-      if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc);
-      if (!__any_sync(0xffffffffu, contrib)) continue;
-      float r8 = reduce8(acc, lane);
-      float r9 = reduce1(acc[8]);
-      // [j][9] layout: the 8 writing lanes hit 8 consecutive words (distinct banks)
-      if ((lane & 3) == 0) atomicAdd(&s_acc[j * 9 + ((lane >> 2) & 7)], r8);
-      if (lane == 1) atomicAdd(&s_acc[j * 9 + 8], r9);
+        for (int q = 0; q < 9; ++q) acc[q] = 0.f;
+        bool contrib = false;
+        if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc);
+        if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc);
+        if (!__any_sync(0xffffffffu, contrib)) continue;
+        float r8 = reduce8(acc, lane);
+        float r9 = reduce1(acc[8]);
+        // [j][9] layout: the 8 writing lanes hit 8 consecutive words (distinct banks)
+        if ((lane & 3) == 0) atomicAdd(&s_acc[j * 9 + ((lane >> 2) & 7)], r8);
+        if (lane == 1) atomicAdd(&s_acc[j * 9 + 8], r9);
+      }
     }
     __syncthreads();
 #pragma unroll
