@@ -76,6 +76,10 @@ SIGNATURES = {
     "gs_l1_ssim_loss_grad": (I, [I, I, P, P, I, F, P, P, P, SZ, P]),
     "gs_preprocess_backward": (I, [I, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P, I, P, I, P,
                                    P, P, P, P, P, P]),
+    "gs_preprocess_forward_views": (I, [I, I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I,
+                                        I, P, P, P, P, P, P, P, P]),
+    "gs_preprocess_backward_views": (I, [I, I, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P, I,
+                                         P, I, P, P, P, P, P, P, P]),
 }
 
 _lib = None

@@ -194,6 +194,9 @@ __device__ __forceinline__ void stage_add(float *__restrict__ dst, const float *
   for (int k = threadIdx.x; k < count; k += blockDim.x) dst[k] += src[k];
 }
 
+// Views: camera v at w2c + 16 v, K + 9 v, campos + 3 v; its outputs at
+// element offset v * n of each per-Gaussian output array, its pair total at
+// total[v]. One staged chunk of parameters serves every view.
 struct PreFwdArgs {
   const float *means, *scales, *quats, *opac, *dc, *rest, *w2c, *K, *campos;
   float near_plane, far_plane, min_opacity, min_radius, max_radius;
@@ -206,11 +209,25 @@ struct PreFwdArgs {
   float4 *splat;
   int32_t *tile_counts;
   unsigned long long *total;
+  int num_views;
+  int64_t n;  // per-view stride of the outputs, in Gaussians
 };
 
-// Forward for Gaussian i = first + t from the staged chunk; returns its tile count.
-__device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S, int t, int i) {
-  Cam c = load_cam(A.w2c, A.K);
+// Sum of the tile counts: warp reduction, one atomic per warp.
+__device__ __forceinline__ void add_total(unsigned long long *total, int count) {
+  unsigned long long c = (unsigned long long)count;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(total, c);
+}
+
+// Forward for Gaussian i = first + t and view v from the staged chunk;
+// returns its tile count.
+__device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S, int t, int i,
+                                           int v) {
+  Cam c = load_cam(A.w2c + 16 * v, A.K + 9 * v);
+  const float *campos = A.campos + 3 * v;
+  const int64_t o = (int64_t)v * A.n + i;
   const float *m = S.means + 3 * t;
   const float *s = S.scales + 3 * t;
   const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
@@ -229,7 +246,7 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
   float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = make_float4(0.f, 0.f, 0.f, 0.f);
   int count = 0;
   if (p.visible) {
-    ViewDir d = view_dir(__ldg(A.campos), __ldg(A.campos + 1), __ldg(A.campos + 2), m[0], m[1], m[2]);
+    ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), m[0], m[1], m[2]);
     float b[16];
     sh_basis(d.x, d.y, d.z, b);
     const float *r = S.rest + 45 * t;
@@ -255,22 +272,22 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
     TileRect tr = tile_rect(p.u, p.v, p.ru, p.rv, A.width, A.height);
     count = tr.empty ? 0 : (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
   }
-  A.points[i] = pt;
-  A.radii[i] = rd;
-  A.depths[i] = depth;
-  A.mask[i] = p.visible ? 1 : 0;
-  A.splat[2 * (size_t)i] = s0;
-  A.splat[2 * (size_t)i + 1] = s1;
-  A.tile_counts[i] = count;
+  A.points[o] = pt;
+  A.radii[o] = rd;
+  A.depths[o] = depth;
+  A.mask[o] = p.visible ? 1 : 0;
+  A.splat[2 * o] = s0;
+  A.splat[2 * o + 1] = s1;
+  A.tile_counts[o] = count;
   return count;
 }
 
-// Sum of the tile counts: warp reduction, one atomic per warp.
-__device__ __forceinline__ void add_total(unsigned long long *total, int count) {
-  unsigned long long c = (unsigned long long)count;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if ((threadIdx.x & 31) == 0 && c) atomicAdd(total, c);
+__device__ __forceinline__ void pre_fwd_views(const PreFwdArgs &A, const PreSmem &S, int t,
+                                              int i, bool active) {
+  for (int v = 0; v < A.num_views; ++v) {
+    const int count = active ? pre_fwd_one(A, S, t, i, v) : 0;
+    add_total(A.total + v, count);
+  }
 }
 
 // Fused forward, one chunk per block, staged with 128-bit loads. Handles
@@ -290,8 +307,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArg
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
   const int t = threadIdx.x;
-  const int count = (t < cnt) ? pre_fwd_one(A, S, t, first + t) : 0;
-  add_total(A.total, count);
+  pre_fwd_views(A, S, t, first + t, t < cnt);
 }
 
 // Bulk loads of one full chunk (kPreBlock Gaussians from `first`) into S,
@@ -348,13 +364,15 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
       return;
     }
     phase ^= 1u << s;
-    const int count = pre_fwd_one(A, stg[s], t, c * kPreBlock + t);
-    add_total(A.total, count);
+    pre_fwd_views(A, stg[s], t, c * kPreBlock + t, true);
     __syncthreads();  // every thread is done with stg[s] before it is refilled
     s ^= 1;
   }
 }
 
+// Views: camera v at w2c + 16 v, K + 9 v, campos + 3 v; its culling mask at
+// mask + v * n and its upstream gradients at g_points + v * gp_vstride,
+// g_splat + v * gs_vstride. The gradients of all views are summed.
 struct PreBwdArgs {
   const float *means, *scales, *quats, *opac, *dc, *rest, *w2c, *K, *campos;
   int width, height, sh_sigmoid;
@@ -366,37 +384,114 @@ struct PreBwdArgs {
   const float *g_splat;
   int gs_stride;
   float *g_means, *g_scales, *g_quats, *g_opac, *g_dc, *g_rest;
+  int num_views;
+  int64_t n;
+  int64_t gp_vstride, gs_vstride;
 };
 
-// Backward for Gaussian i = first + t: reads the staged parameters and
-// overwrites them in place with its gradients (zeros for culled Gaussians).
-__device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int t, int i) {
+// Gradients of one view for one Gaussian (activated parameters sx.., q, op):
+// w.r.t. the mean (projection and SH direction), the activated scale and
+// quaternion, the activated opacity, and the colour pre-activation gradient
+// g[3] with its SH basis b[16] (d colour / d sh coefficients).
+struct ViewGrads {
+  float gm[3], gsc[3], gq[4], gop, g[3], b[16];
+};
+
+__device__ __forceinline__ void view_grads(const PreBwdArgs &A, int v, int64_t i, float px,
+                                           float py, float pz, float sx, float sy, float sz,
+                                           float4 q, const float *dcc, const float *r,
+                                           ViewGrads &G) {
+  Cam c = load_cam(A.w2c + 16 * v, A.K + 9 * v);
+  const float *campos = A.campos + 3 * v;
+  float3 pc = to_camera(c, px, py, pz);
+  float3 cov = image_cov(c, A.width, A.height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
+  const float *gp = A.g_points + v * A.gp_vstride + i * A.gp_stride;
+  const float *gsp = A.g_splat + v * A.gs_vstride + i * A.gs_stride;
+  project_backward_one(c, A.width, A.height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
+                       cov, gsp[0], gsp[1], gsp[2], G.gm, G.gsc, G.gq);
+  G.gop = gsp[3];
+  ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), px, py, pz);
+  sh_basis(d.x, d.y, d.z, G.b);
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) {
+    float raw = G.b[0] * dcc[ch];
+#pragma unroll
+    for (int k = 0; k < 15; ++k) raw += G.b[k + 1] * r[k * 3 + ch];
+    float gc = gsp[4 + ch];
+    if (A.sh_sigmoid) {
+      float col = ref_sigmoid(raw);
+      gc *= col * (1.0f - col);
+    } else {
+      gc = (raw + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
+    }
+    G.g[ch] = gc;
+  }
+  float3 gmsh = sh_dir_backward(d, G.g[0], G.g[1], G.g[2], [&](int k, int ch) { return r[k * 3 + ch]; });
+  G.gm[0] += gmsh.x;
+  G.gm[1] += gmsh.y;
+  G.gm[2] += gmsh.z;
+}
+
+// Backward for Gaussian i = first + t over every view: reads the staged
+// parameters and overwrites them in place with the summed gradients (zeros
+// for a Gaussian culled in every view). With several views the SH-rest
+// gradient is summed in rest_acc (this thread's 45 floats) while the staged
+// coefficients are still needed; the activation Jacobians (exp, quaternion
+// normalisation, sigmoid) are linear and applied once to the sums.
+template <bool MULTI>
+__device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, float *rest_acc,
+                                            int t, int i) {
   float *m = S.means + 3 * t;
   float *s = S.scales + 3 * t;
   float *qq = S.quats + 4 * t;
   float *dcc = S.dc + 3 * t;
   float *r = S.rest + 45 * t;
-  float opac_grad = 0.f;
-  if (A.mask[i]) {
-    Cam c = load_cam(A.w2c, A.K);
-    float px = m[0], py = m[1], pz = m[2];
-    float sx = s[0], sy = s[1], sz = s[2];
-    float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
-    Activated act;
-    if (A.activate) {
-      act = activate_params(sx, sy, sz, q.x, q.y, q.z, q.w, S.opac[t]);
-      sx = act.sx;
-      sy = act.sy;
-      sz = act.sz;
-      q = make_float4(act.qx, act.qy, act.qz, act.qw);
+  const float px = m[0], py = m[1], pz = m[2];
+  float sx = s[0], sy = s[1], sz = s[2];
+  float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+  Activated act;
+  if (A.activate) {
+    act = activate_params(sx, sy, sz, q.x, q.y, q.z, q.w, S.opac[t]);
+    sx = act.sx;
+    sy = act.sy;
+    sz = act.sz;
+    q = make_float4(act.qx, act.qy, act.qz, act.qw);
+  }
+  float gm[3] = {0.f, 0.f, 0.f}, gsc[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
+  float gdc[3] = {0.f, 0.f, 0.f}, opac_grad = 0.f;
+  bool any = false;
+  const int views = MULTI ? A.num_views : 1;
+  if (MULTI) {
+#pragma unroll
+    for (int k = 0; k < 45; ++k) rest_acc[k] = 0.f;
+  }
+  for (int v = 0; v < views; ++v) {
+    if (!A.mask[v * A.n + i]) continue;
+    any = true;
+    ViewGrads G;
+    view_grads(A, v, i, px, py, pz, sx, sy, sz, q, dcc, r, G);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      gm[k] += G.gm[k];
+      gsc[k] += G.gsc[k];
+      gdc[k] += G.g[k] * G.b[0];
     }
-    float3 pc = to_camera(c, px, py, pz);
-    float3 cov = image_cov(c, A.width, A.height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
-    const float *gp = A.g_points + (size_t)i * A.gp_stride;
-    const float *gsp = A.g_splat + (size_t)i * A.gs_stride;
-    float gm[3], gsc[3], gq[4];
-    project_backward_one(c, A.width, A.height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
-                         cov, gsp[0], gsp[1], gsp[2], gm, gsc, gq);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) gq[k] += G.gq[k];
+    opac_grad += G.gop;
+    if (MULTI) {
+#pragma unroll
+      for (int k = 0; k < 15; ++k)
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) rest_acc[k * 3 + ch] += G.g[ch] * G.b[k + 1];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 15; ++k)
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = G.g[ch] * G.b[k + 1];
+    }
+  }
+  if (any) {
     if (A.activate) {
       // exp backward (scale), normalisation backward (quaternion)
       gsc[0] *= act.sx;
@@ -415,53 +510,24 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int
         gq[2] /= nq;
         gq[3] /= nq;
       }
+      opac_grad = opac_grad * (1.0f - act.opac) * act.opac;  // sigmoid backward
     }
-    opac_grad = gsp[3];
-    if (A.activate) opac_grad = opac_grad * (1.0f - act.opac) * act.opac;  // sigmoid backward
-
-    ViewDir d = view_dir(__ldg(A.campos), __ldg(A.campos + 1), __ldg(A.campos + 2), px, py, pz);
-    float b[16];
-    sh_basis(d.x, d.y, d.z, b);
-    float g[3];
+    if (MULTI) {
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) {
-      float raw = b[0] * dcc[ch];
-#pragma unroll
-      for (int k = 0; k < 15; ++k) raw += b[k + 1] * r[k * 3 + ch];
-      float gc = gsp[4 + ch];
-      if (A.sh_sigmoid) {
-        float col = ref_sigmoid(raw);
-        gc *= col * (1.0f - col);
-      } else {
-        gc = (raw + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
-      }
-      g[ch] = gc;
+      for (int k = 0; k < 45; ++k) r[k] = rest_acc[k];
     }
-    float3 gmsh = sh_dir_backward(d, g[0], g[1], g[2], [&](int k, int ch) { return r[k * 3 + ch]; });
-#pragma unroll
-    for (int k = 0; k < 15; ++k)
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = g[ch] * b[k + 1];
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) dcc[ch] = g[ch] * b[0];
-    m[0] = gm[0] + gmsh.x;
-    m[1] = gm[1] + gmsh.y;
-    m[2] = gm[2] + gmsh.z;
-    s[0] = gsc[0];
-    s[1] = gsc[1];
-    s[2] = gsc[2];
-    qq[0] = gq[0];
-    qq[1] = gq[1];
-    qq[2] = gq[2];
-    qq[3] = gq[3];
   } else {
-#pragma unroll
-    for (int k = 0; k < 3; ++k) m[k] = s[k] = dcc[k] = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) qq[k] = 0.f;
 #pragma unroll
     for (int k = 0; k < 45; ++k) r[k] = 0.f;
   }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    m[k] = gm[k];
+    s[k] = gsc[k];
+    dcc[k] = gdc[k];
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) qq[k] = gq[k];
   if (A.g_opac) {
     if (A.accumulate)
       A.g_opac[i] += opac_grad;
@@ -470,10 +536,16 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, int
   }
 }
 
+// Shared memory of the multi-view backward beyond its stages: the SH-rest
+// gradient accumulators, one row of 45 floats per thread.
+constexpr size_t kPreRestAccBytes = sizeof(float) * kPreBlock * 45;
+
 // Fused backward, one chunk per block (tail / unaligned fallback).
+template <bool MULTI>
 __global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdArgs A, int n, int base) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
+  float *rest_acc = reinterpret_cast<float *>(smem_raw + sizeof(PreSmem));
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
@@ -485,7 +557,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdAr
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
   const int t = threadIdx.x;
-  if (t < cnt) pre_bwd_one(A, S, t, first + t);
+  if (t < cnt) pre_bwd_one<MULTI>(A, S, rest_acc + 45 * t, t, first + t);
   __syncthreads();
   if (A.accumulate) {
     stage_add(A.g_means + 3 * f, S.means, 3 * cnt);
@@ -505,11 +577,13 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdAr
 // Fused backward, persistent and double-buffered like the forward; the
 // gradients leave shared memory through bulk stores. Before a stage is
 // refilled its stores must have read their source (bulk wait_group.read).
+template <bool MULTI>
 __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(PreBwdArgs A,
                                                                             int num_chunks,
                                                                             uint32_t *status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
+  float *rest_acc = reinterpret_cast<float *>(smem_raw + 2 * sizeof(PreSmem));
   __shared__ __align__(8) uint64_t bars[2];
   const int t = threadIdx.x;
   if (t == 0) {
@@ -542,7 +616,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
     }
     phase ^= 1u << s;
     const int i0 = c * kPreBlock;
-    pre_bwd_one(A, stg[s], t, i0 + t);
+    pre_bwd_one<MULTI>(A, stg[s], rest_acc + 45 * t, t, i0 + t);
     fence_proxy_async_smem();  // this thread's shared writes are visible to the bulk stores
     __syncthreads();
     if (t == 0) {
@@ -659,31 +733,9 @@ extern "C" int gs_evaluate_sh_backward(int n, const float *grad_colors, const fl
   return launch_status();
 }
 
-extern "C" int gs_preprocess_forward(int n, const float *means, const float *scales,
-                                     const float *quats, const float *opacities,
-                                     const float *sh_dc, const float *sh_rest,
-                                     const float *world_to_camera, const float *intrinsic,
-                                     const float *camera_pos, float near_plane,
-                                     float far_plane, float min_opacity, float min_radius,
-                                     float max_radius, int width, int height, int sh_sigmoid,
-                                     int activate, float *points_img, float *depths,
-                                     float *radii, uint8_t *mask, float *splat,
-                                     int32_t *tile_counts, int64_t *total_dev, void *stream) {
-  if (n < 0 || width <= 0 || height <= 0 || total_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)splat & 15) ||
-      ((uintptr_t)total_dev & 7))
-    return GS_ERR_INVALID_ARGUMENT;
-  cudaStream_t st = as_stream(stream);
-  int rc = cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
-  if (rc || n == 0) return rc;
-  if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
-  PreFwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
-               camera_pos, near_plane, far_plane, min_opacity, min_radius, max_radius, width,
-               height, sh_sigmoid, activate, reinterpret_cast<float2 *>(points_img), depths,
-               reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat),
-               tile_counts, reinterpret_cast<unsigned long long *>(total_dev)};
-  const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
-                       aligned16(opacities) && aligned16(sh_dc) && aligned16(sh_rest);
+static int launch_preprocess_forward(const PreFwdArgs &A, int n, cudaStream_t st) {
+  const bool pipe_ok = aligned16(A.means) && aligned16(A.scales) && aligned16(A.quats) &&
+                       aligned16(A.opac) && aligned16(A.dc) && aligned16(A.rest);
   const int full = pipe_ok ? n / kPreBlock : 0;
   if (full > 0) {
     const size_t smem = 2 * sizeof(PreSmem);
@@ -708,6 +760,131 @@ extern "C" int gs_preprocess_forward(int n, const float *means, const float *sca
   return launch_status();
 }
 
+static int preprocess_forward_impl(int n, int num_views, const float *means, const float *scales,
+                                   const float *quats, const float *opacities,
+                                   const float *sh_dc, const float *sh_rest, const float *w2c,
+                                   const float *K, const float *campos, float near_plane,
+                                   float far_plane, float min_opacity, float min_radius,
+                                   float max_radius, int width, int height, int sh_sigmoid,
+                                   int activate, float *points_img, float *depths, float *radii,
+                                   uint8_t *mask, float *splat, int32_t *tile_counts,
+                                   int64_t *totals, void *stream) {
+  if (n < 0 || num_views < 1 || width <= 0 || height <= 0 || totals == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)splat & 15) ||
+      ((uintptr_t)totals & 7))
+    return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = as_stream(stream);
+  int rc = cuda_status(cudaMemsetAsync(totals, 0, sizeof(int64_t) * num_views, st));
+  if (rc || n == 0) return rc;
+  if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  PreFwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, w2c, K, campos, near_plane,
+               far_plane, min_opacity, min_radius, max_radius, width, height, sh_sigmoid,
+               activate, reinterpret_cast<float2 *>(points_img), depths,
+               reinterpret_cast<float2 *>(radii), mask, reinterpret_cast<float4 *>(splat),
+               tile_counts, reinterpret_cast<unsigned long long *>(totals), num_views,
+               (int64_t)n};
+  return launch_preprocess_forward(A, n, st);
+}
+
+extern "C" int gs_preprocess_forward(int n, const float *means, const float *scales,
+                                     const float *quats, const float *opacities,
+                                     const float *sh_dc, const float *sh_rest,
+                                     const float *world_to_camera, const float *intrinsic,
+                                     const float *camera_pos, float near_plane,
+                                     float far_plane, float min_opacity, float min_radius,
+                                     float max_radius, int width, int height, int sh_sigmoid,
+                                     int activate, float *points_img, float *depths,
+                                     float *radii, uint8_t *mask, float *splat,
+                                     int32_t *tile_counts, int64_t *total_dev, void *stream) {
+  return preprocess_forward_impl(n, 1, means, scales, quats, opacities, sh_dc, sh_rest,
+                                 world_to_camera, intrinsic, camera_pos, near_plane, far_plane,
+                                 min_opacity, min_radius, max_radius, width, height, sh_sigmoid,
+                                 activate, points_img, depths, radii, mask, splat, tile_counts,
+                                 total_dev, stream);
+}
+
+extern "C" int gs_preprocess_forward_views(
+    int n, int num_views, const float *means, const float *scales, const float *quats,
+    const float *opacities, const float *sh_dc, const float *sh_rest,
+    const float *world_to_cameras, const float *intrinsics, const float *camera_positions,
+    float near_plane, float far_plane, float min_opacity, float min_radius, float max_radius,
+    int width, int height, int sh_sigmoid, int activate, float *points_img, float *depths,
+    float *radii, uint8_t *mask, float *splat, int32_t *tile_counts, int64_t *totals,
+    void *stream) {
+  return preprocess_forward_impl(n, num_views, means, scales, quats, opacities, sh_dc, sh_rest,
+                                 world_to_cameras, intrinsics, camera_positions, near_plane,
+                                 far_plane, min_opacity, min_radius, max_radius, width, height,
+                                 sh_sigmoid, activate, points_img, depths, radii, mask, splat,
+                                 tile_counts, totals, stream);
+}
+
+template <bool MULTI>
+static int launch_preprocess_backward(const PreBwdArgs &A, int n, cudaStream_t st) {
+  const bool pipe_ok = aligned16(A.means) && aligned16(A.scales) && aligned16(A.quats) &&
+                       (!A.activate || aligned16(A.opac)) && aligned16(A.dc) &&
+                       aligned16(A.rest) && aligned16(A.g_means) && aligned16(A.g_scales) &&
+                       aligned16(A.g_quats) && aligned16(A.g_dc) && aligned16(A.g_rest);
+  const int full = pipe_ok ? n / kPreBlock : 0;
+  const size_t extra = MULTI ? kPreRestAccBytes : 0;
+  if (full > 0) {
+    const size_t smem = 2 * sizeof(PreSmem) + extra;
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaFuncSetAttribute(preprocess_backward_pipe_kernel<MULTI>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done[dev] = 1;
+    }
+    const int grid = pipe_grid(full, (const void *)preprocess_backward_pipe_kernel<MULTI>, smem);
+    preprocess_backward_pipe_kernel<MULTI>
+        <<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
+    count_launch();
+  }
+  const int base = full * kPreBlock;
+  if (base < n) {
+    const size_t smem = sizeof(PreSmem) + extra;
+    static int attr_done1[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done1[dev]) {
+      cudaFuncSetAttribute(preprocess_backward_kernel<MULTI>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_done1[dev] = 1;
+    }
+    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
+    preprocess_backward_kernel<MULTI><<<blocks, kPreBlock, smem, st>>>(A, n, base);
+    count_launch();
+  }
+  return launch_status();
+}
+
+static int preprocess_backward_impl(int n, int num_views, const float *means,
+                                    const float *scales, const float *quats,
+                                    const float *opacities, const float *sh_dc,
+                                    const float *sh_rest, const float *w2c, const float *K,
+                                    const float *campos, int width, int height, int sh_sigmoid,
+                                    int activate, int accumulate, const uint8_t *mask,
+                                    const float *grad_points_img, int gp_stride,
+                                    const float *grad_splat, int gs_stride, float *grad_means,
+                                    float *grad_scales, float *grad_quats,
+                                    float *grad_opacities, float *grad_dc, float *grad_rest,
+                                    void *stream) {
+  if (n < 0 || num_views < 1 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (activate && opacities == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return GS_OK;
+  cudaStream_t st = as_stream(stream);
+  PreBwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, w2c, K, campos, width, height,
+               sh_sigmoid, activate, accumulate, mask, grad_points_img, gp_stride, grad_splat,
+               gs_stride, grad_means, grad_scales, grad_quats, grad_opacities, grad_dc,
+               grad_rest, num_views, (int64_t)n, (int64_t)n * gp_stride,
+               (int64_t)n * gs_stride};
+  return num_views > 1 ? launch_preprocess_backward<true>(A, n, st)
+                       : launch_preprocess_backward<false>(A, n, st);
+}
+
 extern "C" int gs_preprocess_backward(int n, const float *means, const float *scales,
                                       const float *quats, const float *opacities,
                                       const float *sh_dc, const float *sh_rest,
@@ -719,40 +896,24 @@ extern "C" int gs_preprocess_backward(int n, const float *means, const float *sc
                                       float *grad_means, float *grad_scales, float *grad_quats,
                                       float *grad_opacities, float *grad_dc, float *grad_rest,
                                       void *stream) {
-  if (n < 0 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
-    return GS_ERR_INVALID_ARGUMENT;
-  if (activate && opacities == nullptr) return GS_ERR_INVALID_ARGUMENT;
-  if (n == 0) return GS_OK;
-  cudaStream_t st = as_stream(stream);
-  PreBwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, world_to_camera, intrinsic,
-               camera_pos, width, height, sh_sigmoid, activate, accumulate, mask,
-               grad_points_img, gp_stride, grad_splat, gs_stride, grad_means, grad_scales,
-               grad_quats, grad_opacities, grad_dc, grad_rest};
-  const bool pipe_ok = aligned16(means) && aligned16(scales) && aligned16(quats) &&
-                       (!activate || aligned16(opacities)) &&
-                       aligned16(sh_dc) && aligned16(sh_rest) && aligned16(grad_means) &&
-                       aligned16(grad_scales) && aligned16(grad_quats) && aligned16(grad_dc) &&
-                       aligned16(grad_rest);
-  const int full = pipe_ok ? n / kPreBlock : 0;
-  if (full > 0) {
-    const size_t smem = 2 * sizeof(PreSmem);
-    static int attr_done[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-      cudaFuncSetAttribute(preprocess_backward_pipe_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[dev] = 1;
-    }
-    const int grid = pipe_grid(full, (const void *)preprocess_backward_pipe_kernel, smem);
-    preprocess_backward_pipe_kernel<<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
-    count_launch();
-  }
-  const int base = full * kPreBlock;
-  if (base < n) {
-    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
-    preprocess_backward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(A, n, base);
-    count_launch();
-  }
-  return launch_status();
+  return preprocess_backward_impl(n, 1, means, scales, quats, opacities, sh_dc, sh_rest,
+                                  world_to_camera, intrinsic, camera_pos, width, height,
+                                  sh_sigmoid, activate, accumulate, mask, grad_points_img,
+                                  gp_stride, grad_splat, gs_stride, grad_means, grad_scales,
+                                  grad_quats, grad_opacities, grad_dc, grad_rest, stream);
+}
+
+extern "C" int gs_preprocess_backward_views(
+    int n, int num_views, const float *means, const float *scales, const float *quats,
+    const float *opacities, const float *sh_dc, const float *sh_rest,
+    const float *world_to_cameras, const float *intrinsics, const float *camera_positions,
+    int width, int height, int sh_sigmoid, int activate, int accumulate, const uint8_t *mask,
+    const float *grad_points_img, int gp_stride, const float *grad_splat, int gs_stride,
+    float *grad_means, float *grad_scales, float *grad_quats, float *grad_opacities,
+    float *grad_dc, float *grad_rest, void *stream) {
+  return preprocess_backward_impl(n, num_views, means, scales, quats, opacities, sh_dc, sh_rest,
+                                  world_to_cameras, intrinsics, camera_positions, width, height,
+                                  sh_sigmoid, activate, accumulate, mask, grad_points_img,
+                                  gp_stride, grad_splat, gs_stride, grad_means, grad_scales,
+                                  grad_quats, grad_opacities, grad_dc, grad_rest, stream);
 }

@@ -15,9 +15,12 @@ views sharded across ranks:
 * the clamp*255 of render() and the loss with its gradient in one kernel
   (L1, or with ssim_lambda > 0 the reference's (1 - lambda) L1 +
   lambda (1 - SSIM) of scripts/train.py:186-203, in two kernels);
-* each view's raw-parameter gradients added straight into the flat gradient
-  buffer by the preprocess backward (TMA bulk reduce-add), so neither
-  autograd nor a per-view gradient copy is involved;
+* every view's preprocess in one launch that reads each Gaussian's
+  parameters once (gs_preprocess_forward_views), and every view's
+  raw-parameter gradients summed on chip by one multi-view preprocess
+  backward written straight into the flat gradient buffer
+  (gs_preprocess_backward_views), so neither autograd nor a per-view
+  gradient pass over the parameters is involved;
 * the optimizer step of dp.FlatParams: one NCCL all-reduce of the flat
   gradient (world > 1) and the one-launch Adam, or with fused_dp one kernel
   that reduce-scatters the gradient over NVLink / NVSwitch, applies Adam to
@@ -93,22 +96,26 @@ class NativeTrainer:
         campos = (-(w2c[:, :3, :3].transpose(1, 2) @ w2c[:, :3, 3:4])).squeeze(-1).contiguous()
         totals = torch.empty(V, dtype=torch.int64, device=dev)
         f = dict(device=dev, dtype=torch.float32)
+        # every view's preprocess outputs in (V, n, ...) arrays, filled by one
+        # launch that reads each Gaussian's parameters once for all views
+        batch = dict(points=torch.empty((V, n, 2), **f), depths=torch.empty((V, n), **f),
+                     radii=torch.empty((V, n, 2), **f),
+                     mask=torch.empty((V, n), device=dev, dtype=torch.uint8),
+                     splat=torch.empty((V, n, 8), **f),
+                     counts=torch.empty((V, max(n, 1)), device=dev, dtype=torch.int32))
+        nat.call("gs_preprocess_forward_views", n, V, self._ptr("means"), self._ptr("scales"),
+                 self._ptr("quaternions"), self._ptr("opacities"), self._ptr("sh_coeffs_dc"),
+                 self._ptr("sh_coeffs_rest"), w2c.data_ptr(), Ks.data_ptr(), campos.data_ptr(),
+                 o["near_plane"], o["far_plane"], o["min_opacity"], o["min_radius"],
+                 o["max_radius"], W, H, 0, 1, batch["points"].data_ptr(),
+                 batch["depths"].data_ptr(), batch["radii"].data_ptr(), batch["mask"].data_ptr(),
+                 batch["splat"].data_ptr(), batch["counts"].data_ptr(), totals.data_ptr(), st)
         views = []
         for v in range(V):
-            s = dict(points=torch.empty((n, 2), **f), depths=torch.empty((n,), **f),
-                     radii=torch.empty((n, 2), **f),
-                     mask=torch.empty((n,), device=dev, dtype=torch.uint8),
-                     splat=torch.empty((n, 8), **f),
-                     counts=torch.empty((max(n, 1),), device=dev, dtype=torch.int32),
-                     w2c=w2c[v], K=Ks[v], campos=campos[v])
-            nat.call("gs_preprocess_forward", n, self._ptr("means"), self._ptr("scales"),
-                     self._ptr("quaternions"), self._ptr("opacities"), self._ptr("sh_coeffs_dc"),
-                     self._ptr("sh_coeffs_rest"), s["w2c"].data_ptr(), s["K"].data_ptr(),
-                     s["campos"].data_ptr(), o["near_plane"], o["far_plane"], o["min_opacity"],
-                     o["min_radius"], o["max_radius"], W, H, 0, 1, s["points"].data_ptr(),
-                     s["depths"].data_ptr(), s["radii"].data_ptr(), s["mask"].data_ptr(),
-                     s["splat"].data_ptr(), s["counts"].data_ptr(), totals[v:].data_ptr(), st)
+            s = {k: t[v] for k, t in batch.items()}
+            s.update(w2c=w2c[v], K=Ks[v], campos=campos[v])
             views.append(s)
+        self._batch = dict(batch, w2c=w2c, K=Ks, campos=campos)
         # one host synchronisation for every view's pair count
         host_totals = totals.cpu()
         rc = nat.query("gs_check_status", st)
@@ -133,9 +140,10 @@ class NativeTrainer:
         """Loss of every view against its target (H, W, 3; float in [0, 255]
         or uint8) -- L1, or (1 - ssim_lambda) L1 + ssim_lambda (1 - SSIM)
         when ssim_lambda > 0 -- and the backward into the flat gradient buffer.
-        The first view's gradients overwrite the buffer (every element is
-        written, zeros for Gaussians it culled) unless `accumulate`; later
-        views add to it. Returns the per-view losses (device tensor)."""
+        The views' gradients are summed by one multi-view preprocess backward
+        and overwrite the buffer (every element is written, zeros for
+        Gaussians every view culled) unless `accumulate`, which adds them.
+        Returns the per-view losses (device tensor)."""
         o = self.opts
         dev = self.device
         st = nat.stream_ptr(dev)
@@ -148,9 +156,11 @@ class NativeTrainer:
         if lam > 0 and self._ssim_scratch is None:
             self._ssim_scratch = torch.empty(nat.query("gs_ssim_scratch_bytes", 3, H, W) // 4,
                                              device=dev, dtype=torch.float32)
-        g_points = torch.empty((n, 2), device=dev, dtype=torch.float32)
-        g_splat = torch.empty((n, 8), device=dev, dtype=torch.float32)
+        # every view's blend gradients, consumed by one multi-view preprocess backward
+        g_points_all = torch.zeros((V, n, 2), device=dev, dtype=torch.float32)
+        g_splat_all = torch.zeros((V, n, 8), device=dev, dtype=torch.float32)
         for v, s in enumerate(views):
+            g_points, g_splat = g_points_all[v], g_splat_all[v]
             tgt = targets[v]
             if tgt.device != dev or not tgt.is_contiguous():
                 tgt = tgt.to(dev).contiguous()
@@ -165,8 +175,6 @@ class NativeTrainer:
                 nat.call("gs_l1_loss_grad", npx, s["image"].data_ptr(), tgt.data_ptr(),
                          int(tgt.dtype == torch.uint8), grad_img.data_ptr(),
                          loss_sums[v].data_ptr(), st)
-            g_points.zero_()
-            g_splat.zero_()
             nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
                      s["total"], s["ids"].data_ptr(), n, s["points"].data_ptr(),
                      s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
@@ -175,15 +183,16 @@ class NativeTrainer:
                      g_points.data_ptr(), g_splat.data_ptr(), st)
             if self.strategy is not None:  # strategy.py:48-72, per view
                 self.strategy.accumulate(g_points, s["radii"], W, H)
-            nat.call("gs_preprocess_backward", n, self._ptr("means"), self._ptr("scales"),
-                     self._ptr("quaternions"), self._ptr("opacities"),
-                     self._ptr("sh_coeffs_dc"), self._ptr("sh_coeffs_rest"), s["w2c"].data_ptr(),
-                     s["K"].data_ptr(), s["campos"].data_ptr(), W, H, 0, 1,
-                     int(accumulate or v > 0),
-                     s["mask"].data_ptr(), g_points.data_ptr(), 2, g_splat.data_ptr(), 8,
-                     self._gptr("means"), self._gptr("scales"), self._gptr("quaternions"),
-                     self._gptr("opacities"), self._gptr("sh_coeffs_dc"),
-                     self._gptr("sh_coeffs_rest"), st)
+        b = self._batch
+        if V != b["mask"].shape[0]:
+            raise ValueError("loss_and_backward takes the views of the last forward_views call")
+        nat.call("gs_preprocess_backward_views", n, V, self._ptr("means"), self._ptr("scales"),
+                 self._ptr("quaternions"), self._ptr("opacities"), self._ptr("sh_coeffs_dc"),
+                 self._ptr("sh_coeffs_rest"), b["w2c"].data_ptr(), b["K"].data_ptr(),
+                 b["campos"].data_ptr(), W, H, 0, 1, int(accumulate), b["mask"].data_ptr(),
+                 g_points_all.data_ptr(), 2, g_splat_all.data_ptr(), 8, self._gptr("means"),
+                 self._gptr("scales"), self._gptr("quaternions"), self._gptr("opacities"),
+                 self._gptr("sh_coeffs_dc"), self._gptr("sh_coeffs_rest"), st)
         l1 = loss_sums[:, 0] / npx
         if lam == 0:
             return l1

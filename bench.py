@@ -54,6 +54,9 @@ FALLBACK_BF16_TFLOPS = 1590.0
 PRE_FWD_BYTES_PER_G = 281
 PRE_BWD_BYTES_PER_G = 504
 LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
+PARAM_BYTES_PER_G = 236     # the 59 fp32 parameters of one Gaussian
+PRE_OUT_BYTES_PER_G = 45    # per view: points 8, depth 4, conic 12, radii 8, rgb 12, mask 1
+PRE_UP_BYTES_PER_G = 40     # per view: upstream gradients of points (8) and splat (32)
 # 8-rank NCCL all-reduce bus bandwidth at 1 GiB measured on this pool's B200s (GB/s): the
 # reference figure for the fused data-parallel optimizer step
 NVLINK_ALLREDUCE_BUS_GBS = 725.0
@@ -167,7 +170,7 @@ class StageTimer:
 
     WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_blend_forward", "gs_blend_backward",
              "gs_preprocess_backward", "gs_l1_loss_grad", "gs_l1_ssim_loss_grad", "gs_adam_step",
-             "gs_dp_adam_step")
+             "gs_dp_adam_step", "gs_preprocess_forward_views", "gs_preprocess_backward_views")
 
     def __init__(self):
         self.events = {k: [] for k in self.WATCH}
@@ -598,6 +601,22 @@ def main():
         gbs = PRE_BWD_BYTES_PER_G * n / (stage_ms["gs_preprocess_backward"] * 1e-3) / 1e9
         roof["preprocess_bwd"] = {"bound": "hbm", "ms": stage_ms["gs_preprocess_backward"],
                                   "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    # multi-view launches (NativeTrainer): one launch covers this rank's V views; the
+    # algorithmic bytes are those of the fused operation -- parameters read once, every
+    # view's outputs written (forward); parameters and every view's upstream gradients
+    # read, the summed gradient written once (backward)
+    if stage_ms.get("gs_preprocess_forward_views"):
+        ms = stage_ms["gs_preprocess_forward_views"]
+        gbs = (PARAM_BYTES_PER_G + PRE_OUT_BYTES_PER_G * V) * n / (ms * 1e-3) / 1e9
+        roof["preprocess_fwd"] = {"bound": "hbm", "ms": ms / V, "ms_per_launch": ms,
+                                  "views_per_launch": V, "achieved": gbs, "peak": hbm,
+                                  "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_preprocess_backward_views"):
+        ms = stage_ms["gs_preprocess_backward_views"]
+        gbs = (2 * PARAM_BYTES_PER_G + PRE_UP_BYTES_PER_G * V) * n / (ms * 1e-3) / 1e9
+        roof["preprocess_bwd"] = {"bound": "hbm", "ms": ms / V, "ms_per_launch": ms,
+                                  "views_per_launch": V, "achieved": gbs, "peak": hbm,
+                                  "unit": "GB/s", "frac": gbs / hbm}
     if stage_ms.get("gs_tile_layout"):
         gbs = (LAYOUT_BYTES_PER_PAIR * K + 4 * T) / (stage_ms["gs_tile_layout"] * 1e-3) / 1e9
         roof["tile_layout"] = {"bound": "hbm", "ms": stage_ms["gs_tile_layout"], "achieved": gbs,

@@ -242,6 +242,40 @@ GS_API int gs_preprocess_backward(int n, const float *means, const float *scales
                            float *grad_scales, float *grad_quats, float *grad_opacities,
                            float *grad_dc, float *grad_rest, void *stream);
 
+/* gs_preprocess_forward for num_views cameras in one launch: each chunk of
+ * parameters is read from HBM once and projected into every view. Camera v:
+ * world_to_cameras + 16 v, intrinsics + 9 v, camera_positions + 3 v. Outputs
+ * are (num_views, n, ...) arrays (view v's rows at element offset v * n of
+ * each; splat (num_views, n, 8)), totals[v] the pair count of view v. No
+ * counterpart in the reference, which preprocesses one view per call. */
+GS_API int gs_preprocess_forward_views(int n, int num_views, const float *means,
+                                       const float *scales, const float *quats,
+                                       const float *opacities, const float *sh_dc,
+                                       const float *sh_rest, const float *world_to_cameras,
+                                       const float *intrinsics, const float *camera_positions,
+                                       float near_plane, float far_plane, float min_opacity,
+                                       float min_radius, float max_radius, int width, int height,
+                                       int sh_sigmoid, int activate, float *points_img,
+                                       float *depths, float *radii, uint8_t *mask, float *splat,
+                                       int32_t *tile_counts, int64_t *totals, void *stream);
+
+/* gs_preprocess_backward summed over num_views cameras in one launch: the
+ * parameters are read once, the gradients written (or added) once. mask is
+ * (num_views, n); view v's upstream gradients start at grad_points_img +
+ * v * n * gp_stride and grad_splat + v * n * gs_stride. */
+GS_API int gs_preprocess_backward_views(int n, int num_views, const float *means,
+                                        const float *scales, const float *quats,
+                                        const float *opacities, const float *sh_dc,
+                                        const float *sh_rest, const float *world_to_cameras,
+                                        const float *intrinsics, const float *camera_positions,
+                                        int width, int height, int sh_sigmoid, int activate,
+                                        int accumulate, const uint8_t *mask,
+                                        const float *grad_points_img, int gp_stride,
+                                        const float *grad_splat, int gs_stride,
+                                        float *grad_means, float *grad_scales,
+                                        float *grad_quats, float *grad_opacities, float *grad_dc,
+                                        float *grad_rest, void *stream);
+
 /* ---- training step helpers -------------------------------------------------
  * One-launch Adam over a flat fp32 buffer holding consecutive parameter
  * groups (group k = elements [group_ends[k-1], group_ends[k]), host arrays of

@@ -537,3 +537,67 @@ def test_native_trainer_step_matches_autograd_path(gs, u8, lam):
     for k in p:
         a, n = tr.fp.spans[k]
         assert_close_metric(k, np_(tr.fp.grad[a:a + n]), np_(p[k].grad).ravel(), 0.9999, 1e-3)
+
+
+@pytest.mark.parametrize("n", [4000, 4000 + 37])
+def test_multi_view_preprocess_matches_per_view(gs, n):
+    """gs_preprocess_forward_views equals one gs_preprocess_forward per view
+    (bit for bit), and gs_preprocess_backward_views equals the per-view
+    backward calls accumulated (summation order aside); n not a multiple of
+    the chunk size exercises the tail kernel."""
+    nat = importlib.import_module("3dgs_from_scratch_b200._native")
+    cfg = gs.scenes.CONFIGS[0]
+    raw = {k: v.to(DEV) for k, v in gs.scenes.make_gaussians(cfg, seed=9, n=n).items()}
+    V, W, H = 3, 200, 150
+    w2c = gs.scenes.orbit_cameras(cfg, V).to(DEV).contiguous()
+    K = torch.tensor([[180.0, 0, 100], [0, 180.0, 75], [0, 0, 1]], device=DEV)
+    Ks = K.expand(V, 3, 3).contiguous()
+    campos = (-(w2c[:, :3, :3].transpose(1, 2) @ w2c[:, :3, 3:4])).squeeze(-1).contiguous()
+    st = nat.stream_ptr()
+    p = [raw[k].data_ptr() for k in ("means", "scales", "quaternions", "opacities",
+                                     "sh_coeffs_dc", "sh_coeffs_rest")]
+    f = dict(device=DEV, dtype=torch.float32)
+
+    def outs(shape_v):
+        return dict(points=torch.empty(shape_v + (n, 2), **f), depths=torch.empty(shape_v + (n,), **f),
+                    radii=torch.empty(shape_v + (n, 2), **f),
+                    mask=torch.empty(shape_v + (n,), device=DEV, dtype=torch.uint8),
+                    splat=torch.empty(shape_v + (n, 8), **f),
+                    counts=torch.empty(shape_v + (n,), device=DEV, dtype=torch.int32))
+    opts = (0.01, 100.0, 1 / 255, 0.5, 128.0, W, H, 0, 1)
+    b = outs((V,))
+    totals = torch.empty(V, dtype=torch.int64, device=DEV)
+    nat.call("gs_preprocess_forward_views", n, V, *p, w2c.data_ptr(), Ks.data_ptr(),
+             campos.data_ptr(), *opts, b["points"].data_ptr(), b["depths"].data_ptr(),
+             b["radii"].data_ptr(), b["mask"].data_ptr(), b["splat"].data_ptr(),
+             b["counts"].data_ptr(), totals.data_ptr(), st)
+    for v in range(V):
+        o = outs(())
+        tot = torch.empty(1, dtype=torch.int64, device=DEV)
+        nat.call("gs_preprocess_forward", n, *p, w2c[v].data_ptr(), Ks[v].data_ptr(),
+                 campos[v].data_ptr(), *opts, o["points"].data_ptr(), o["depths"].data_ptr(),
+                 o["radii"].data_ptr(), o["mask"].data_ptr(), o["splat"].data_ptr(),
+                 o["counts"].data_ptr(), tot.data_ptr(), st)
+        for k in o:
+            assert torch.equal(o[k], b[k][v]), k
+        assert int(tot) == int(totals[v])
+    assert int(b["mask"].sum()) > 100
+    # backward
+    g = torch.Generator(device=DEV).manual_seed(2)
+    gp = torch.randn((V, n, 2), device=DEV, generator=g) * 1e-3
+    gsp = torch.randn((V, n, 8), device=DEV, generator=g) * 1e-3
+    numel = sum(raw[k].numel() for k in raw)
+    grads_multi = {k: torch.empty_like(raw[k]) for k in raw}
+    grads_ref = {k: torch.zeros_like(raw[k]) for k in raw}
+    order = ("means", "scales", "quaternions", "opacities", "sh_coeffs_dc", "sh_coeffs_rest")
+    nat.call("gs_preprocess_backward_views", n, V, *p, w2c.data_ptr(), Ks.data_ptr(),
+             campos.data_ptr(), W, H, 0, 1, 0, b["mask"].data_ptr(), gp.data_ptr(), 2,
+             gsp.data_ptr(), 8, *[grads_multi[k].data_ptr() for k in order], st)
+    for v in range(V):
+        nat.call("gs_preprocess_backward", n, *p, w2c[v].data_ptr(), Ks[v].data_ptr(),
+                 campos[v].data_ptr(), W, H, 0, 1, 1, b["mask"][v].data_ptr(),
+                 gp[v].data_ptr(), 2, gsp[v].data_ptr(), 8,
+                 *[grads_ref[k].data_ptr() for k in order], st)
+    del numel
+    for k in order:
+        assert_close_metric(k, np_(grads_multi[k]), np_(grads_ref[k]), 0.999999, 1e-5)
