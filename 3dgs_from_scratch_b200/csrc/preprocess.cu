@@ -213,13 +213,6 @@ struct PreFwdArgs {
   int64_t n;  // per-view stride of the outputs, in Gaussians
 };
 
-// Sum of the tile counts: warp reduction, one atomic per warp.
-__device__ __forceinline__ void add_total(unsigned long long *total, int count) {
-  unsigned long long c = (unsigned long long)count;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if ((threadIdx.x & 31) == 0 && c) atomicAdd(total, c);
-}
 
 // Forward for Gaussian i = first + t and view v from the staged chunk;
 // returns its tile count.
@@ -282,20 +275,43 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
   return count;
 }
 
+// All views of one staged chunk. The pair counts go to the block's per-view
+// partial sums in shared memory (s_tot, one warp-reduced shared atomic per
+// warp and view; a chunk's sum is below 128 * 2^24 tiles, so 32 bits hold
+// it), added to the global totals once per chunk: one global atomic per
+// view per chunk rather than per warp (same-address atomics from every warp
+// of every view serialise in L2).
 __device__ __forceinline__ void pre_fwd_views(const PreFwdArgs &A, const PreSmem &S, int t,
-                                              int i, bool active) {
+                                              int i, bool active, uint32_t *s_tot) {
   for (int v = 0; v < A.num_views; ++v) {
-    const int count = active ? pre_fwd_one(A, S, t, i, v) : 0;
-    add_total(A.total + v, count);
+    int count = active ? pre_fwd_one(A, S, t, i, v) : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) count += __shfl_xor_sync(0xffffffffu, count, o);
+    if ((threadIdx.x & 31) == 0 && count) atomicAdd(s_tot + v, (uint32_t)count);
   }
+}
+
+__device__ __forceinline__ void flush_totals(const PreFwdArgs &A, const uint32_t *s_tot) {
+  __syncthreads();
+  for (int v = threadIdx.x; v < A.num_views; v += blockDim.x)
+    if (s_tot[v]) atomicAdd(A.total + v, (unsigned long long)s_tot[v]);
+}
+
+__device__ __forceinline__ void zero_totals(const PreFwdArgs &A, uint32_t *s_tot) {
+  for (int v = threadIdx.x; v < A.num_views; v += blockDim.x) s_tot[v] = 0u;
 }
 
 // Fused forward, one chunk per block, staged with 128-bit loads. Handles
 // Gaussians [base, n) (any alignment); used for the tail of the pipelined
 // kernel and when a pointer is not 16-byte aligned.
+// One chunk per block. Dynamic shared memory: the chunk stage, then
+// num_views per-view partial totals.
 __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArgs A, int n, int base) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
+  uint32_t *s_tot = reinterpret_cast<uint32_t *>(smem_raw + sizeof(PreSmem));
+  zero_totals(A, s_tot);
+  const int t = threadIdx.x;
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
@@ -306,8 +322,8 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArg
   stage(S.dc, A.dc + 3 * f, 3 * cnt);
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
-  const int t = threadIdx.x;
-  pre_fwd_views(A, S, t, first + t, t < cnt);
+  pre_fwd_views(A, S, t, first + t, t < cnt, s_tot);
+  flush_totals(A, s_tot);
 }
 
 // Bulk loads of one full chunk (kPreBlock Gaussians from `first`) into S,
@@ -334,8 +350,10 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
                                                                            uint32_t *status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
+  uint32_t *s_tot = reinterpret_cast<uint32_t *>(smem_raw + 2 * sizeof(PreSmem));
   __shared__ __align__(8) uint64_t bars[2];
   const int t = threadIdx.x;
+  zero_totals(A, s_tot);
   if (t == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -364,8 +382,10 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
       return;
     }
     phase ^= 1u << s;
-    pre_fwd_views(A, stg[s], t, c * kPreBlock + t, true);
-    __syncthreads();  // every thread is done with stg[s] before it is refilled
+    pre_fwd_views(A, stg[s], t, c * kPreBlock + t, true, s_tot);
+    flush_totals(A, s_tot);  // per chunk: the 32-bit partials cannot overflow
+    __syncthreads();  // every thread is done with stg[s] (and s_tot) before reuse
+    zero_totals(A, s_tot);
     s ^= 1;
   }
 }
@@ -540,9 +560,17 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, flo
 // gradient accumulators, one row of 45 floats per thread.
 constexpr size_t kPreRestAccBytes = sizeof(float) * kPreBlock * 45;
 
+#ifndef GS_PRE_MULTI_MINB
+#define GS_PRE_MULTI_MINB 3  // resident blocks per SM the multi-view register budget targets
+#endif
+#ifndef GS_PRE_MULTI_SIMPLE
+#define GS_PRE_MULTI_SIMPLE 1  // 1: the multi-view backward stages chunks with plain loads
+#endif
+
 // Fused backward, one chunk per block (tail / unaligned fallback).
 template <bool MULTI>
-__global__ void __launch_bounds__(kPreBlock) preprocess_backward_kernel(PreBwdArgs A, int n, int base) {
+__global__ void __launch_bounds__(kPreBlock, MULTI ? GS_PRE_MULTI_MINB : 1)
+    preprocess_backward_kernel(PreBwdArgs A, int n, int base) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
   float *rest_acc = reinterpret_cast<float *>(smem_raw + sizeof(PreSmem));
@@ -644,18 +672,14 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// Grid of a persistent kernel: every SM filled to its occupancy for this
+// kernel and shared-memory size (queried per call: both vary by caller).
 static int pipe_grid(int num_chunks, const void *kernel, size_t smem) {
-  static int cached[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   int per_sm = 0;
-  if (dev >= 0 && dev < 64 && cached[dev]) {
-    per_sm = cached[dev];
-  } else {
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kPreBlock, smem);
-    if (per_sm < 1) per_sm = 1;
-    if (dev >= 0 && dev < 64) cached[dev] = per_sm;
-  }
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kPreBlock, smem);
+  if (per_sm < 1) per_sm = 1;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int g = sms * per_sm;
@@ -733,28 +757,32 @@ extern "C" int gs_evaluate_sh_backward(int n, const float *grad_colors, const fl
   return launch_status();
 }
 
+#ifndef GS_PRE_FWD_MULTI_SIMPLE
+#define GS_PRE_FWD_MULTI_SIMPLE 1  // 1: the multi-view forward stages chunks with plain loads
+#endif
+
 static int launch_preprocess_forward(const PreFwdArgs &A, int n, cudaStream_t st) {
   const bool pipe_ok = aligned16(A.means) && aligned16(A.scales) && aligned16(A.quats) &&
-                       aligned16(A.opac) && aligned16(A.dc) && aligned16(A.rest);
+                       aligned16(A.opac) && aligned16(A.dc) && aligned16(A.rest) &&
+                       !(A.num_views > 1 && GS_PRE_FWD_MULTI_SIMPLE);
   const int full = pipe_ok ? n / kPreBlock : 0;
+  const size_t tot_bytes = sizeof(uint32_t) * (size_t)A.num_views;
+  if (2 * sizeof(PreSmem) + tot_bytes > 200 * 1024) return GS_ERR_CAPACITY;  // views per launch
   if (full > 0) {
-    const size_t smem = 2 * sizeof(PreSmem);
-    static int attr_done[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-      cudaFuncSetAttribute(preprocess_forward_pipe_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[dev] = 1;
-    }
+    const size_t smem = 2 * sizeof(PreSmem) + tot_bytes;
+    cudaFuncSetAttribute(preprocess_forward_pipe_kernel,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int grid = pipe_grid(full, (const void *)preprocess_forward_pipe_kernel, smem);
     preprocess_forward_pipe_kernel<<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
     count_launch();
   }
   const int base = full * kPreBlock;
   if (base < n) {
-    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
-    preprocess_forward_kernel<<<blocks, kPreBlock, sizeof(PreSmem), st>>>(A, n, base);
+    const size_t smem = sizeof(PreSmem) + tot_bytes;
+    cudaFuncSetAttribute(preprocess_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    const int blocks = (n - base + kPreBlock - 1) / kPreBlock;  // one chunk per block
+    preprocess_forward_kernel<<<blocks, kPreBlock, smem, st>>>(A, n, base);
     count_launch();
   }
   return launch_status();
@@ -825,7 +853,7 @@ static int launch_preprocess_backward(const PreBwdArgs &A, int n, cudaStream_t s
                        (!A.activate || aligned16(A.opac)) && aligned16(A.dc) &&
                        aligned16(A.rest) && aligned16(A.g_means) && aligned16(A.g_scales) &&
                        aligned16(A.g_quats) && aligned16(A.g_dc) && aligned16(A.g_rest);
-  const int full = pipe_ok ? n / kPreBlock : 0;
+  const int full = (pipe_ok && !(MULTI && GS_PRE_MULTI_SIMPLE)) ? n / kPreBlock : 0;
   const size_t extra = MULTI ? kPreRestAccBytes : 0;
   if (full > 0) {
     const size_t smem = 2 * sizeof(PreSmem) + extra;
