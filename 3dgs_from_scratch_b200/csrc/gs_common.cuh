@@ -499,18 +499,19 @@ __device__ __forceinline__ float3 sh_dir_backward(const ViewDir &d, float g0, fl
   float in = d.inv_norm;
   float j00 = (1.0f - xx) * in, j01 = -xy * in, j02 = -xz * in;
   float j11 = (1.0f - yy) * in, j12 = -yz * in, j22 = (1.0f - zz) * in;
-  float gx = 0.f, gy = 0.f, gz = 0.f;
+  // d/d(unnormalised direction) = J^T d/d(unit direction), J symmetric: sum
+  // the basis derivatives weighted by s_k = sum_ch g_ch rest[k][ch] first,
+  // then apply J once
+  float tx = 0.f, ty = 0.f, tz = 0.f;
 #pragma unroll
   for (int k = 0; k < 15; ++k) {
-    float px = bx[k] * j00 + by[k] * j01 + bz[k] * j02;
-    float py = bx[k] * j01 + by[k] * j11 + bz[k] * j12;
-    float pz = bx[k] * j02 + by[k] * j12 + bz[k] * j22;
-    float r0 = rest(k, 0), r1 = rest(k, 1), r2 = rest(k, 2);
-    gx += g0 * r0 * px + g1 * r1 * px + g2 * r2 * px;
-    gy += g0 * r0 * py + g1 * r1 * py + g2 * r2 * py;
-    gz += g0 * r0 * pz + g1 * r1 * pz + g2 * r2 * pz;
+    const float sk = g0 * rest(k, 0) + g1 * rest(k, 1) + g2 * rest(k, 2);
+    tx += sk * bx[k];
+    ty += sk * by[k];
+    tz += sk * bz[k];
   }
-  return make_float3(gx, gy, gz);
+  return make_float3(j00 * tx + j01 * ty + j02 * tz, j01 * tx + j11 * ty + j12 * tz,
+                     j02 * tx + j12 * ty + j22 * tz);
 }
 
 // ---- tiles --------------------------------------------------------------------
