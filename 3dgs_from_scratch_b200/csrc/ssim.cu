@@ -44,6 +44,8 @@ constexpr int kSsimStride = kSsimHW + 1;       // 43: conflict-free row starts
 constexpr int kSsimHRow = kSsimTW + 1;         // 33: conflict-free horizontal-pass stores
 constexpr int kSsimRunH = 8;                   // outputs per thread, horizontal pass
 constexpr int kSsimRunV = 4;                   // outputs per thread, vertical pass
+constexpr int kSsimStageRows = 6;              // staged rows per step (6 x 42 threads)
+constexpr int kSsimStageThreads = kSsimStageRows * kSsimHW;
 constexpr int kSsimThreads = 256;
 constexpr float kSsimC1 = 0.01f * 0.01f;
 constexpr float kSsimC2 = 0.03f * 0.03f;
@@ -54,22 +56,28 @@ __constant__ float c_ssim_win[kSsimWin];
 //   HWC = false: planar fp32, plane p = n * C + c at offset p * H * W.
 //   HWC = true : raw rendered (H, W, C) fp32 -> clamp(r, 0, 1) * 255 / 255,
 //                target (H, W, C) of type TT -> t / 255; plane = channel.
+// Index arithmetic is 32-bit: the host entry points reject images of 2^31
+// or more elements. The / 255 of the reference's normalisation is a product
+// with the rounded reciprocal (within an ulp of the division; the loss and
+// its gradient do not need the quotient bit for bit).
+constexpr float kInv255 = 1.0f / 255.0f;
+
 template <bool HWC, typename TT>
 struct SsimSrc {
   const float *a;
   const TT *b;
   int C, H, W;
 
-  __device__ __forceinline__ int64_t index(int plane, int y, int x) const {
-    if (HWC) return ((int64_t)y * W + x) * C + plane;
-    return (int64_t)plane * H * W + (int64_t)y * W + x;
+  __device__ __forceinline__ int index(int plane, int y, int x) const {
+    if (HWC) return (y * W + x) * C + plane;
+    return (plane * H + y) * W + x;
   }
   __device__ __forceinline__ void load(int plane, int y, int x, float &xv, float &yv) const {
-    const int64_t i = index(plane, y, x);
+    const int i = index(plane, y, x);
     if (HWC) {
       const float c = fminf(fmaxf(a[i], 0.0f), 1.0f);
-      xv = (c * 255.0f) / 255.0f;
-      yv = (float)b[i] / 255.0f;
+      xv = (c * 255.0f) * kInv255;
+      yv = (float)b[i] * kInv255;
     } else {
       xv = a[i];
       yv = (float)b[i];
@@ -167,13 +175,17 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
   const int plane = blockIdx.x % planes;
   const int tx = blockIdx.x / planes;
   const int gx0 = tx * kSsimTW, gy0 = blockIdx.y * kSsimTH;
-  for (int k = threadIdx.x; k < kSsimHH * kSsimHW; k += kSsimThreads) {
-    const int r = k / kSsimHW, c = k - r * kSsimHW;
-    const int gy = gy0 - kSsimR + r, gx = gx0 - kSsimR + c;
-    float xv = 0.0f, yv = 0.0f;
-    if (gy >= 0 && gy < H && gx >= 0 && gx < W) src.load(plane, gy, gx, xv, yv);
-    sx[r * kSsimStride + c] = xv;
-    sy[r * kSsimStride + c] = yv;
+  if (threadIdx.x < kSsimStageThreads) {  // 6 rows of 42 columns per step
+    const int c = threadIdx.x % kSsimHW, r0 = threadIdx.x / kSsimHW;
+    const int gx = gx0 - kSsimR + c;
+    const bool in_x = gx >= 0 && gx < W;
+    for (int r = r0; r < kSsimHH; r += kSsimStageRows) {
+      const int gy = gy0 - kSsimR + r;
+      float xv = 0.0f, yv = 0.0f;
+      if (in_x && gy >= 0 && gy < H) src.load(plane, gy, gx, xv, yv);
+      sx[r * kSsimStride + c] = xv;
+      sy[r * kSsimStride + c] = yv;
+    }
   }
   __syncthreads();
   if (threadIdx.x < kSsimHItems) {
@@ -219,7 +231,7 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
       d_xx *= wscale;
       d_xy *= wscale;
     }
-    const int64_t oi = (int64_t)plane * H * W + (int64_t)gy * W + gx;
+    const int oi = (plane * H + gy) * W + gx;
     m0[oi] = d_mu;
     m1[oi] = d_xx;
     m2[oi] = d_xy;
@@ -243,20 +255,24 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
   const int plane = blockIdx.x % planes;
   const int tx = blockIdx.x / planes;
   const int gx0 = tx * kSsimTW, gy0 = blockIdx.y * kSsimTH;
-  const int64_t pbase = (int64_t)plane * H * W;
-  for (int k = threadIdx.x; k < kSsimHH * kSsimHW; k += kSsimThreads) {
-    const int r = k / kSsimHW, c = k - r * kSsimHW;
-    const int gy = gy0 - kSsimR + r, gx = gx0 - kSsimR + c;
-    float v0 = 0.f, v1 = 0.f, v2 = 0.f;
-    if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
-      const int64_t o = pbase + (int64_t)gy * W + gx;
-      v0 = m0[o];
-      v1 = m1[o];
-      v2 = m2[o];
+  const int pbase = plane * H * W;
+  if (threadIdx.x < kSsimStageThreads) {  // 6 rows of 42 columns per step
+    const int c = threadIdx.x % kSsimHW, r0 = threadIdx.x / kSsimHW;
+    const int gx = gx0 - kSsimR + c;
+    const bool in_x = gx >= 0 && gx < W;
+    for (int r = r0; r < kSsimHH; r += kSsimStageRows) {
+      const int gy = gy0 - kSsimR + r;
+      float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+      if (in_x && gy >= 0 && gy < H) {
+        const int o = pbase + gy * W + gx;
+        v0 = m0[o];
+        v1 = m1[o];
+        v2 = m2[o];
+      }
+      sm[0][r * kSsimStride + c] = v0;
+      sm[1][r * kSsimStride + c] = v1;
+      sm[2][r * kSsimStride + c] = v2;
     }
-    sm[0][r * kSsimStride + c] = v0;
-    sm[1][r * kSsimStride + c] = v1;
-    sm[2][r * kSsimStride + c] = v2;
   }
   __syncthreads();
   if (threadIdx.x < kSsimHItems) {
@@ -285,17 +301,17 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
     src.load(plane, gy, gx, xv, yv);
     const float gs = cv[o][0] + 2.f * xv * cv[o][1] + yv * cv[o][2];
     if (FUSED) {
-      const int64_t i = src.index(plane, gy, gx);
+      const int i = src.index(plane, gy, gx);
       const float d = xv - yv;
       acc += (double)fabsf(d);
       const float sgn = (d > 0.0f) ? 1.0f : ((d < 0.0f) ? -1.0f : 0.0f);
       const float gn = l1_weight * sgn * inv_numel + gs;  // d loss / d rendered_norm
-      float g = gn / 255.0f;                             // rendered_norm = rendered / 255
+      float g = gn * kInv255;                            // rendered_norm = rendered / 255
       g = g * 255.0f;                                    // rendered = clamp(raw) * 255
       const float raw = src.a[i];
       grad[i] = (raw >= 0.0f && raw <= 1.0f) ? g : 0.0f;
     } else {
-      grad[pbase + (int64_t)gy * W + gx] = up * gs;
+      grad[pbase + gy * W + gx] = up * gs;
     }
   }
   if (FUSED) {
@@ -335,7 +351,8 @@ static dim3 ssim_grid(int planes, int H, int W) {
 
 static bool ssim_grid_ok(int planes, int H, int W) {
   return (int64_t)((W + kSsimTW - 1) / kSsimTW) * planes < (int64_t)INT32_MAX &&
-         (H + kSsimTH - 1) / kSsimTH <= 65535;
+         (H + kSsimTH - 1) / kSsimTH <= 65535 &&
+         (int64_t)planes * H * W < (int64_t)INT32_MAX;  // 32-bit element indices
 }
 
 static int64_t ssim_count(int planes, int H, int W, int valid) {
