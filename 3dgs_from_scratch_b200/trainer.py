@@ -49,12 +49,11 @@ class NativeTrainer:
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 **render_opts):
+                 streams: int = 2, **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
         self.ssim_lambda = float(ssim_lambda)
-        self._ssim_scratch = None
         self.device = self.fp.device
         if self.device.type != "cuda":
             raise RuntimeError("NativeTrainer needs the parameters on a CUDA device")
@@ -62,8 +61,33 @@ class NativeTrainer:
         self.opts = dict(RENDER_DEFAULTS)
         self.opts.update(render_opts)
         self.strategy = strategy  # a densify.DeviceStrategy, or None
+        # Views are independent between the batched preprocess and the batched
+        # preprocess backward: view v's layout, blend and loss run on stream
+        # v % streams, so one view's latency-bound layout kernels overlap
+        # another's throughput-bound blend.
+        if streams < 1:
+            raise ValueError("streams must be at least 1")
+        self.num_streams = int(streams)
+        self._side = [torch.cuda.Stream(device=self.device) for _ in range(self.num_streams - 1)]
+        self._ssim_scratch = [None] * self.num_streams
         self.tx = (self.width + 15) // 16
         self.ty = (self.height + 15) // 16
+
+    def _view_stream(self, v):
+        k = v % self.num_streams
+        return torch.cuda.current_stream(self.device) if k == 0 else self._side[k - 1]
+
+    def _fork(self):
+        """Side streams start after the work queued so far on the current stream."""
+        ev = torch.cuda.current_stream(self.device).record_event()
+        for s in self._side:
+            s.wait_event(ev)
+
+    def _join(self):
+        """The current stream continues after the side streams' work."""
+        cur = torch.cuda.current_stream(self.device)
+        for s in self._side:
+            cur.wait_event(s.record_event())
 
     @property
     def params(self):
@@ -121,19 +145,25 @@ class NativeTrainer:
         rc = nat.query("gs_check_status", st)
         if rc:
             raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+        self._fork()
         for v, s in enumerate(views):
             total = int(host_totals[v])
             s["total"] = total
-            s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
-                s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
-            s["image"] = torch.empty((H, W, 3), **f)
-            s["final_t"] = torch.empty((H * W,), **f)
-            s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
-            nat.call("gs_blend_forward", s["offsets"].shape[0], s["offsets"].data_ptr(), total,
-                     s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(), W, H,
-                     o["alpha_threshold"], o["transmittance_threshold"],
-                     o["chi_squared_threshold"], s["image"].data_ptr(), s["final_t"].data_ptr(),
-                     s["pixel_end"].data_ptr(), st)
+            s["stream"] = self._view_stream(v)
+            with torch.cuda.stream(s["stream"]):
+                vst = nat.stream_ptr(dev)
+                s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
+                    s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
+                s["image"] = torch.empty((H, W, 3), **f)
+                s["final_t"] = torch.empty((H * W,), **f)
+                s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
+                nat.call("gs_blend_forward", s["offsets"].shape[0], s["offsets"].data_ptr(),
+                         total, s["ids"].data_ptr(), n, s["points"].data_ptr(),
+                         s["splat"].data_ptr(), W, H, o["alpha_threshold"],
+                         o["transmittance_threshold"], o["chi_squared_threshold"],
+                         s["image"].data_ptr(), s["final_t"].data_ptr(), s["pixel_end"].data_ptr(),
+                         vst)
+        self._join()
         return views
 
     def loss_and_backward(self, views, targets, accumulate=False):
@@ -152,37 +182,28 @@ class NativeTrainer:
         V = len(views)
         lam = self.ssim_lambda
         loss_sums = torch.zeros((V, 2), dtype=torch.float64, device=dev)
-        grad_img = torch.empty((H, W, 3), device=dev, dtype=torch.float32)
-        if lam > 0 and self._ssim_scratch is None:
-            self._ssim_scratch = torch.empty(nat.query("gs_ssim_scratch_bytes", 3, H, W) // 4,
-                                             device=dev, dtype=torch.float32)
+        grad_imgs = [torch.empty((H, W, 3), device=dev, dtype=torch.float32)
+                     for _ in range(min(V, self.num_streams))]
+        if lam > 0:
+            for k in range(len(grad_imgs)):
+                if self._ssim_scratch[k] is None:
+                    self._ssim_scratch[k] = torch.empty(
+                        nat.query("gs_ssim_scratch_bytes", 3, H, W) // 4, device=dev,
+                        dtype=torch.float32)
         # every view's blend gradients, consumed by one multi-view preprocess backward
         g_points_all = torch.zeros((V, n, 2), device=dev, dtype=torch.float32)
         g_splat_all = torch.zeros((V, n, 8), device=dev, dtype=torch.float32)
+        self._fork()
         for v, s in enumerate(views):
-            g_points, g_splat = g_points_all[v], g_splat_all[v]
-            tgt = targets[v]
-            if tgt.device != dev or not tgt.is_contiguous():
-                tgt = tgt.to(dev).contiguous()
-            if tgt.dtype not in (torch.uint8, torch.float32):
-                tgt = tgt.float()
-            if lam > 0:
-                nat.call("gs_l1_ssim_loss_grad", H, W, s["image"].data_ptr(), tgt.data_ptr(),
-                         int(tgt.dtype == torch.uint8), lam, grad_img.data_ptr(),
-                         loss_sums[v].data_ptr(), self._ssim_scratch.data_ptr(),
-                         self._ssim_scratch.numel() * 4, st)
-            else:
-                nat.call("gs_l1_loss_grad", npx, s["image"].data_ptr(), tgt.data_ptr(),
-                         int(tgt.dtype == torch.uint8), grad_img.data_ptr(),
-                         loss_sums[v].data_ptr(), st)
-            nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
-                     s["total"], s["ids"].data_ptr(), n, s["points"].data_ptr(),
-                     s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
-                     s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
-                     o["transmittance_threshold"], o["chi_squared_threshold"],
-                     g_points.data_ptr(), g_splat.data_ptr(), st)
-            if self.strategy is not None:  # strategy.py:48-72, per view
-                self.strategy.accumulate(g_points, s["radii"], W, H)
+            k = v % self.num_streams
+            with torch.cuda.stream(self._view_stream(v)):
+                self._view_backward(s, targets[v], grad_imgs[k], self._ssim_scratch[k],
+                                    loss_sums[v], g_points_all[v], g_splat_all[v])
+        self._join()
+        st = nat.stream_ptr(dev)
+        if self.strategy is not None:  # strategy.py:48-72, per view
+            for v, s in enumerate(views):
+                self.strategy.accumulate(g_points_all[v], s["radii"], W, H)
         b = self._batch
         if V != b["mask"].shape[0]:
             raise ValueError("loss_and_backward takes the views of the last forward_views call")
@@ -198,6 +219,33 @@ class NativeTrainer:
             return l1
         ssim = loss_sums[:, 1] / (3 * (H - 10) * (W - 10))
         return (1 - lam) * l1 + lam * (1 - ssim)
+
+    def _view_backward(self, s, tgt, grad_img, ssim_scratch, loss_slot, g_points, g_splat):
+        """One view's loss, its gradient w.r.t. the raw image and the blend
+        backward into g_points / g_splat, on the current stream."""
+        o = self.opts
+        dev = self.device
+        st = nat.stream_ptr(dev)
+        n, W, H = self.n, self.width, self.height
+        if tgt.device != dev or not tgt.is_contiguous():
+            tgt = tgt.to(dev).contiguous()
+        if tgt.dtype not in (torch.uint8, torch.float32):
+            tgt = tgt.float()
+        if self.ssim_lambda > 0:
+            nat.call("gs_l1_ssim_loss_grad", H, W, s["image"].data_ptr(), tgt.data_ptr(),
+                     int(tgt.dtype == torch.uint8), self.ssim_lambda, grad_img.data_ptr(),
+                     loss_slot.data_ptr(), ssim_scratch.data_ptr(), ssim_scratch.numel() * 4,
+                     st)
+        else:
+            nat.call("gs_l1_loss_grad", H * W * 3, s["image"].data_ptr(), tgt.data_ptr(),
+                     int(tgt.dtype == torch.uint8), grad_img.data_ptr(), loss_slot.data_ptr(),
+                     st)
+        nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
+                 s["total"], s["ids"].data_ptr(), n, s["points"].data_ptr(),
+                 s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
+                 s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
+                 o["transmittance_threshold"], o["chi_squared_threshold"], g_points.data_ptr(),
+                 g_splat.data_ptr(), st)
 
     def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True, step_index=None):
         """One training step over this rank's views: render, loss, backward
