@@ -82,6 +82,8 @@ def parse():
     p.add_argument("--global-views", type=int, default=None,
                    help="views per step over all ranks, sharded (strong scaling); "
                         "config 2 defaults to its batch of 32")
+    p.add_argument("--streams", type=int, default=2,
+                   help="CUDA streams the native trainer spreads a step's views over")
     p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="fused",
                    help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
                         "reduce-scatter / sharded Adam / all-gather kernel (multicast when "
@@ -357,7 +359,7 @@ def workload_config(args, cfg, views_per_rank):
                    "peer loads and stores)")),
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
             "optimizer": "Adam, six groups in one flat buffer, one native launch",
-            "trainer": args.trainer}
+            "trainer": args.trainer, "streams": getattr(args, "streams", 1)}
 
 
 # ---------------------------------------------------------------------------
@@ -423,14 +425,15 @@ class Trainer:
 class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
-    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl"):
+    def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl",
+                 streams=2):
         self.cfg = cfg
         self.world = world
         self.device = device
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
         fused = {"nccl": False, "fused": "auto", "fused-p2p": "p2p"}[dp_mode]
         self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda,
-                                            fused_dp=fused)
+                                            fused_dp=fused, streams=streams)
         self.fp = self.nt.fp
         self.params = self.fp.params
         cams = scenes.orbit_cameras(cfg, total_views)
@@ -526,7 +529,7 @@ def main():
     total_views, V, lam = view_plan(args, world, rank)
     if args.trainer == "native":
         tr = NativeBenchTrainer(cfg, args.n, total_views, world, rank, device, ssim_lambda=lam,
-                                dp_mode=args.dp)
+                                dp_mode=args.dp, streams=args.streams)
     else:
         if args.dp != "nccl":
             raise SystemExit("--dp fused needs --trainer native")
