@@ -63,12 +63,12 @@ NVLINK_ALLREDUCE_BUS_GBS = 725.0
 BLEND_FWD_FLOP_PER_PAIR = 22
 BLEND_BWD_FLOP_PER_PAIR = 60
 
-# DRAM bytes (read + write) per launch at config 1, from the ncu --set full
-# capture summarised in profiles/kernels_cfg1_full.md (dram__bytes_read.sum +
-# dram__bytes_write.sum).
-NCU_TRAFFIC_BYTES = {"preprocess_fwd": 277.0e6, "preprocess_bwd": 463.4e6,
-                     "blend_fwd": 56.6e6, "blend_bwd": 111.1e6, "optimizer": 1598.3e6,
-                     "loss": 51.2e6}
+# DRAM bytes (read + write) per launch at config 1 (4 views per step), from the
+# ncu --set full captures summarised in profiles/kernels_cfg1_full.md and
+# profiles/blend_backward_cfg1.md (dram__bytes_read.sum + dram__bytes_write.sum;
+# preprocess_fwd is the one multi-view launch).
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 56.8e6, "blend_bwd": 109.5e6,
+                     "loss": 50.8e6}
 
 
 def parse():
@@ -680,7 +680,7 @@ def main():
                     "peak": r["peak"], "unit": r["unit"], "frac": r["frac"],
                     "traffic": NCU_TRAFFIC_BYTES.get(dom) if args.config == 1 and args.n is None
                     else None,
-                    "traffic_unit": "bytes/launch (ncu, profiles/kernels_cfg1_full.md)",
+                    "traffic_unit": "bytes/launch (ncu, profiles/)",
                     "peak_source": (f"{src} MEASURED_PEAKS.json hbm_gbs" if r["bound"] == "hbm"
                                     else "nominal FP32: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
                                          " (MEASURED_PEAKS.json has no FP32 figure)"),
