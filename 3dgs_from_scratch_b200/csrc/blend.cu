@@ -27,6 +27,9 @@ namespace gs {
 constexpr int kBlendThreads = 128;  // 4 warps per 16x16 tile, 2 pixels per thread
 constexpr int kBatch = 256;         // records staged per batch (2 per thread)
 constexpr int kWarps = kBlendThreads / 32;
+#ifndef GS_BWD_PAIRED
+#define GS_BWD_PAIRED 1  // 1: the backward reduces two visible entries per step
+#endif
 
 // Pixels owned by thread t: warp w covers the 8x8 block at (8*(w&1), 8*(w>>1));
 // lane l takes column l&7 and rows (l>>3) and (l>>3)+4 of that block.
@@ -277,6 +280,51 @@ __device__ __forceinline__ float reduce1(float x) {
   return x;
 }
 
+// Transposing warp reduction of 16 values (16 shuffles): afterwards lane L
+// holds the warp-wide sum of value index (L >> 1) & 15.
+__device__ __forceinline__ float reduce16(const float v[16], uint32_t lane) {
+  const unsigned FULL = 0xffffffffu;
+  float a[8];
+  const bool b4 = lane & 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float send = b4 ? v[i] : v[i + 8];
+    const float keep = b4 ? v[i + 8] : v[i];
+    a[i] = keep + __shfl_xor_sync(FULL, send, 16);
+  }
+  float c[4];
+  const bool b3 = lane & 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b3 ? a[i] : a[i + 4];
+    const float keep = b3 ? a[i + 4] : a[i];
+    c[i] = keep + __shfl_xor_sync(FULL, send, 8);
+  }
+  float d[2];
+  const bool b2 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b2 ? c[i] : c[i + 2];
+    const float keep = b2 ? c[i + 2] : c[i];
+    d[i] = keep + __shfl_xor_sync(FULL, send, 4);
+  }
+  const bool b1 = lane & 2;
+  const float send = b1 ? d[0] : d[1];
+  const float keep = b1 ? d[1] : d[0];
+  float e = keep + __shfl_xor_sync(FULL, send, 2);
+  return e + __shfl_xor_sync(FULL, e, 1);
+}
+
+// Two values (5 shuffles): afterwards lane L holds the warp-wide sum of
+// value (L >> 4) & 1.
+__device__ __forceinline__ float reduce2(float x0, float x1, uint32_t lane) {
+  const bool b4 = lane & 16;
+  float x = (b4 ? x1 : x0) + __shfl_xor_sync(0xffffffffu, b4 ? x0 : x1, 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
 // Backward state of one pixel.
 struct BwdPx {
   float fu, fv, gr, gg, gb, Ta, suffix;
@@ -338,7 +386,10 @@ __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float
 // Backward blend. Gradient slot order per Gaussian: 0,1 = d(u,v);
 // 2,3,4 = d(conic a,b,c); 5 = d opacity; 6,7,8 = d colour.
 template <bool PACKED>
-__global__ void __launch_bounds__(kBlendThreads, 8) blend_backward_kernel(
+#ifndef GS_BWD_MINB
+#define GS_BWD_MINB 8  // resident blocks per SM the backward's register budget targets
+#endif
+__global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_kernel(
     int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
     const int32_t *__restrict__ ids, int n, const float2 *__restrict__ points,
     const float4 *__restrict__ splat, const float *__restrict__ conic,
@@ -426,6 +477,50 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_backward_kernel(
     for (int j1 = jmax; j1 > 0; j1 -= 32) {
       const int jl = j1 - 1 - (int)lane;
       uint32_t todo = __ballot_sync(0xffffffffu, jl >= 0 && ((s_mask[jl] >> warp) & 1u));
+#if GS_BWD_PAIRED
+      // two visible entries per step, reduced together (21 shuffles for 18
+      // sums instead of 28); their per-pixel updates stay in back-to-front
+      // order (j before j2)
+      while (todo & (todo - 1)) {
+        const int j = j1 - __ffs(todo);
+        todo &= todo - 1;
+        const int j2 = j1 - __ffs(todo);
+        todo &= todo - 1;
+        float acc[18];
+#pragma unroll
+        for (int q = 0; q < 18; ++q) acc[q] = 0.f;
+        bool contrib = false;
+        {
+          const int k = bstart + j;
+          const float4 g0 = s_g0[j];
+          const float4 g1 = s_g1[j];
+          const float c2 = s_b[j];
+          if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc);
+          if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc);
+        }
+        {
+          const int k = bstart + j2;
+          const float4 g0 = s_g0[j2];
+          const float4 g1 = s_g1[j2];
+          const float c2 = s_b[j2];
+          if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc + 9);
+          if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc + 9);
+        }
+        if (!__any_sync(0xffffffffu, contrib)) continue;
+        float v16[16];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          v16[q] = acc[q];
+          v16[q + 8] = acc[9 + q];
+        }
+        const float r16 = reduce16(v16, lane);
+        const float r2 = reduce2(acc[8], acc[17], lane);
+        const int q16 = (lane >> 1) & 15;
+        if ((lane & 1) == 0)
+          atomicAdd(&s_acc[(q16 < 8 ? j : j2) * 9 + (q16 & 7)], r16);
+        if ((lane & 15) == 0) atomicAdd(&s_acc[((lane >> 4) ? j2 : j) * 9 + 8], r2);
+      }
+#endif
       while (todo) {
         const int j = j1 - __ffs(todo);
         todo &= todo - 1;
