@@ -6,8 +6,8 @@
 // streamed in batches of 256: each thread stages two Gaussians' records in
 // shared memory, together with a 4-bit mask of the warp blocks whose pixels
 // that Gaussian can reach (a conservative bound; see reach_mask), and then
-// every warp walks the batch from shared memory, skipping records its block
-// cannot see as one uniform branch. Per pixel the forward arithmetic is the
+// every warp walks the batch from shared memory, 32 records at a time: one
+// ballot of their masks, then only the records its block can see. Per pixel the forward arithmetic is the
 // reference's, operation for operation (ruguangyou/3dgs_from_scratch
 // src/cuda/kernel.cu:954-982), so images match it bit for bit; the backward
 // (kernel.cu:1066-1110) keeps the forward's skip tests and reorganises the
@@ -17,9 +17,10 @@
 // its last contributing list entry, so the backward needs no forward replay.
 // The backward walks each batch back to front, sums a thread's two pixels,
 // pre-reduces the 9 gradient terms of a (warp, Gaussian) pair with a
-// transposing warp-shuffle reduction (14 shuffles instead of 45), accumulates
-// warps into shared memory, and issues one vector atomic per gradient group
-// per (tile, Gaussian).
+// transposing warp-shuffle reduction (two visible records at a time: their
+// 18 sums in 21 shuffles, against 45 per record for plain butterflies),
+// accumulates warps into shared memory, and issues one vector atomic per
+// gradient group per (tile, Gaussian).
 #include "gs_common.cuh"
 
 namespace gs {
