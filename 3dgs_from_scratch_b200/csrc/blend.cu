@@ -219,9 +219,23 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
       if (__all_sync(0xffffffffu, p0.done && p1.done)) break;
       const int jl = j0 + lane;
       uint32_t todo = __ballot_sync(0xffffffffu, jl < cnt && ((s_mask[jl] >> warp) & 1u));
-      while (todo) {
+      // two visible records per step: both are read from shared memory up
+      // front, then applied to each pixel in list order
+      while (todo & (todo - 1)) {
         const int j = j0 + __ffs(todo) - 1;
         todo &= todo - 1;
+        const int j2 = j0 + __ffs(todo) - 1;
+        todo &= todo - 1;
+        const float4 g0 = s_g0[j], h0 = s_g0[j2];
+        const float4 g1 = s_g1[j], h1 = s_g1[j2];
+        const float cb = ACCUM ? s_b[j] : 0.f, hb = ACCUM ? s_b[j2] : 0.f;
+        if (!p0.done) fwd_step<ACCUM>(p0, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+        if (!p1.done) fwd_step<ACCUM>(p1, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+        if (!p0.done) fwd_step<ACCUM>(p0, h0, h1, hb, base + j2, alpha_thr, trans_thr, chi_thr);
+        if (!p1.done) fwd_step<ACCUM>(p1, h0, h1, hb, base + j2, alpha_thr, trans_thr, chi_thr);
+      }
+      if (todo) {
+        const int j = j0 + __ffs(todo) - 1;
         const float4 g0 = s_g0[j];
         const float4 g1 = s_g1[j];
         const float cb = ACCUM ? s_b[j] : 0.f;
