@@ -12,7 +12,8 @@ renders its own views of a replicated scene.
 value = views/s over all ranks, device-timed with CUDA events, max over
 ranks. e2e = the same step through render() with each step's target images
 (uint8) and cameras copied from pinned host memory and the loss read back,
-wall-clock timed. See DESIGN.md for the roofline definitions.
+wall-clock timed. The roofline of each stage is its algorithmic bytes (or
+FLOPs) per launch, listed below, over the launch's CUDA-event time.
 
 --trainer native (default) runs the step with trainer.NativeTrainer: the same
 math with the activations fused into the preprocess kernels, one host
@@ -50,7 +51,7 @@ PEAKS_PATH = os.path.join(HERE, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
-# algorithmic bytes / flops ("Roofline")
+# algorithmic bytes / flops per unit (Gaussian, pair or evaluated pixel-Gaussian pair)
 PRE_FWD_BYTES_PER_G = 281
 PRE_BWD_BYTES_PER_G = 504
 LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
@@ -685,7 +686,7 @@ def main():
                                     else "nominal FP32: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
                                          " (MEASURED_PEAKS.json has no FP32 figure)"),
                     "work_per_launch": (f"{E} evaluated pairs" if r["bound"] == "fp32"
-                                        else "see DESIGN.md")}
+                                        else "algorithmic bytes per launch over its time")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not render_mode:

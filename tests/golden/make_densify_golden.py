@@ -1,8 +1,8 @@
 """Golden vectors for the device densification (DeviceStrategy) from the
 reference's own Strategy (src/strategy.py), run on the CPU.
 
-Run in a container that has the reference checkout (default /root/reference,
-or $GS_REFERENCE_ROOT); the .npz files it writes are committed and the tests
+Run where the reference checkout is present (its path in $GS_REFERENCE_ROOT,
+or the default below); the .npz files it writes are committed and the tests
 never read the reference at run time.
 
 Each case: a seeded set of Gaussians with torch.optim.Adam states after two

@@ -1,7 +1,7 @@
 """Generate the golden vectors in tests/golden/ from the reference's own code.
 
-Run in a container that has the reference checkout (default /root/reference,
-or $GS_REFERENCE_ROOT); the generated .npz files are committed and the tests
+Run where the reference checkout is present (its path in $GS_REFERENCE_ROOT,
+or the default below); the generated .npz files are committed and the tests
 never read the reference at run time.
 
 What it does:
@@ -12,7 +12,7 @@ What it does:
 * runs the reference's gradient checks (check_project_points,
   check_rasterize, check_rasterize_multitile,
   check_rasterize_multitile_truncated, check_sh, check_end_to_end) on the
-  CPU, so the reference's own thresholds judge the oracle, and records their
+  CPU, so the reference's own thresholds assess the oracle, and records their
   verdicts in manifest.json;
 * captures the reference-side tensors of every check (inputs, upstream
   gradients, the reference's layout from build_reference_tile_layout, its
