@@ -2,6 +2,7 @@
 include/gs_b200.h, the ctypes signatures match the header, and host-only
 queries behave. No kernel is launched here."""
 import ctypes
+import importlib
 import os
 import re
 
@@ -66,3 +67,24 @@ def test_product_path_has_no_cpu_fallback(gs):
     with pytest.raises(RuntimeError):
         gs.render(torch.eye(4), torch.eye(3), 16, 16, z(n, 3), z(n, 3), z(n, 4), z(n), z(n, 3),
                   z(n, 15, 3))
+
+
+def test_entry_points_reject_bad_arguments_before_touching_a_device(gs):
+    """Size and pointer checks come first: these calls return
+    GS_ERR_INVALID_ARGUMENT (1) without a GPU."""
+    lib = gs.load_native()
+    nat = importlib.import_module("3dgs_from_scratch_b200._native")
+    bad = nat.GS_ERR_INVALID_ARGUMENT
+    P = None
+    assert lib.gs_preprocess_forward_views(10, 0, *[P] * 9, 0.01, 100.0, 0.0, 0.5, 128.0, 16, 16,
+                                           0, 1, *[P] * 8) == bad          # no views
+    assert lib.gs_preprocess_backward_views(10, 2, *[P] * 9, 0, 16, 0, 1, 0, P, P, 2, P, 8,
+                                            *[P] * 6, P) == bad            # width 0
+    assert lib.gs_ssim_forward(0, 16, 16, P, P, 1, P, 0, P, P) == bad      # no planes
+    assert lib.gs_ssim_forward(1, 8, 64, P, P, 1, P, 0, P, P) == bad       # valid needs > 10 rows
+    assert lib.gs_l1_ssim_loss_grad(8, 64, P, P, 0, 0.2, P, P, P, 0, P) == bad
+    assert lib.gs_dp_adam_step(0, 0, P, P, P, P, P, 16, P, P, 6, P, P, P, 0.9, 0.999, 1, 1, 1,
+                               P, P) == bad                                # world 0
+    assert lib.gs_densify_accumulate(-1, P, P, 16, 16, P, P, P) == bad
+    assert lib.gs_reset_opacities(-1, P, P, P, 0.0, P) == bad
+    assert lib.gs_l1_loss_grad(-1, P, P, 0, P, P, P) == bad
