@@ -166,7 +166,20 @@ class NativeTrainer:
         self._join()
         return views
 
-    def loss_and_backward(self, views, targets, accumulate=False):
+    def _stage_targets(self, targets):
+        """Targets held in host memory (pinned, for the copy to be
+        asynchronous) are copied to the device on a copy stream, so the copy
+        overlaps the forward pass; returns the device targets and the event
+        the copies complete on (None when they were already on the device)."""
+        if all(t.device == self.device for t in targets):
+            return list(targets), None
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        with torch.cuda.stream(self._copy_stream):
+            dev = [t.to(self.device, non_blocking=True) for t in targets]
+        return dev, self._copy_stream.record_event()
+
+    def loss_and_backward(self, views, targets, accumulate=False, targets_ready=None):
         """Loss of every view against its target (H, W, 3; float in [0, 255]
         or uint8) -- L1, or (1 - ssim_lambda) L1 + ssim_lambda (1 - SSIM)
         when ssim_lambda > 0 -- and the backward into the flat gradient buffer.
@@ -196,7 +209,11 @@ class NativeTrainer:
         self._fork()
         for v, s in enumerate(views):
             k = v % self.num_streams
-            with torch.cuda.stream(self._view_stream(v)):
+            vs = self._view_stream(v)
+            if targets_ready is not None:  # targets copied on another stream
+                vs.wait_event(targets_ready)
+                targets[v].record_stream(vs)
+            with torch.cuda.stream(vs):
                 self._view_backward(s, targets[v], grad_imgs[k], self._ssim_scratch[k],
                                     loss_sums[v], g_points_all[v], g_splat_all[v])
         self._join()
@@ -255,9 +272,11 @@ class NativeTrainer:
         fused_dp the one-kernel reduce-scatter / sharded Adam / all-gather).
         With a strategy and step_index, the densification schedule of
         scripts/train.py:224-227 runs after the optimizer step (it may change
-        the number of Gaussians). Returns the losses."""
+        the number of Gaussians). Targets in host memory are copied while the
+        views are rendered. Returns the losses."""
+        targets, ready = self._stage_targets(targets)
         views = self.forward_views(world_to_cameras, intrinsics)
-        losses = self.loss_and_backward(views, targets)
+        losses = self.loss_and_backward(views, targets, targets_ready=ready)
         if optimizer_step:
             self.fp.step()
             if self.strategy is not None and step_index is not None:

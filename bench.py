@@ -453,9 +453,11 @@ class NativeBenchTrainer:
 
     def step(self, e2e=False):
         if e2e:
+            # cameras copied here; the pinned host targets go to the trainer, which
+            # copies them on a copy stream while the views are rendered
             cams = self.host_cams.to(self.device, non_blocking=True)
             K = self.host_K.to(self.device, non_blocking=True)
-            tg = [t.to(self.device, non_blocking=True) for t in self.host_targets]
+            tg = self.host_targets
         else:
             cams, K, tg = self.cams, self.K, self.targets
         losses = self.nt.step(cams, K, tg)

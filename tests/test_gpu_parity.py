@@ -601,3 +601,26 @@ def test_multi_view_preprocess_matches_per_view(gs, n):
     del numel
     for k in order:
         assert_close_metric(k, np_(grads_multi[k]), np_(grads_ref[k]), 0.999999, 1e-5)
+
+
+def test_native_trainer_host_targets_match_device_targets(gs):
+    """Targets in pinned host memory (copied on the trainer's copy stream
+    while the views render) give the same step as targets on the device."""
+    tr_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
+    W, H, f = 160, 120, 170.0
+    cfg = gs.scenes.CONFIGS[0]
+    raw = gs.scenes.make_gaussians(cfg, seed=5, n=3000)
+    w2cs = gs.scenes.orbit_cameras(cfg, 3)
+    K = torch.tensor([[f, 0, W / 2], [0, f, H / 2], [0, 0, 1]], dtype=torch.float32)
+    g = torch.Generator().manual_seed(8)
+    host = [(torch.rand((H, W, 3), generator=g) * 255).round().to(torch.uint8).pin_memory()
+            for _ in range(3)]
+    out = []
+    for targets in (host, [t.to(DEV) for t in host]):
+        tr = tr_mod.NativeTrainer({k: v.to(DEV) for k, v in raw.items()}, W, H, ssim_lambda=0.2)
+        losses = tr.step(w2cs, K, targets, optimizer_step=False)
+        torch.cuda.synchronize()
+        out.append((losses.cpu(), tr.fp.grad.cpu().clone()))
+    assert torch.allclose(out[0][0], out[1][0], rtol=1e-6, atol=1e-9)
+    # the gradients are sums of atomics: equal up to their order
+    assert_close_metric("grad", np_(out[0][1]), np_(out[1][1]), 0.999999, 1e-5)
