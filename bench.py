@@ -66,9 +66,9 @@ BLEND_BWD_FLOP_PER_PAIR = 60
 
 # DRAM bytes (read + write) per launch at config 1 (4 views per step), from the
 # ncu --set full captures summarised in profiles/kernels_cfg1_full.md and
-# profiles/blend_backward_cfg1.md (dram__bytes_read.sum + dram__bytes_write.sum;
+# profiles/blend_kernels_cfg1.md (dram__bytes_read.sum + dram__bytes_write.sum;
 # preprocess_fwd is the one multi-view launch).
-NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 56.8e6, "blend_bwd": 109.5e6,
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 58.8e6, "blend_bwd": 113.2e6,
                      "loss": 50.8e6}
 
 
