@@ -135,3 +135,42 @@ def test_dead_rank_surfaces_as_error_not_hang():
     assert procs[1].exitcode == 3
     assert procs[0].exitcode == 0
     assert str(out.get(0, "")).startswith("error"), out.get(0)
+
+
+def test_flat_params_rebuild_relayouts_every_group():
+    """FlatParams.rebuild re-lays the six groups out for a new Gaussian count
+    and hands the fill function both layouts (host-side logic; the device
+    fill is gs_densify_apply)."""
+    n, n_new = 5, 8
+    fp = dp.FlatParams(_tensors(n, 1))
+    fp.exp_avg = torch.arange(fp.padded, dtype=torch.float32)
+    fp.exp_avg_sq = torch.arange(fp.padded, dtype=torch.float32) * 2
+    old = {k: fp[k].detach().clone() for k in dp.GROUPS}
+    seen = {}
+
+    def fill(old_data, old_off, new_data, new_off, old_m, old_v, new_m, new_v):
+        seen["offsets"] = (list(old_off), list(new_off))
+        for i, k in enumerate(dp.GROUPS):
+            per = old[k][0].numel()
+            a, b = old_off[i], new_off[i]
+            # keep the first n Gaussians, then repeat the first n_new - n
+            new_data[b:b + n * per] = old_data[a:a + n * per]
+            new_data[b + n * per:b + n_new * per] = old_data[a:a + (n_new - n) * per]
+            new_m[b:b + n * per] = old_m[a:a + n * per]
+            new_v[b:b + n * per] = old_v[a:a + n * per]
+
+    fp.rebuild(n_new, fill)
+    assert fp.num_gaussians == n_new
+    for k in dp.GROUPS:
+        p = fp[k]
+        assert p.shape == (n_new,) + old[k].shape[1:]
+        assert torch.equal(p[:n].detach(), old[k])
+        assert torch.equal(p[n:].detach(), old[k][:n_new - n])
+        assert p.grad is not None and float(p.grad.abs().sum()) == 0.0
+        assert p.data_ptr() >= fp.data.data_ptr()
+    old_off, new_off = seen["offsets"]
+    assert old_off[0] == new_off[0] == 0 and new_off[-1] > old_off[-1]
+    assert all(o % 4 == 0 for o in new_off)
+    assert fp.exp_avg.shape[0] == fp.padded
+    a, _ = fp.spans["means"]
+    assert torch.equal(fp.exp_avg[a:a + 3 * n], torch.arange(3 * n, dtype=torch.float32))
