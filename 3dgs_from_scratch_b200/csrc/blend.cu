@@ -15,7 +15,9 @@
 //
 // The forward records each pixel's final transmittance and the index one past
 // its last contributing list entry, so the backward needs no forward replay.
-// The backward walks each batch back to front, sums a thread's two pixels,
+// The backward walks each batch back to front, runs a thread's two pixels
+// (same column) as fp32x2 pairs with Blackwell's packed FMA / MUL / ADD
+// (bwd_step2: one instruction for both pixels' chains), sums them,
 // pre-reduces the 9 gradient terms of a (warp, Gaussian) pair with a
 // transposing warp-shuffle reduction (two visible records at a time: their
 // 18 sums in 21 shuffles, against 45 per record for plain butterflies),
@@ -30,6 +32,9 @@ constexpr int kBatch = 256;         // records staged per batch (2 per thread)
 constexpr int kWarps = kBlendThreads / 32;
 #ifndef GS_BWD_PAIRED
 #define GS_BWD_PAIRED 1  // 1: the backward reduces two visible entries per step
+#endif
+#ifndef GS_BWD_F32X2
+#define GS_BWD_F32X2 1  // 1: the backward runs a thread's two pixels as fp32x2 pairs
 #endif
 
 // Pixels owned by thread t: warp w covers the 8x8 block at (8*(w&1), 8*(w>>1));
@@ -398,6 +403,71 @@ __device__ __forceinline__ bool bwd_step(BwdPx &p, const float4 &g0, const float
   return true;
 }
 
+// Backward state of a thread's two pixels (same column, rows 4 apart) as
+// fp32x2 pairs: .x the upper pixel, .y the lower one. nsuffix holds the
+// negated suffix sum.
+struct BwdPx2 {
+  float fu;
+  float2 fv, gr, gg, gb, Ta, nsuffix;
+  int end0, end1;
+};
+
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+// bwd_step for both pixels at once with the packed fp32x2 instructions
+// (__ffma2_rn, __fmul2_rn, __fadd2_rn: two IEEE round-to-nearest operations
+// per instruction, the same results as the scalar forms). The column terms of
+// the exponent are computed once: inv00 du^2 + dv (2 inv01 du + inv11 dv).
+// A pixel past its end or cut by the chi-square / alpha test gets alpha =
+// density = 0, so it adds nothing and keeps its transmittance. acc receives
+// the pair's sums (not accumulated): slots 0-4 and 6-8 negated (the sign
+// comes from carrying -alpha, which turns the subtractions into fused
+// multiply-adds; restored in the flush), slot 5 as is.
+__device__ __forceinline__ bool bwd_step2(BwdPx2 &p, int k, const float4 &g0, const float4 &g1,
+                                          float c2, float alpha_thr, float chi_thr,
+                                          float acc[9]) {
+  bool v0 = k < p.end0, v1 = k < p.end1;
+  const float du = p.fu - g0.x;
+  const float2 dv = __fadd2_rn(p.fv, f2(-g0.y));
+  const float P = g0.z * du * du;
+  const float Q = 2.0f * g0.w * du;
+  const float2 e = __ffma2_rn(dv, __ffma2_rn(f2(g1.x), dv, f2(Q)), f2(P));
+  v0 = v0 && !(e.x > chi_thr);
+  v1 = v1 && !(e.y > chi_thr);
+  if (!(v0 || v1)) return false;
+  const float2 h = __fmul2_rn(e, f2(-0.5f));
+  float2 dens = make_float2(__expf(h.x), __expf(h.y));
+  float2 nal = __fmul2_rn(dens, f2(-g1.y));  // -alpha
+  v0 = v0 && !(-nal.x < alpha_thr);
+  v1 = v1 && !(-nal.y < alpha_thr);
+  if (!(v0 || v1)) return false;
+  if (!v0) dens.x = nal.x = 0.f;
+  if (!v1) dens.y = nal.y = 0.f;
+  const float2 oma = __fadd2_rn(__fadd2_rn(nal, f2(1.0f)), f2(kTransEps));
+  const float2 rcp = make_float2(rcp_approx(oma.x), rcp_approx(oma.y));
+  const float2 prefix = __fmul2_rn(p.Ta, rcp);
+  const float2 nw = __fmul2_rn(nal, prefix);  // -weight
+  const float2 grgb =
+      __ffma2_rn(p.gb, f2(c2), __ffma2_rn(p.gg, f2(g1.w), __fmul2_rn(p.gr, f2(g1.z))));
+  const float2 galpha = __ffma2_rn(prefix, grgb, __fmul2_rn(p.nsuffix, rcp));
+  const float2 nag = __fmul2_rn(nal, galpha);
+  const float2 nau = __fmul2_rn(f2(du), nag);
+  const float2 nav = __fmul2_rn(dv, nag);
+  acc[0] = nau.x + nau.y;
+  acc[1] = nav.x + nav.y;
+  acc[2] = du * acc[0];
+  acc[3] = fmaf(nau.x, dv.x, nau.y * dv.y);
+  acc[4] = fmaf(nav.x, dv.x, nav.y * dv.y);
+  acc[5] = fmaf(dens.x, galpha.x, dens.y * galpha.y);
+  acc[6] = fmaf(nw.x, p.gr.x, nw.y * p.gr.y);
+  acc[7] = fmaf(nw.x, p.gg.x, nw.y * p.gg.y);
+  acc[8] = fmaf(nw.x, p.gb.x, nw.y * p.gb.y);
+  p.nsuffix = __ffma2_rn(nw, grgb, p.nsuffix);
+  if (v0) p.Ta.x = prefix.x;
+  if (v1) p.Ta.y = prefix.y;
+  return true;
+}
+
 // Backward blend. Gradient slot order per Gaussian: 0,1 = d(u,v);
 // 2,3,4 = d(conic a,b,c); 5 = d opacity; 6,7,8 = d colour.
 template <bool PACKED>
@@ -453,6 +523,18 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
       }
     }
   }
+#if GS_BWD_F32X2
+  BwdPx2 P2;
+  P2.fu = px[0].fu;
+  P2.fv = make_float2(px[0].fv, px[1].fv);
+  P2.gr = make_float2(px[0].gr, px[1].gr);
+  P2.gg = make_float2(px[0].gg, px[1].gg);
+  P2.gb = make_float2(px[0].gb, px[1].gb);
+  P2.Ta = make_float2(px[0].Ta, px[1].Ta);
+  P2.nsuffix = make_float2(0.f, 0.f);
+  P2.end0 = px[0].end;
+  P2.end1 = px[1].end;
+#endif
   if (t == 0) s_max_end = s;
   __syncthreads();
   const int my_end = max(px[0].end, px[1].end);
@@ -505,6 +587,11 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
 #pragma unroll
         for (int q = 0; q < 18; ++q) acc[q] = 0.f;
         bool contrib = false;
+#if GS_BWD_F32X2
+        contrib |= bwd_step2(P2, bstart + j, s_g0[j], s_g1[j], s_b[j], alpha_thr, chi_thr, acc);
+        contrib |= bwd_step2(P2, bstart + j2, s_g0[j2], s_g1[j2], s_b[j2], alpha_thr, chi_thr,
+                             acc + 9);
+#else
         {
           const int k = bstart + j;
           const float4 g0 = s_g0[j];
@@ -521,6 +608,7 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
           if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc + 9);
           if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc + 9);
         }
+#endif
         if (!__any_sync(0xffffffffu, contrib)) continue;
         float v16[16];
 #pragma unroll
@@ -547,8 +635,12 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
 #pragma unroll
         for (int q = 0; q < 9; ++q) acc[q] = 0.f;
         bool contrib = false;
+#if GS_BWD_F32X2
+        contrib = bwd_step2(P2, k, g0, g1, c2, alpha_thr, chi_thr, acc);
+#else
         if (k < px[0].end) contrib |= bwd_step(px[0], g0, g1, c2, alpha_thr, chi_thr, acc);
         if (k < px[1].end) contrib |= bwd_step(px[1], g0, g1, c2, alpha_thr, chi_thr, acc);
+#endif
         if (!__any_sync(0xffffffffu, contrib)) continue;
         float r8 = reduce8(acc, lane);
         float r9 = reduce1(acc[8]);
@@ -569,12 +661,23 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
         {  // apply the per-Gaussian constants factored out of bwd_step's sums
           const float4 g0 = s_g0[slot];
           const float inv00 = g0.z, inv01 = g0.w, inv11 = s_g1[slot].x;
+#if GS_BWD_F32X2  // slots 0-4 and 6-8 were summed negated
+          const float su = -a[0], sv = -a[1];
+          a[0] = inv00 * su + inv01 * sv;
+          a[1] = inv01 * su + inv11 * sv;
+          a[2] = 0.5f * a[2];
+          a[4] = 0.5f * a[4];
+          a[6] = -a[6];
+          a[7] = -a[7];
+          a[8] = -a[8];
+#else
           const float su = a[0], sv = a[1];
           a[0] = inv00 * su + inv01 * sv;
           a[1] = inv01 * su + inv11 * sv;
           a[2] = -0.5f * a[2];
           a[3] = -a[3];
           a[4] = -0.5f * a[4];
+#endif
         }
         if (a[0] != 0.f || a[1] != 0.f)
           atomicAdd(reinterpret_cast<float2 *>(g_points) + id, make_float2(a[0], a[1]));
