@@ -9,7 +9,9 @@
 // every warp walks the batch from shared memory, 32 records at a time: one
 // ballot of their masks, then only the records its block can see. Per pixel the forward arithmetic is the
 // reference's, operation for operation (ruguangyou/3dgs_from_scratch
-// src/cuda/kernel.cu:954-982), so images match it bit for bit; the backward
+// src/cuda/kernel.cu:954-982), so images match it bit for bit; a thread's
+// two pixels (same column) run as fp32x2 pairs through Blackwell's packed
+// FMA / MUL / ADD, which round exactly as the scalar forms (fwd_step2); the backward
 // (kernel.cu:1066-1110) keeps the forward's skip tests and reorganises the
 // gradient sums (see bwd_step).
 //
@@ -139,6 +141,8 @@ __device__ __forceinline__ Rec load_rec(int id, int n, const float2 *__restrict_
   return r;
 }
 
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
 // Forward state of one pixel.
 struct FwdPx {
   float fu, fv, T, r, g, b;
@@ -170,6 +174,67 @@ __device__ __forceinline__ void fwd_step(FwdPx &p, const float4 &g0, const float
   if (p.T < trans_thr) p.done = true;
 }
 
+#ifndef GS_FWD_F32X2
+#define GS_FWD_F32X2 1  // 1: the forward runs a thread's two pixels as fp32x2 pairs
+#endif
+
+// Forward state of a thread's two pixels as fp32x2 pairs (.x upper, .y lower).
+struct FwdPx2 {
+  float fu;
+  float2 fv, T, r, g, b;
+  int last0, last1;
+  bool done0, done1;
+};
+
+// fwd_step for both pixels with packed fp32x2 instructions, rounding for
+// rounding the scalar step as compiled (multiply-adds contracted): the
+// exponent is fma(inv11 dv, dv, fma(inv00 du, du, (2 inv01 du) dv)), the
+// colour updates fma(weight, colour, sum); the column terms (inv00 du,
+// 2 inv01 du) are computed once for both pixels. -alpha is carried so that
+// 1 - alpha and the colour updates stay single operations; a pixel that is
+// done or cut gets -alpha = 0, which leaves its colour and (1 + 0 + 1e-10
+// rounds to 1) its transmittance unchanged. Images, transmittances and end
+// indices are identical to the scalar step's.
+template <bool ACCUM>
+__device__ __forceinline__ void fwd_step2(FwdPx2 &p, const float4 &g0, const float4 &g1, float cb,
+                                          int k, float alpha_thr, float trans_thr,
+                                          float chi_thr) {
+  bool v0 = !p.done0, v1 = !p.done1;
+  const float du = p.fu - g0.x;
+  const float2 dv = __fadd2_rn(p.fv, f2(-g0.y));
+  const float inv00 = g0.z, inv01 = g0.w, inv11 = g1.x;
+  const float A = inv00 * du;
+  const float B = 2.0f * inv01 * du;
+  const float2 s1 = __ffma2_rn(f2(A), f2(du), __fmul2_rn(f2(B), dv));
+  const float2 e = __ffma2_rn(__fmul2_rn(f2(inv11), dv), dv, s1);
+  v0 = v0 && !(e.x > chi_thr);
+  v1 = v1 && !(e.y > chi_thr);
+  if (!(v0 || v1)) return;
+  const float2 h = __fmul2_rn(e, f2(-0.5f));
+  float2 nal = __fmul2_rn(make_float2(expf(h.x), expf(h.y)), f2(-g1.y));
+  v0 = v0 && !(-nal.x < alpha_thr);
+  v1 = v1 && !(-nal.y < alpha_thr);
+  if (!(v0 || v1)) return;
+  if (!v0) nal.x = 0.f;
+  if (!v1) nal.y = 0.f;
+  if (ACCUM) {
+    const float2 nw = __fmul2_rn(nal, p.T);  // -weight
+    p.r = __ffma2_rn(nw, f2(-g1.z), p.r);
+    p.g = __ffma2_rn(nw, f2(-g1.w), p.g);
+    p.b = __ffma2_rn(nw, f2(-cb), p.b);
+  }
+  const float2 oma = __fadd2_rn(__fadd2_rn(nal, f2(1.0f)), f2(kTransEps));
+  p.T = __fmul2_rn(p.T, oma);
+  if (v0) {
+    p.last0 = k + 1;
+    if (p.T.x < trans_thr) p.done0 = true;
+  }
+  if (v1) {
+    p.last1 = k + 1;
+    if (p.T.y < trans_thr) p.done1 = true;
+  }
+}
+
 // Forward blend. With ACCUM = false only the transmittance bookkeeping is
 // done (the replay used by the reference-API backward).
 template <bool PACKED, bool ACCUM>
@@ -197,11 +262,19 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
   const int s = offsets[tile];
   const int e = (tile + 1 < num_tiles) ? offsets[tile + 1] : (int)total;
 
+#if GS_FWD_F32X2
+  FwdPx2 P{(float)u, make_float2((float)v0, (float)v1), make_float2(1.f, 1.f),
+           make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), s, s, !in0,
+           !in1};
+#define GS_ALL_DONE (P.done0 && P.done1)
+#else
   FwdPx p0{(float)u, (float)v0, 1.0f, 0.f, 0.f, 0.f, s, !in0};
   FwdPx p1{(float)u, (float)v1, 1.0f, 0.f, 0.f, 0.f, s, !in1};
+#define GS_ALL_DONE (p0.done && p1.done)
+#endif
 
   for (int base = s; base < e; base += kBatch) {
-    if (__syncthreads_count(!(p0.done && p1.done)) == 0) break;
+    if (__syncthreads_count(!GS_ALL_DONE) == 0) break;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int slot = t + h * kBlendThreads;
@@ -221,7 +294,7 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
     // 32 entries at a time: one ballot of the reach masks, then only the
     // entries this warp's block can see, in list order
     for (int j0 = 0; j0 < cnt; j0 += 32) {
-      if (__all_sync(0xffffffffu, p0.done && p1.done)) break;
+      if (__all_sync(0xffffffffu, GS_ALL_DONE)) break;
       const int jl = j0 + lane;
       uint32_t todo = __ballot_sync(0xffffffffu, jl < cnt && ((s_mask[jl] >> warp) & 1u));
       // two visible records per step: both are read from shared memory up
@@ -234,21 +307,35 @@ __global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
         const float4 g0 = s_g0[j], h0 = s_g0[j2];
         const float4 g1 = s_g1[j], h1 = s_g1[j2];
         const float cb = ACCUM ? s_b[j] : 0.f, hb = ACCUM ? s_b[j2] : 0.f;
+#if GS_FWD_F32X2
+        fwd_step2<ACCUM>(P, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+        fwd_step2<ACCUM>(P, h0, h1, hb, base + j2, alpha_thr, trans_thr, chi_thr);
+#else
         if (!p0.done) fwd_step<ACCUM>(p0, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
         if (!p1.done) fwd_step<ACCUM>(p1, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
         if (!p0.done) fwd_step<ACCUM>(p0, h0, h1, hb, base + j2, alpha_thr, trans_thr, chi_thr);
         if (!p1.done) fwd_step<ACCUM>(p1, h0, h1, hb, base + j2, alpha_thr, trans_thr, chi_thr);
+#endif
       }
       if (todo) {
         const int j = j0 + __ffs(todo) - 1;
         const float4 g0 = s_g0[j];
         const float4 g1 = s_g1[j];
         const float cb = ACCUM ? s_b[j] : 0.f;
+#if GS_FWD_F32X2
+        fwd_step2<ACCUM>(P, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+#else
         if (!p0.done) fwd_step<ACCUM>(p0, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
         if (!p1.done) fwd_step<ACCUM>(p1, g0, g1, cb, base + j, alpha_thr, trans_thr, chi_thr);
+#endif
       }
     }
   }
+#undef GS_ALL_DONE
+#if GS_FWD_F32X2
+  const FwdPx p0{P.fu, P.fv.x, P.T.x, P.r.x, P.g.x, P.b.x, P.last0, P.done0};
+  const FwdPx p1{P.fu, P.fv.y, P.T.y, P.r.y, P.g.y, P.b.y, P.last1, P.done1};
+#endif
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const FwdPx &p = h ? p1 : p0;
@@ -411,8 +498,6 @@ struct BwdPx2 {
   float2 fv, gr, gg, gb, Ta, nsuffix;
   int end0, end1;
 };
-
-__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
 // bwd_step for both pixels at once with the packed fp32x2 instructions
 // (__ffma2_rn, __fmul2_rn, __fadd2_rn: two IEEE round-to-nearest operations

@@ -68,7 +68,7 @@ BLEND_BWD_FLOP_PER_PAIR = 60
 # ncu --set full captures summarised in profiles/kernels_cfg1_full.md and
 # profiles/blend_kernels_cfg1.md (dram__bytes_read.sum + dram__bytes_write.sum;
 # preprocess_fwd is the one multi-view launch).
-NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 58.8e6, "blend_bwd": 110.0e6,
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 57.2e6, "blend_bwd": 110.0e6,
                      "loss": 50.8e6}
 
 
