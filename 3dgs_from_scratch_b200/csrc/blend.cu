@@ -237,8 +237,11 @@ __device__ __forceinline__ void fwd_step2(FwdPx2 &p, const float4 &g0, const flo
 
 // Forward blend. With ACCUM = false only the transmittance bookkeeping is
 // done (the replay used by the reference-API backward).
+#ifndef GS_FWD_MINB
+#define GS_FWD_MINB 8  // resident blocks per SM the forward's register budget targets
+#endif
 template <bool PACKED, bool ACCUM>
-__global__ void __launch_bounds__(kBlendThreads, 8) blend_forward_kernel(
+__global__ void __launch_bounds__(kBlendThreads, GS_FWD_MINB) blend_forward_kernel(
     int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
     const int32_t *__restrict__ ids, int n, const float2 *__restrict__ points,
     const float4 *__restrict__ splat, const float *__restrict__ conic,
