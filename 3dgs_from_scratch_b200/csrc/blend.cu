@@ -38,6 +38,9 @@ constexpr int kWarps = kBlendThreads / 32;
 #ifndef GS_BWD_F32X2
 #define GS_BWD_F32X2 1  // 1: the backward runs a thread's two pixels as fp32x2 pairs
 #endif
+#ifndef GS_BWD_EX2
+#define GS_BWD_EX2 1  // 1: the backward's exponential as 2^(x log2 e) with the scale folded
+#endif
 
 // Pixels owned by thread t: warp w covers the 8x8 block at (8*(w&1), 8*(w>>1));
 // lane l takes column l&7 and rows (l>>3) and (l>>3)+4 of that block.
@@ -448,8 +451,9 @@ struct BwdPx {
 // the flush: acc[0..4] = sum of du*ag, dv*ag, du*du*ag, du*dv*ag, dv*dv*ag
 // (ag = alpha * dL/dalpha), from which d(u,v) = conic * (acc0, acc1) and
 // d conic = (-acc2 / 2, -acc3, -acc4 / 2). The skip decisions (chi-square
-// cut, alpha threshold) use the forward's expressions, with the fast
-// exponential (__expf, a few 1e-7 relative): a pair whose alpha lies within
+// cut, alpha threshold) use the forward's expressions, with an approximate
+// exponential (a few 1e-7 relative; in bwd_step2 exp(x) = 2^(x log2 e) by
+// ex2.approx, the scale folded into the packed multiply): a pair whose alpha lies within
 // that of the threshold may be decided differently from the forward, which
 // changes the pixel's gradient by about alpha_thr relative; the two
 // divisions by (1 - alpha) of the reference (kernel.cu:1088,1094) become one
@@ -457,6 +461,13 @@ struct BwdPx {
 __device__ __forceinline__ float rcp_approx(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// 2^x by the PTX approximate base-2 exponential (flush-to-zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
 
@@ -523,8 +534,14 @@ __device__ __forceinline__ bool bwd_step2(BwdPx2 &p, int k, const float4 &g0, co
   v0 = v0 && !(e.x > chi_thr);
   v1 = v1 && !(e.y > chi_thr);
   if (!(v0 || v1)) return false;
+#if GS_BWD_EX2
+  // exp(-e/2) = 2^(e * (-log2(e) / 2)), the scale folded into one packed multiply
+  const float2 h = __fmul2_rn(e, f2(-0.72134752044448170f));
+  float2 dens = make_float2(ex2_approx(h.x), ex2_approx(h.y));
+#else
   const float2 h = __fmul2_rn(e, f2(-0.5f));
   float2 dens = make_float2(__expf(h.x), __expf(h.y));
+#endif
   float2 nal = __fmul2_rn(dens, f2(-g1.y));  // -alpha
   v0 = v0 && !(-nal.x < alpha_thr);
   v1 = v1 && !(-nal.y < alpha_thr);
