@@ -251,9 +251,13 @@ def test_rasterize_multitile_golden(cr, name):
     assert_close_metric("colors", gcol, g["ref_grad_colors"], 0.99999, 1e-5)
 
 
+@pytest.mark.parametrize("size", [(160, 120), (157, 150)])
 @pytest.mark.parametrize("thr", [(1e-4, 1e-4, 9.21), (0.0, 0.0, 20.0), (0.01, 0.3, 4.0)])
-def test_rasterize_matches_oracle(cr, orc, thr):
-    W, H, n = 160, 120, 3000
+def test_rasterize_matches_oracle(cr, orc, thr, size):
+    """Blend forward and backward against the oracle. 157 x 150 leaves the
+    bottom tile row 6 pixels high, so some threads have their upper pixel in
+    the image and their lower pixel (4 rows down) outside it."""
+    (W, H), n = size, 3000
     rng = np.random.default_rng(7)
     pts = np.stack([rng.uniform(-5, W + 5, n), rng.uniform(-5, H + 5, n)], 1).astype(np.float32)
     radii = rng.uniform(1, 25, (n, 2)).astype(np.float32)
