@@ -2,8 +2,8 @@
 reference's own Strategy (src/strategy.py), run on the CPU.
 
 Run where the reference checkout is present (its path in $GS_REFERENCE_ROOT,
-or the default below); the .npz files it writes are committed and the tests
-never read the reference at run time.
+or a directory named "reference" beside the repository); the .npz files it
+writes are committed and the tests never read the reference at run time.
 
 Each case: a seeded set of Gaussians with torch.optim.Adam states after two
 optimizer steps (the per-group learning rates and eps of
@@ -23,7 +23,8 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("GS_REFERENCE_ROOT", "/root/reference")
+REPO = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("GS_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
 GROUPS = ("means", "scales", "quaternions", "opacities", "sh_coeffs_dc", "sh_coeffs_rest")
 LRS = {"means": 1.6e-4, "scales": 5e-3, "quaternions": 1e-3, "opacities": 5e-2,
        "sh_coeffs_dc": 2.5e-3, "sh_coeffs_rest": 2.5e-3 / 20}

@@ -1,8 +1,8 @@
 """Generate the golden vectors in tests/golden/ from the reference's own code.
 
 Run where the reference checkout is present (its path in $GS_REFERENCE_ROOT,
-or the default below); the generated .npz files are committed and the tests
-never read the reference at run time.
+or a directory named "reference" beside the repository); the generated .npz
+files are committed and the tests never read the reference at run time.
 
 What it does:
 * imports the reference's Python modules (src/torch_rasterizer.py,
@@ -35,7 +35,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("GS_REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("GS_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
 sys.path.insert(0, REPO)
 
 from oracle import oracle as orc  # noqa: E402
