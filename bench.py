@@ -58,16 +58,13 @@ LAYOUT_BYTES_PER_PAIR = 12 + 144 + 8
 PARAM_BYTES_PER_G = 236     # the 59 fp32 parameters of one Gaussian
 PRE_OUT_BYTES_PER_G = 45    # per view: points 8, depth 4, conic 12, radii 8, rgb 12, mask 1
 PRE_UP_BYTES_PER_G = 40     # per view: upstream gradients of points (8) and splat (32)
-# 8-rank NCCL all-reduce bus bandwidth at 1 GiB measured on this pool's B200s (GB/s): the
-# reference figure for the fused data-parallel optimizer step
-NVLINK_ALLREDUCE_BUS_GBS = 725.0
 BLEND_FWD_FLOP_PER_PAIR = 22
 BLEND_BWD_FLOP_PER_PAIR = 60
 
-# DRAM bytes (read + write) per launch at config 1 (4 views per step), from the
-# ncu --set full captures summarised in profiles/kernels_cfg1_full.md and
-# profiles/blend_kernels_cfg1.md (dram__bytes_read.sum + dram__bytes_write.sum;
-# preprocess_fwd is the one multi-view launch).
+# DRAM bytes (read + write) per launch at config 1 (4 views per step):
+# dram__bytes_read.sum + dram__bytes_write.sum from one-kernel ncu captures of
+# the same kernels on the same workload (preprocess_fwd is the one multi-view
+# launch).
 NCU_TRAFFIC_BYTES = {"preprocess_fwd": 416.7e6, "blend_fwd": 57.2e6, "blend_bwd": 110.0e6,
                      "loss": 50.8e6}
 
@@ -98,6 +95,9 @@ def parse():
     p.add_argument("--cpu-sample-views", type=int, default=2)
     p.add_argument("--mode", choices=["train", "render"], default="train",
                    help="render: forward-only novel-view rendering (config 4), frames/s")
+    p.add_argument("--no-subrecords", action="store_true",
+                   help="skip the config-2 / config-4 / render() / GPU-reference / Torch-CPU "
+                        "sub-records and the multi-GPU parity check")
     p.add_argument("--trainer", choices=["native", "autograd"], default="native",
                    help="native: NativeTrainer (fused activations/loss, flat-buffer gradients); "
                         "autograd: render() + Torch activations/loss + autograd")
@@ -275,7 +275,7 @@ def cpu_setup(cfg, n, views):
     orc.set_num_threads(os.cpu_count() or 1)
     raw = scenes.make_gaussians(cfg, seed=0, n=n)
     act = {k: v.numpy() for k, v in scenes.activate(raw).items()}
-    cams = scenes.orbit_cameras(cfg, views).numpy()
+    cams = bench_cameras(cfg, views).numpy()
     rng = np.random.default_rng(0)
     tg = [rng.uniform(0, 255, (cfg.height, cfg.width, 3)).astype(np.float32) for _ in range(views)]
     return act, cams, tg, orc.num_threads()
@@ -317,6 +317,13 @@ def run_reference(args, world, rank):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def bench_cameras(cfg, count):
+    """The configuration's views: a seeded-uniform sphere of cameras for
+    configuration 2 ("cameras on a radius-10 sphere"), an orbit in the
+    horizontal plane otherwise (view 0 at (0, 0, -distance))."""
+    return scenes.orbit_cameras(cfg, count, sphere=cfg.name == "cfg2")
 
 
 def view_plan(args, world, rank):
@@ -376,7 +383,7 @@ class Trainer:
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
         self.fp = dp.FlatParams(raw)  # replicas: identical on every rank
         self.params = self.fp.params
-        cams = scenes.orbit_cameras(cfg, total_views)
+        cams = bench_cameras(cfg, total_views)
         mine = dp.shard_views(total_views, rank, world)
         views = len(mine)
         self.cams = cams[mine].to(device)
@@ -437,7 +444,7 @@ class NativeBenchTrainer:
                                             fused_dp=fused, streams=streams)
         self.fp = self.nt.fp
         self.params = self.fp.params
-        cams = scenes.orbit_cameras(cfg, total_views)
+        cams = bench_cameras(cfg, total_views)
         mine = dp.shard_views(total_views, rank, world)
         views = len(mine)
         self.cams = cams[mine].to(device)
@@ -515,6 +522,320 @@ def count_pairs(tr, view=0):
         broke = work_t < 1e-4
         visited = torch.where(broke, work_e.long() - s, e - s)
         return int(visited.sum().item()), int(ids.shape[0]), int(mask.sum().item())
+
+
+# ---------------------------------------------------------------------------
+# Sub-records: the other configurations and paths, measured in the same run
+# ---------------------------------------------------------------------------
+
+def sub_record(fn, *args):
+    """A sub-record's result, or its failure written into the record (the
+    headline line is printed either way; a failed sub-record says why)."""
+    try:
+        return fn(*args)
+    except Exception as exc:  # recorded, not hidden: the line carries the error
+        import traceback
+
+        traceback.print_exc()
+        torch.cuda.empty_cache()
+        return {"error": f"{type(exc).__name__}: {exc}"}
+
+
+def timed_steps(fn, steps, warmup, world):
+    """warmup untimed calls, then `steps` calls between barriers and device
+    synchronisations, timed with CUDA events on the current stream; returns
+    the total in ms, max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(a.elapsed_time(b), world)
+
+
+def sub_config2(args, world, rank, device, steps=3, warmup=2):
+    """Configuration 2: 3M Gaussians, a fixed batch of 32 views of 1600x1064
+    on a radius-10 sphere sharded over the ranks (strong scaling),
+    0.8 L1 + 0.2 (1 - SSIM), the optimizer step of the main run's --dp mode."""
+    cfg = scenes.CONFIGS[2]
+    total = 32
+    tr = NativeBenchTrainer(cfg, None, total, world, rank, device, ssim_lambda=0.2,
+                            dp_mode=args.dp, streams=args.streams)
+    V = len(tr.targets)
+    ms = timed_steps(tr.step, steps, warmup, world)
+    with StageTimer() as st:
+        tr.step()
+        torch.cuda.synchronize()
+    sm = st.mean_ms()
+    opt = sm.get("gs_dp_adam_step") or sm.get("gs_adam_step")
+    opt = max_over_ranks(opt or 0.0, world)
+    rec = {"workload": f"config 2: {cfg.n} SH3 Gaussians, {cfg.width}x{cfg.height}, batch of "
+                       f"{total} views on a radius-{cfg.camera_distance} sphere sharded over "
+                       f"{world} rank(s), 0.8 L1 + 0.2 (1 - SSIM valid), Adam",
+           "value": total * steps / (ms / 1000.0), "unit": "views/s", "scaling": "strong",
+           "global_batch": total, "views_per_rank": V, "steps": steps, "warmup": warmup,
+           "ms_per_step": ms / steps, "optimizer_ms": opt,
+           "optimizer_share": opt / (ms / steps) if ms > 0 else None,
+           "optimizer": "fused DP kernel" if tr.fp.fused else (
+               "NCCL all-reduce + Adam" if world > 1 else "Adam")}
+    del tr
+    torch.cuda.empty_cache()
+    return rec
+
+
+def render_frames(nt, cams, K, chunk):
+    """Forward-only rendering of `cams` into uint8 frames, `chunk` views per
+    multi-view preprocess launch."""
+    frames = []
+    for c in range(0, cams.shape[0], chunk):
+        views = nt.forward_views(cams[c:c + chunk], K)
+        frames += [(v["image"].clamp(0, 1) * 255).round().to(torch.uint8) for v in views]
+        del views
+    return frames
+
+
+def sub_config4(args, world, rank, device, steps=2, warmup=1, chunk=8):
+    """Configuration 4: inference of 6M Gaussians, 256 views of 1920x1080 on a
+    radius-12 orbit sharded over the ranks with no communication."""
+    cfg = scenes.CONFIGS[4]
+    total = 256
+    raw = scenes.make_gaussians(cfg, seed=0, device=device)
+    nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, streams=args.streams)
+    del raw
+    mine = dp.shard_views(total, rank, world)
+    cams = scenes.orbit_cameras(cfg, total)[mine].to(device)
+    K = scenes.intrinsic_for(cfg).to(device)
+    ms = timed_steps(lambda: render_frames(nt, cams, K, chunk), steps, warmup, world)
+    rec = {"workload": f"config 4: {cfg.n} SH3 Gaussians, {total} views of {cfg.width}x"
+                       f"{cfg.height} on a radius-{cfg.camera_distance} orbit sharded over "
+                       f"{world} rank(s), forward only to uint8 frames, no communication",
+           "value": total * steps / (ms / 1000.0), "unit": "frames/s", "scaling": "strong",
+           "views_per_rank": len(mine), "views_per_launch": chunk, "steps": steps,
+           "warmup": warmup, "ms_per_step": ms / steps}
+    del nt
+    torch.cuda.empty_cache()
+    return rec
+
+
+def sub_render_api(args, world, rank, device, steps=10, warmup=3):
+    """The drop-in path scripts/train.py drives unchanged: render() with Torch
+    activations, L1 loss and autograd, one view per rank per step (the
+    reference's script steps once per view), gradient all-reduce over NCCL
+    (world > 1) and the one-launch Adam; configuration 1."""
+    cfg = scenes.CONFIGS[1]
+    tr = Trainer(cfg, None, world, world, rank, device)
+    ms = timed_steps(tr.step, steps, warmup, world)
+    rec = {"workload": f"config 1 through render() + autograd, 1 view per rank per step, "
+                       f"{world} rank(s)",
+           "value": world * steps / (ms / 1000.0), "unit": "views/s", "scaling": "weak",
+           "steps": steps, "warmup": warmup, "ms_per_step": ms / steps}
+    del tr
+    torch.cuda.empty_cache()
+    return rec
+
+
+def sub_gpu_reference(device, ours_ms, reps=3):
+    """The reference's own CUDA extension (its rasterizer.cpp + kernel.cu
+    built for sm_100a into oracle/_ref) on configuration 1's first view, per
+    stage with CUDA events (median of `reps` after one warm-up), beside this
+    library's per-view stage times from the same run."""
+    from oracle import build_ref
+
+    ref = build_ref.load_module()
+    if ref is None:
+        return {"unavailable": "reference extension not built (oracle/_ref)"}
+    cfg = scenes.CONFIGS[1]
+    W, H = cfg.width, cfg.height
+    a = scenes.activate(scenes.make_gaussians(cfg, seed=0, device=device))
+    w2c = scenes.primary_camera(cfg).to(device)
+    K = scenes.intrinsic_for(cfg).to(device)
+    campos = (-w2c[:3, :3].t() @ w2c[:3, 3]).contiguous()
+    tgt = torch.rand((H, W, 3), device=device, generator=torch.Generator(device).manual_seed(5))
+    args = (0.01, 100.0, 1 / 255, 0.5, 128.0)
+    st = {}
+
+    def ev(name, fn):
+        x = torch.cuda.Event(enable_timing=True)
+        y = torch.cuda.Event(enable_timing=True)
+        x.record()
+        out = fn()
+        y.record()
+        st.setdefault(name, []).append((x, y))
+        return out
+
+    for _ in range(reps + 1):
+        pp = ev("project_points", lambda: ref.project_points(
+            a["means"], a["scales"], a["quaternions"], a["opacities"], w2c, K, *args, W, H))
+        pts, depths, cov, conic, radii, mask = pp
+        raw_col = ev("spherical_harmonics", lambda: ref.evaluate_spherical_harmonics(
+            campos, a["means"], a["sh_coeffs_dc"], a["sh_coeffs_rest"], mask, False))
+        colors = torch.clamp_min(raw_col + 0.5, 0.0)
+        off, ids = ev("compute_tile_intersection", lambda: ref.compute_tile_intersection(
+            pts, radii, depths, mask, W, H, 16))
+        rargs = (off, ids, pts, conic, a["opacities"], colors, W, H, 16, 1e-4, 1e-4, 9.21)
+        img = ev("rasterize", lambda: ref.rasterize(*rargs))
+        up = (torch.sign(img.clamp(0, 1) - tgt) / img.numel()).contiguous()
+        gp, gc, go, gcol = ev("rasterize_backward", lambda: ref.rasterize_backward(up, *rargs))
+        ev("spherical_harmonics_backward", lambda: ref.evaluate_spherical_harmonics_backward(
+            gcol.contiguous(), campos, a["means"], a["sh_coeffs_dc"], a["sh_coeffs_rest"],
+            raw_col, mask, False))
+        ev("project_points_backward", lambda: ref.project_points_backward(
+            gp.contiguous(), gc.contiguous(), a["means"], a["scales"], a["quaternions"],
+            a["opacities"], w2c, K, W, H, cov, mask))
+    torch.cuda.synchronize()
+    ref_ms = {k: statistics.median(x.elapsed_time(y) for x, y in v[1:]) for k, v in st.items()}
+    groups = {
+        "preprocess_fwd": ["project_points", "spherical_harmonics"],
+        "tile_layout": ["compute_tile_intersection"],
+        "blend_fwd": ["rasterize"],
+        "blend_bwd": ["rasterize_backward"],
+        "preprocess_bwd": ["spherical_harmonics_backward", "project_points_backward"],
+    }
+    per_stage = {}
+    for g, names in groups.items():
+        r = sum(ref_ms[n] for n in names)
+        o = ours_ms.get(g)
+        per_stage[g] = {"reference_ms": r, "ours_ms": o,
+                        "speedup": (r / o) if o else None}
+    ref_total = sum(ref_ms.values())
+    ours_total = sum(v for v in ours_ms.values() if v is not None)
+    del a, pp, pts, depths, cov, conic, radii, mask, off, ids, img, up, gp, gc, go, gcol
+    torch.cuda.empty_cache()
+    return {"what": "reference src/cuda extension (rasterizer.cpp + kernel.cu) built for "
+                    "sm_100a, config 1 view 0 (1M SH3 Gaussians, 1920x1080), L1 gradient; "
+                    "CUDA events per stage, median of 3",
+            "reference_stage_ms": ref_ms, "per_stage": per_stage,
+            "reference_ms_per_view": ref_total, "ours_ms_per_view": ours_total,
+            "speedup_per_view": ref_total / ours_total if ours_total else None,
+            "ours_basis": "per-view stage times of this run (multi-view launches divided by "
+                          "their views)"}
+
+
+def cpu_torch_reference_cfg0(iters=3):
+    """The reference's own CPU path: src/torch_rasterizer.render(device="cpu"),
+    forward + backward of configuration 0 (20k Gaussians, 256x256, L1 against a
+    uniform target) with torch.set_num_threads(os.cpu_count()); one warm-up,
+    median of `iters`. The module is the reference's, byte-compiled by
+    oracle/build_ref.py into oracle/_ref/py."""
+    from oracle import build_ref
+
+    build_ref.stage_python()
+    if not build_ref.install_staged_importer():
+        return {"unavailable": "reference Python modules not staged (oracle/_ref/py)"}
+    tr_mod = importlib.import_module("src.torch_rasterizer")
+    prev = torch.get_num_threads()
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        cfg = scenes.CONFIGS[0]
+        raw = scenes.make_gaussians(cfg, seed=0)
+        w2c = scenes.primary_camera(cfg)
+        K = scenes.intrinsic_for(cfg)
+        tgt = torch.rand((cfg.height, cfg.width, 3), generator=torch.Generator().manual_seed(0))
+        times = []
+        for it in range(iters + 1):
+            p = {k: v.clone().requires_grad_(True) for k, v in raw.items()}
+            act = scenes.activate(p)
+            t0 = time.perf_counter()
+            img, _, _ = tr_mod.render(w2c, K, cfg.width, cfg.height, act["means"], act["scales"],
+                                      act["quaternions"], act["opacities"], act["sh_coeffs_dc"],
+                                      act["sh_coeffs_rest"], device="cpu")
+            torch.nn.functional.l1_loss(img / 255.0, tgt).backward()
+            if it > 0:
+                times.append(time.perf_counter() - t0)
+        sec = statistics.median(times)
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": 1.0 / sec, "unit": "views/s", "cores": cores, "kind": "reference",
+            "ms_per_view": sec * 1000.0,
+            "sample": f"config 0 (N={cfg.n}, {cfg.width}x{cfg.height}), fwd+bwd through "
+                      f"src/torch_rasterizer.render(device='cpu'), median of {iters}",
+            "cpu": cpu_model()}
+
+
+def nccl_allreduce_bus_gbs(numel, world, device, iters=5):
+    """NCCL all-reduce bus bandwidth over this run's ranks for a flat fp32
+    buffer of `numel` elements: 2 (w - 1) / w * bytes / time, max over ranks."""
+    import torch.distributed as dist
+
+    x = torch.ones(numel, device=device, dtype=torch.float32)
+    for _ in range(2):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    barrier(world)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        dist.all_reduce(x)
+    b.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / iters, world)
+    del x
+    return 2 * (world - 1) / world * 4 * numel / (ms * 1e-3) / 1e9, ms
+
+
+def dp_parity(tr, world, rank):
+    """Multi-GPU correctness in the bench itself: (a) every rank's flat
+    parameters are bitwise identical to rank 0's after the timed steps;
+    (b) from one state and one set of per-rank gradients, the fused data-
+    parallel step equals an NCCL all-reduce of the gradients followed by the
+    one-GPU Adam kernel (parameters within 1e-5)."""
+    import torch.distributed as dist
+
+    fp = tr.fp
+    dev = fp.device
+    torch.cuda.synchronize()
+    r0 = fp.data.clone()
+    dist.broadcast(r0, 0)
+    same = torch.tensor([1 if torch.equal(r0, fp.data) else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    del r0
+    out = {"ranks_bitwise_identical": bool(same.item()), "world": world}
+    nt = getattr(tr, "nt", None)
+    if not fp.fused or nt is None:
+        out["fused_vs_nccl"] = None
+        out["pass"] = out["ranks_bitwise_identical"]
+        return out
+    views = nt.forward_views(tr.cams, tr.K)
+    nt.loss_and_backward(views, tr.targets)
+    del views
+    torch.cuda.synchronize()
+    g = fp.grad.clone()
+    p0 = fp.data.clone()
+    m0, v0 = fp.full_moments()
+    step0 = fp.step_count
+    fp.fused_step()
+    torch.cuda.synchronize()
+    p_fused = fp.data.clone()
+    dist.all_reduce(g)
+    p_ref, m, v = p0.clone(), m0.clone(), v0.clone()
+    ends_c, lrs_c, eps_c = fp._group_table()
+    import ctypes
+
+    nat.call("gs_adam_step", fp.padded, p_ref.data_ptr(), g.data_ptr(), m.data_ptr(),
+             v.data_ptr(), len(dp.GROUPS), ctypes.cast(ends_c, ctypes.c_void_p),
+             ctypes.cast(lrs_c, ctypes.c_void_p), ctypes.cast(eps_c, ctypes.c_void_p),
+             fp.betas[0], fp.betas[1], step0 + 1, nat.stream_ptr(dev))
+    torch.cuda.synchronize()
+    d = (p_fused - p_ref).abs()
+    du = ((p_fused - p0) - (p_ref - p0)).norm() / (p_ref - p0).norm().clamp_min(1e-30)
+    mx = max_over_ranks(float(d.max()), world)
+    out["fused_vs_nccl"] = {"max_abs_param_diff": mx, "update_rel_l2": float(du),
+                            "elements_over_1e-5": int((d > 1e-5).sum()),
+                            "multicast": bool(getattr(fp, "multicast", False))}
+    out["pass"] = out["ranks_bitwise_identical"] and mx <= 1e-5
+    del g, p0, m0, v0, p_fused, p_ref, m, v, d
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -662,18 +983,26 @@ def main():
         roof["loss"] = {"bound": "hbm", "ms": stage_ms["gs_l1_ssim_loss_grad"], "achieved": gbs,
                         "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
     numel = tr.fp.padded
+    nccl = None
+    if world > 1 and not render_mode:
+        bus_gbs, ar_ms = nccl_allreduce_bus_gbs(numel, world, device)
+        nccl = {"bus_gbs": bus_gbs, "ms": ar_ms, "bytes": 4 * numel,
+                "what": "NCCL all-reduce of the flat gradient's size in this run, "
+                        "2 (w - 1) / w * bytes / time, max over ranks"}
     if stage_ms.get("gs_adam_step"):  # param, grad, m, v read; param, m, v written
         gbs = 28 * numel / (stage_ms["gs_adam_step"] * 1e-3) / 1e9
         roof["optimizer"] = {"bound": "hbm", "ms": stage_ms["gs_adam_step"], "achieved": gbs,
                              "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
     if stage_ms.get("gs_dp_adam_step"):
         # all-reduce-equivalent bus bytes per rank, 2 (w - 1) / w * 4 B * numel, against the
-        # measured 8-rank NCCL all-reduce bus bandwidth of this pool
+        # NCCL all-reduce bus bandwidth measured in this run at the same size
         bus = 2 * (world - 1) / world * 4 * numel
         gbs = bus / (stage_ms["gs_dp_adam_step"] * 1e-3) / 1e9
+        peak_bus = nccl["bus_gbs"]
         roof["optimizer"] = {"bound": "nvlink", "ms": stage_ms["gs_dp_adam_step"],
-                             "achieved": gbs, "peak": NVLINK_ALLREDUCE_BUS_GBS, "unit": "GB/s",
-                             "frac": gbs / NVLINK_ALLREDUCE_BUS_GBS,
+                             "achieved": gbs, "peak": peak_bus, "unit": "GB/s",
+                             "frac": gbs / peak_bus,
+                             "peak_source": "NCCL all-reduce bus bandwidth of this run",
                              "multicast": bool(getattr(tr.fp, "multicast", False))}
     dom = max(roof, key=lambda k: roof[k]["ms"]) if roof else None
     roofline = None
@@ -683,12 +1012,29 @@ def main():
                     "peak": r["peak"], "unit": r["unit"], "frac": r["frac"],
                     "traffic": NCU_TRAFFIC_BYTES.get(dom) if args.config == 1 and args.n is None
                     else None,
-                    "traffic_unit": "bytes/launch (ncu, profiles/)",
+                    "traffic_unit": "bytes/launch (ncu capture of this kernel, config 1)",
                     "peak_source": (f"{src} MEASURED_PEAKS.json hbm_gbs" if r["bound"] == "hbm"
                                     else "nominal FP32: 148 SMs x 128 lanes x 2 FLOP x max SM clock"
                                          " (MEASURED_PEAKS.json has no FP32 figure)"),
                     "work_per_launch": (f"{E} evaluated pairs" if r["bound"] == "fp32"
                                         else "algorithmic bytes per launch over its time")}
+
+    parity = None
+    if world > 1 and not render_mode and not args.no_subrecords:
+        parity = dp_parity(tr, world, rank)
+    subs = {}
+    headline = args.config == 1 and args.n is None and not render_mode
+    if headline and not args.no_subrecords:
+        ours_view_ms = {k: (roof[k]["ms"] if k in roof else None)
+                        for k in ("preprocess_fwd", "tile_layout", "blend_fwd", "blend_bwd",
+                                  "preprocess_bwd")}
+        del tr
+        torch.cuda.empty_cache()
+        subs["config2"] = sub_record(sub_config2, args, world, rank, device)
+        subs["config4"] = sub_record(sub_config4, args, world, rank, device)
+        subs["render_api"] = sub_record(sub_render_api, args, world, rank, device)
+        if world == 1:
+            subs["gpu_reference"] = sub_record(sub_gpu_reference, device, ours_view_ms)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not render_mode:
@@ -715,13 +1061,20 @@ def main():
             "pairs": {"K": K, "evaluated_fwd": E, "visible": visible, "tiles": T},
             "cpu_baseline": cpu,
         }
+        if headline and not args.no_cpu_baseline and world == 1:
+            line["cpu_reference_cfg0"] = sub_record(cpu_torch_reference_cfg0)
+        if nccl is not None:
+            line["nccl_allreduce"] = nccl
+        if parity is not None:
+            line["dp_parity"] = parity
+        line.update(subs)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
         torch.cuda.synchronize()
         barrier(world)
-        del tr  # symmetric-memory buffers go before the process group
+        tr = None  # symmetric-memory buffers go before the process group
         dist.destroy_process_group()
 
 
