@@ -18,11 +18,13 @@ GS_ERR_INVALID_ARGUMENT = 1
 GS_ERR_CUDA = 2
 GS_ERR_DEVICE_TIMEOUT = 3
 GS_ERR_CAPACITY = 4
+GS_ERR_PEER = 5
 _MESSAGES = {
     GS_ERR_INVALID_ARGUMENT: "invalid argument (size, pointer or alignment)",
     GS_ERR_CUDA: "CUDA error",
     GS_ERR_DEVICE_TIMEOUT: "a bounded device-side wait timed out",
     GS_ERR_CAPACITY: "capacity exceeded (scratch too small or count >= 2^30)",
+    GS_ERR_PEER: "another rank reported an error in this step (update skipped on every rank)",
 }
 
 P = ctypes.c_void_p
@@ -39,6 +41,9 @@ SIGNATURES = {
     "gs_check_status": (I, [P]),
     "gs_sync": (I, [P]),
     "gs_selftest_bounded_wait": (I, [P, P]),
+    "gs_selftest_set_timeout": (I, [P, P]),
+    "gs_status_export": (I, [P, P]),
+    "gs_status_merge": (I, [P, P]),
     "gs_project_points": (I, [I, P, P, P, P, P, P, F, F, F, F, F, I, I, P, P, P, P, P, P, P]),
     "gs_project_points_backward": (I, [I, P, P, P, P, P, P, P, P, P, I, I, P, P, P, P]),
     "gs_evaluate_sh": (I, [I, P, P, P, P, P, I, P, P]),
@@ -50,6 +55,8 @@ SIGNATURES = {
     "gs_read_total": (I, [P, P, P]),
     "gs_tile_layout_scratch_bytes": (SZ, [I, I64, I, I]),
     "gs_tile_layout": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
+    "gs_tile_layout_views_scratch_bytes": (SZ, [I, I, P, I, I]),
+    "gs_tile_layout_views": (I, [I, I, P, P, P, P, P, I, I, P, P, P, SZ, P]),
     "gs_sort_scratch_bytes": (SZ, [I64]),
     "gs_sort_pairs": (I, [I64, P, P, P, P, I, P, SZ, P]),
     "gs_rasterize": (I, [I, P, I64, P, I, P, P, P, P, I, I, F, F, F, P, P, P, P]),

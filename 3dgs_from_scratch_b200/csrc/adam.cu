@@ -15,9 +15,15 @@
 
 namespace gs {
 
+// Gated on the device status word: when an earlier kernel of the step
+// recorded an error (a bounded wait that gave up, a capacity overflow), the
+// gradient may be incomplete, so the update is skipped and the parameters and
+// moments stay as they were; the host reads the status with gs_check_status.
 __global__ void __launch_bounds__(256) adam_kernel(float4 *__restrict__ p, const float4 *__restrict__ g,
                                                    float4 *__restrict__ m, float4 *__restrict__ v,
-                                                   int64_t n4, AdamGroups G, float b1, float b2) {
+                                                   int64_t n4, AdamGroups G, float b1, float b2,
+                                                   const uint32_t *status) {
+  if (ld_volatile_u32(status) != 0u) return;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
     float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
@@ -78,10 +84,12 @@ extern "C" int gs_adam_step(int64_t n, float *params, const float *grads, float 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (n4 + 255) / 256;
   const int grid = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  uint32_t *status = device_status_word();
+  if (status == nullptr) return GS_ERR_CUDA;
   adam_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
       reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), n4, G, beta1,
-      beta2);
+      beta2, status);
   count_launch();
   return launch_status();
 }

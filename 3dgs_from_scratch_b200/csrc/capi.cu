@@ -88,6 +88,43 @@ __global__ void bounded_wait_probe_kernel(const uint32_t *flag, uint32_t *status
   if (v == 0) atomicExch(status, (uint32_t)GS_ERR_DEVICE_TIMEOUT);
 }
 
+// The device status word, copied to dst (one uint32 in device memory) on
+// `stream`, without clearing it.
+extern "C" int gs_status_export(uint32_t *dst, void *stream) {
+  if (dst == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  uint32_t *w = device_status_word();
+  if (w == nullptr) return GS_ERR_CUDA;
+  return cuda_status(cudaMemcpyAsync(dst, w, sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+__global__ void status_merge_kernel(const uint32_t *src, uint32_t *status) {
+  if (*src != 0u) atomicCAS(status, 0u, (uint32_t)GS_ERR_PEER);
+}
+
+// Makes the device status word non-zero when *src (device memory, e.g. the
+// maximum of every rank's exported status) is: a code of this rank's own is
+// kept, otherwise GS_ERR_PEER is recorded.
+extern "C" int gs_status_merge(const uint32_t *src, void *stream) {
+  if (src == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  uint32_t *w = device_status_word();
+  if (w == nullptr) return GS_ERR_CUDA;
+  status_merge_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(src, w);
+  count_launch();
+  return launch_status();
+}
+
+// The bounded-wait probe without the read-back: leaves GS_ERR_DEVICE_TIMEOUT
+// in the status word, as a kernel whose wait gave up would, for tests of the
+// paths gated on it.
+extern "C" int gs_selftest_set_timeout(const uint32_t *flag_dev, void *stream) {
+  if (flag_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  bounded_wait_probe_kernel<<<1, 1, 0, st>>>(flag_dev, device_status_word());
+  count_launch();
+  return launch_status();
+}
+
 extern "C" int gs_selftest_bounded_wait(const uint32_t *flag_dev, void *stream) {
   if (flag_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

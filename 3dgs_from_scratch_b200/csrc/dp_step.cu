@@ -19,6 +19,12 @@
 //      multimem.st (the switch replicates) or a peer store per rank;
 //   5. waits until every rank has written, so that when the kernel has
 //      finished on a rank, its parameter buffer holds the whole update.
+// Every rank also publishes, with its arrival at the first barrier, whether
+// its device status word holds an error from earlier in the step (its
+// gradient may then be incomplete); if any rank does, every rank skips
+// steps 2-4 -- the update is dropped on all ranks alike, so the replicas
+// stay identical -- and a rank without an error of its own records
+// GS_ERR_PEER.
 // The gradient crosses NVLink once per rank (in, reduced) and the parameters
 // once per rank (out); no all-reduce and no full-size Adam pass remain.
 //
@@ -117,7 +123,25 @@ __global__ void __launch_bounds__(kDpThreads) dp_adam_kernel(
     DpPeers P, float4 *mc_grad, float4 *mc_param, int world, int rank, int64_t shard4,
     float4 *__restrict__ m, float4 *__restrict__ v, AdamGroups G, float b1, float b2,
     uint32_t epoch, float4 *__restrict__ grad_out, uint32_t *status) {
+  // this rank's status for the step, to every rank (phase-2 words: 2 epoch +
+  // error), ahead of the release store of the first barrier
+  __shared__ int s_skip;
+  const uint32_t err = ld_volatile_u32(status) != 0u ? 1u : 0u;
+  if (threadIdx.x == 0) s_skip = 0;
+  if (threadIdx.x < world)
+    P.flags[threadIdx.x][flag_index(2, blockIdx.x, gridDim.x, rank)] = 2u * epoch + err;
   if (!rank_barrier(P, world, rank, 0, epoch, status)) return;
+  if (threadIdx.x < world) {
+    const uint32_t w = ld_acquire_sys(P.flags[rank] + flag_index(2, blockIdx.x, gridDim.x,
+                                                                 threadIdx.x));
+    if (w != 2u * epoch) atomicOr(&s_skip, 1);
+  }
+  __syncthreads();
+  if (s_skip) {
+    if (threadIdx.x == 0 && !err) atomicCAS(status, 0u, (uint32_t)GS_ERR_PEER);
+    rank_barrier(P, world, rank, 1, epoch, status);
+    return;
+  }
   const int64_t off4 = (int64_t)rank * shard4;
   const float4 *own = P.param[rank];
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -168,7 +192,7 @@ using namespace gs;
 
 extern "C" size_t gs_dp_flag_words(int max_blocks) {
   if (max_blocks <= 0) return 0;
-  return (size_t)2 * max_blocks * kDpMaxWorld;
+  return (size_t)3 * max_blocks * kDpMaxWorld;  // two barriers and the status exchange
 }
 
 extern "C" int gs_dp_max_blocks(void) {

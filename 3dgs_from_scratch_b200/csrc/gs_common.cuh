@@ -214,21 +214,24 @@ __device__ __forceinline__ Jac jacobian(const Cam &c, int width, int height, flo
   return j;
 }
 
-// Image-space covariance (a, b, c) with low-pass and symmetrisation
-// (kernel.cu:46-155).
-__device__ __forceinline__ float3 image_cov(const Cam &c, int width, int height, float3 p,
-                                            float sx, float sy, float sz, float qx, float qy,
-                                            float qz, float qw) {
+// World covariance R diag(s^2) R^T, full 3x3 (kernel.cu:66-80); view-independent.
+__device__ __forceinline__ void world_cov(float sx, float sy, float sz, float qx, float qy,
+                                          float qz, float qw, float Cw[9]) {
   float R[9];
   quat_to_rot(qx, qy, qz, qw, R);
   float s2[3] = {sx * sx, sy * sy, sz * sz};
-  float Cw[9];
 #pragma unroll
   for (int i = 0; i < 3; ++i)
 #pragma unroll
     for (int k = 0; k < 3; ++k)
       Cw[i * 3 + k] = R[i * 3] * s2[0] * R[k * 3] + R[i * 3 + 1] * s2[1] * R[k * 3 + 1] +
                       R[i * 3 + 2] * s2[2] * R[k * 3 + 2];
+}
+
+// Image-space covariance (a, b, c) with low-pass and symmetrisation from the
+// world covariance (kernel.cu:82-155).
+__device__ __forceinline__ float3 image_cov_from(const Cam &c, int width, int height, float3 p,
+                                                 const float Cw[9]) {
   float Cc[9];
   cam_cov(c, Cw, Cc);
   Jac j = jacobian(c, width, height, p);
@@ -245,6 +248,16 @@ __device__ __forceinline__ float3 image_cov(const Cam &c, int width, int height,
   return make_float3(c00 + kLowPass, 0.5f * (c01 + c10), c11 + kLowPass);
 }
 
+// Image-space covariance (a, b, c) with low-pass and symmetrisation
+// (kernel.cu:46-155).
+__device__ __forceinline__ float3 image_cov(const Cam &c, int width, int height, float3 p,
+                                            float sx, float sy, float sz, float qx, float qy,
+                                            float qz, float qw) {
+  float Cw[9];
+  world_cov(sx, sy, sz, qx, qy, qz, qw, Cw);
+  return image_cov_from(c, width, height, p, Cw);
+}
+
 // Result of the per-Gaussian projection with the reference's culling order
 // (kernel.cu:438-500). visible == false means mask = 0.
 struct Projected {
@@ -255,13 +268,14 @@ struct Projected {
   float ru, rv;
 };
 
-__device__ __forceinline__ Projected project_one(const Cam &c, int width, int height,
-                                                 float near_plane, float far_plane,
-                                                 float min_opacity, float min_radius,
-                                                 float max_radius, float px, float py,
-                                                 float pz, float sx, float sy, float sz,
-                                                 float qx, float qy, float qz, float qw,
-                                                 float opac) {
+// project_one with the world covariance given (computed once per Gaussian
+// when several views share it); covw == nullptr computes it from the scale
+// and quaternion.
+__device__ __forceinline__ Projected project_one_cw(const Cam &c, int width, int height,
+                                                    float near_plane, float far_plane,
+                                                    float min_opacity, float min_radius,
+                                                    float max_radius, float px, float py,
+                                                    float pz, const float covw[9], float opac) {
   Projected r;
   r.visible = false;
   r.cov_written = false;
@@ -271,7 +285,7 @@ __device__ __forceinline__ Projected project_one(const Cam &c, int width, int he
   r.u = c.fx * pc.x / pc.z + c.cx;
   r.v = c.fy * pc.y / pc.z + c.cy;
   r.depth = pc.z;
-  r.cov = image_cov(c, width, height, pc, sx, sy, sz, qx, qy, qz, qw);
+  r.cov = image_cov_from(c, width, height, pc, covw);
   r.cov_written = true;
   float det = r.cov.x * r.cov.z - r.cov.y * r.cov.y;
   float inv_det = 1.0f / fmaxf(det, 1e-12f);
@@ -284,6 +298,19 @@ __device__ __forceinline__ Projected project_one(const Cam &c, int width, int he
   r.conic = make_float3(r.cov.z * inv_det, -r.cov.y * inv_det, r.cov.x * inv_det);
   r.visible = true;
   return r;
+}
+
+__device__ __forceinline__ Projected project_one(const Cam &c, int width, int height,
+                                                 float near_plane, float far_plane,
+                                                 float min_opacity, float min_radius,
+                                                 float max_radius, float px, float py,
+                                                 float pz, float sx, float sy, float sz,
+                                                 float qx, float qy, float qz, float qw,
+                                                 float opac) {
+  float Cw[9];
+  world_cov(sx, sy, sz, qx, qy, qz, qw, Cw);
+  return project_one_cw(c, width, height, near_plane, far_plane, min_opacity, min_radius,
+                        max_radius, px, py, pz, Cw, opac);
 }
 
 // Backward of projection + covariance for one Gaussian (kernel.cu:157-409).
@@ -409,6 +436,167 @@ __device__ __forceinline__ void project_backward_one(
   gm[2] = gm2 + (W[2] * gx + W[6] * gy + W[10] * gz);
 }
 
+// ---- fused backward: per-view and per-Gaussian parts ---------------------------
+//
+// project_backward_one's chain, split for the multi-view backward: the part
+// from the conic gradient down to d loss / d (world covariance) and the
+// mean's terms depend on the view; the part from d loss / d (world
+// covariance) to the scale and rotation is linear and view-independent, so
+// it runs once per Gaussian on the sum over views.
+
+// World covariance Sigma = M M^T, M = R diag(s), symmetric: xx xy xz yy yz zz.
+__device__ __forceinline__ void world_cov_sym(float sx, float sy, float sz, float qi, float qj,
+                                              float qk, float qr, float Sg[6]) {
+  float R[9];
+  quat_to_rot(qi, qj, qk, qr, R);
+  const float M[9] = {R[0] * sx, R[1] * sy, R[2] * sz, R[3] * sx, R[4] * sy,
+                      R[5] * sz, R[6] * sx, R[7] * sy, R[8] * sz};
+  Sg[0] = M[0] * M[0] + M[1] * M[1] + M[2] * M[2];
+  Sg[1] = M[0] * M[3] + M[1] * M[4] + M[2] * M[5];
+  Sg[2] = M[0] * M[6] + M[1] * M[7] + M[2] * M[8];
+  Sg[3] = M[3] * M[3] + M[4] * M[4] + M[5] * M[5];
+  Sg[4] = M[3] * M[6] + M[4] * M[7] + M[5] * M[8];
+  Sg[5] = M[6] * M[6] + M[7] * M[7] + M[8] * M[8];
+}
+
+__device__ __forceinline__ constexpr int sym3(int r, int k) {
+  return r <= k ? (r == 0 ? k : (r == 1 ? 2 + k : 5)) : (k == 0 ? r : (k == 1 ? 2 + r : 5));
+}
+
+// Camera covariance Cc = W3 Sigma W3^T of a symmetric Sigma (both as 6 values).
+__device__ __forceinline__ void cam_cov_sym(const Cam &c, const float Sg[6], float Cc[6]) {
+  const float *W = c.W;
+  float WA[9];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      WA[i * 3 + j] = W[i * 4] * Sg[sym3(0, j)] + W[i * 4 + 1] * Sg[sym3(1, j)] +
+                      W[i * 4 + 2] * Sg[sym3(2, j)];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = i; j < 3; ++j)
+      Cc[sym3(i, j)] = WA[i * 3] * W[j * 4] + WA[i * 3 + 1] * W[j * 4 + 1] +
+                       WA[i * 3 + 2] * W[j * 4 + 2];
+}
+
+// One view's part: adds d loss / d mean (projection and the Jacobian's
+// dependence on the mean) to gm and d loss / d Sigma (symmetric) to gSg.
+// Same formulas as project_backward_one (kernel.cu:157-409), including the
+// full off-diagonal conic gradient in the Jacobian term (kernel.cu:384-389).
+__device__ __forceinline__ void view_proj_backward(const Cam &c, int width, int height, float3 pc,
+                                                   const float Sg[6], float gu, float gv,
+                                                   float gA, float gB, float gC, float gm[3],
+                                                   float gSg[6]) {
+  const float *W = c.W;
+  const float fx = c.fx, fy = c.fy;
+  const Jac j = jacobian(c, width, height, pc);
+  const float x = pc.x, y = pc.y, z = pc.z;
+  const float iz2 = j.inv_z * j.inv_z;
+  const float iz3 = iz2 * j.inv_z;
+  const bool xcl = fabsf(j.x_ndc) > j.lim_x;
+  const bool ycl = fabsf(j.y_ndc) > j.lim_y;
+  const float gm0 = (gu * fx * (W[0] * z - W[8] * x) + gv * fy * (W[4] * z - W[8] * y)) * iz2;
+  const float gm1 = (gu * fx * (W[1] * z - W[9] * x) + gv * fy * (W[5] * z - W[9] * y)) * iz2;
+  const float gm2 = (-gu * fx * (W[10] * x - W[2] * z) - gv * fy * (W[10] * y - W[6] * z)) * iz2;
+
+  float Cc[6];
+  cam_cov_sym(c, Sg, Cc);
+  // image covariance (image_cov)
+  const float A0 = j.J0 * Cc[0] + j.J2 * Cc[2];
+  const float A1 = j.J0 * Cc[1] + j.J2 * Cc[4];
+  const float A2 = j.J0 * Cc[2] + j.J2 * Cc[5];
+  const float B0 = j.J4 * Cc[1] + j.J5 * Cc[2];
+  const float B1 = j.J4 * Cc[3] + j.J5 * Cc[4];
+  const float B2 = j.J4 * Cc[4] + j.J5 * Cc[5];
+  const float a = A0 * j.J0 + A2 * j.J2 + kLowPass;
+  const float b = 0.5f * ((A1 * j.J4 + A2 * j.J5) + (B0 * j.J0 + B2 * j.J2));
+  const float cc = B1 * j.J4 + B2 * j.J5 + kLowPass;
+  const float det = a * cc - b * b;
+  const float id = 1.0f / fmaxf(det, 1e-12f);
+  const float id2 = id * id;
+  // d loss / d (image covariance a, b, c) from the conic gradient
+  const float g00 = (-cc * cc * gA + b * cc * gB - b * b * gC) * id2;
+  const float g01 = (2.0f * b * cc * gA - (a * cc + b * b) * gB + 2.0f * a * b * gC) * id2;
+  const float g11 = (-b * b * gA + a * b * gB - a * a * gC) * id2;
+  float U[6];
+  U[0] = j.J0 * W[0] + j.J2 * W[8];
+  U[1] = j.J0 * W[1] + j.J2 * W[9];
+  U[2] = j.J0 * W[2] + j.J2 * W[10];
+  U[3] = j.J4 * W[4] + j.J5 * W[8];
+  U[4] = j.J4 * W[5] + j.J5 * W[9];
+  U[5] = j.J4 * W[6] + j.J5 * W[10];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = r; k < 3; ++k)
+      gSg[sym3(r, k)] += g00 * (U[r] * U[k]) + 0.5f * g01 * (U[r] * U[3 + k] + U[k] * U[3 + r]) +
+                         g11 * (U[3 + r] * U[3 + k]);
+  const float GJ00 = g00 * j.J0;
+  const float GJ01 = g01 * j.J4;
+  const float GJ02 = g00 * j.J2 + g01 * j.J5;
+  const float GJ10 = g01 * j.J0;
+  const float GJ11 = g11 * j.J4;
+  const float GJ12 = g01 * j.J2 + g11 * j.J5;
+  const float dJ00 = 2.0f * (GJ00 * Cc[0] + GJ01 * Cc[1] + GJ02 * Cc[2]);
+  const float dJ02 = 2.0f * (GJ00 * Cc[2] + GJ01 * Cc[4] + GJ02 * Cc[5]);
+  const float dJ11 = 2.0f * (GJ10 * Cc[1] + GJ11 * Cc[3] + GJ12 * Cc[4]);
+  const float dJ12 = 2.0f * (GJ10 * Cc[2] + GJ11 * Cc[4] + GJ12 * Cc[5]);
+  const float gx = xcl ? 0.0f : dJ02 * (-fx * iz2);
+  const float gy = ycl ? 0.0f : dJ12 * (-fy * iz2);
+  const float dJ02dz = xcl ? (fx * j.xc * iz2) : (2.0f * fx * x * iz3);
+  const float dJ12dz = ycl ? (fy * j.yc * iz2) : (2.0f * fy * y * iz3);
+  const float gz = dJ00 * (-fx * iz2) + dJ11 * (-fy * iz2) + dJ02 * dJ02dz + dJ12 * dJ12dz;
+  gm[0] += gm0 + (W[0] * gx + W[4] * gy + W[8] * gz);
+  gm[1] += gm1 + (W[1] * gx + W[5] * gy + W[9] * gz);
+  gm[2] += gm2 + (W[2] * gx + W[6] * gy + W[10] * gz);
+}
+
+// The view-independent part: d loss / d Sigma (symmetric, summed over the
+// views) to the activated scale and the quaternion (kernel.cu:300-375).
+__device__ __forceinline__ void cov_backward(const float gSg[6], float sx, float sy, float sz,
+                                             float qi, float qj, float qk, float qr, float gs[3],
+                                             float gq[4]) {
+  float R[9];
+  quat_to_rot(qi, qj, qk, qr, R);
+  const float M[9] = {R[0] * sx, R[1] * sy, R[2] * sz, R[3] * sx, R[4] * sy,
+                      R[5] * sz, R[6] * sx, R[7] * sy, R[8] * sz};
+  float gM[9];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int col = 0; col < 3; ++col) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) acc += (2.0f * gSg[sym3(r, k)]) * M[k * 3 + col];
+      gM[r * 3 + col] = acc;
+    }
+  gs[0] = gM[0] * R[0] + gM[3] * R[3] + gM[6] * R[6];
+  gs[1] = gM[1] * R[1] + gM[4] * R[4] + gM[7] * R[7];
+  gs[2] = gM[2] * R[2] + gM[5] * R[5] + gM[8] * R[8];
+  const float dqi[9] = {0.0f, 2.0f * sy * qj, 2.0f * sz * qk, 2.0f * sx * qj, -4.0f * sy * qi,
+                        -2.0f * sz * qr, 2.0f * sx * qk, 2.0f * sy * qr, -4.0f * sz * qi};
+  const float dqj[9] = {-4.0f * sx * qj, 2.0f * sy * qi, 2.0f * sz * qr, 2.0f * sx * qi, 0.0f,
+                        2.0f * sz * qk, -2.0f * sx * qr, 2.0f * sy * qk, -4.0f * sz * qj};
+  const float dqk[9] = {-4.0f * sx * qk, -2.0f * sy * qr, 2.0f * sz * qi, 2.0f * sx * qr,
+                        -4.0f * sy * qk, 2.0f * sz * qj, 2.0f * sx * qi, 2.0f * sy * qj, 0.0f};
+  const float dqr[9] = {0.0f, -2.0f * sy * qk, 2.0f * sz * qj, 2.0f * sx * qk, 0.0f,
+                        -2.0f * sz * qi, -2.0f * sx * qj, 2.0f * sy * qi, 0.0f};
+  float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    q0 += gM[k] * dqi[k];
+    q1 += gM[k] * dqj[k];
+    q2 += gM[k] * dqk[k];
+    q3 += gM[k] * dqr[k];
+  }
+  gq[0] = q0;
+  gq[1] = q1;
+  gq[2] = q2;
+  gq[3] = q3;
+}
+
 // ---- parameter activations (scripts/train.py:135-140 of the reference) --------
 
 // exp(log-scale), q / max(|q|, 1e-12), sigmoid(logit): the activations the
@@ -512,6 +700,73 @@ __device__ __forceinline__ float3 sh_dir_backward(const ViewDir &d, float g0, fl
   }
   return make_float3(j00 * tx + j01 * ty + j02 * tz, j01 * tx + j11 * ty + j12 * tz,
                      j02 * tx + j12 * ty + j22 * tz);
+}
+
+// The SH part of one view of the fused backward in one pass over the 45 rest
+// coefficients: raw colour (for the clamp / sigmoid backward) and, per
+// channel, the direction-derivative sums T[ch] = sum_k d basis_{k+1} / d dir
+// * rest[k][ch]; then g (d loss / d raw colour) from the upstream colour
+// gradient, and d loss / d mean through the normalised direction. Same
+// quantities as the raw-colour loop plus sh_dir_backward (kernel.cu:619-782),
+// with the channel sum taken last. Adds into gm and gdc; returns g in g[3].
+template <typename RestAt>
+__device__ __forceinline__ void sh_view_backward(const ViewDir &d, const float b[16],
+                                                 const float dc[3], RestAt rest, float up_r,
+                                                 float up_g, float up_b, int sh_sigmoid,
+                                                 float g[3], float gm[3], float gdc[3]) {
+  const float x = d.x, y = d.y, z = d.z;
+  const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+  const float bx[15] = {0.0f, 0.0f, -kC1, kC2xy * y, 0.0f, 0.0f, kC2xy * z, 2.0f * kC2xxyy * x,
+                        2.0f * kC3a * x * y, kC3xyz * y * z, -2.0f * kC3c * x * y,
+                        -6.0f * kC3zzz * x * z, kC3c * (4.0f * zz - 3.0f * xx - yy),
+                        2.0f * kC3zxx * x * z, 3.0f * kC3a * (xx - yy)};
+  const float by[15] = {-kC1, 0.0f, 0.0f, kC2xy * x, kC2xy * z, 0.0f, 0.0f, -2.0f * kC2xxyy * y,
+                        kC3a * (xx - 3.0f * yy), kC3xyz * x * z,
+                        kC3c * (4.0f * zz - xx - 3.0f * yy), -6.0f * kC3zzz * y * z,
+                        -2.0f * kC3c * x * y, -2.0f * kC3zxx * y * z, -6.0f * kC3a * x * y};
+  const float bz[15] = {0.0f, kC1, 0.0f, 0.0f, kC2xy * y, 6.0f * kC2zz * z, kC2xy * x, 0.0f, 0.0f,
+                        kC3xyz * x * y, 8.0f * kC3c * y * z,
+                        3.0f * kC3zzz * (2.0f * zz - xx - yy), 8.0f * kC3c * x * z,
+                        kC3zxx * (xx - yy), 0.0f};
+  float raw[3], Tx[3], Ty[3], Tz[3];
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) {
+    raw[ch] = b[0] * dc[ch];
+    Tx[ch] = Ty[ch] = Tz[ch] = 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < 15; ++k)
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const float r = rest(k, ch);
+      raw[ch] += b[k + 1] * r;
+      Tx[ch] += bx[k] * r;
+      Ty[ch] += by[k] * r;
+      Tz[ch] += bz[k] * r;
+    }
+  const float up[3] = {up_r, up_g, up_b};
+  float tx = 0.f, ty = 0.f, tz = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) {
+    float gc = up[ch];
+    if (sh_sigmoid) {
+      const float col = ref_sigmoid(raw[ch]);
+      gc *= col * (1.0f - col);
+    } else {
+      gc = (raw[ch] + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
+    }
+    g[ch] = gc;
+    gdc[ch] += gc * b[0];
+    tx += gc * Tx[ch];
+    ty += gc * Ty[ch];
+    tz += gc * Tz[ch];
+  }
+  const float in = d.inv_norm;
+  const float j00 = (1.0f - xx) * in, j01 = -xy * in, j02 = -xz * in;
+  const float j11 = (1.0f - yy) * in, j12 = -yz * in, j22 = (1.0f - zz) * in;
+  gm[0] += j00 * tx + j01 * ty + j02 * tz;
+  gm[1] += j01 * tx + j11 * ty + j12 * tz;
+  gm[2] += j02 * tx + j12 * ty + j22 * tz;
 }
 
 // ---- tiles --------------------------------------------------------------------

@@ -214,32 +214,61 @@ struct PreFwdArgs {
 };
 
 
-// Forward for Gaussian i = first + t and view v from the staged chunk;
-// returns its tile count.
-__device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S, int t, int i,
-                                           int v) {
-  Cam c = load_cam(A.w2c + 16 * v, A.K + 9 * v);
-  const float *campos = A.campos + 3 * v;
+// Per-view camera record staged in shared memory by the fused kernels: rows
+// 0..2 of world_to_camera (12), fx, fy, cx, cy, camera position (3), pad.
+constexpr int kCamFloats = 20;
+
+__device__ __forceinline__ void stage_cameras(const float *w2c, const float *K,
+                                              const float *campos, int num_views,
+                                              float *s_cam) {
+  for (int k = threadIdx.x; k < num_views * kCamFloats; k += blockDim.x) {
+    const int v = k / kCamFloats, e = k - v * kCamFloats;
+    float x = 0.f;
+    if (e < 12)
+      x = w2c[16 * v + e];
+    else if (e == 12)
+      x = K[9 * v + 0];
+    else if (e == 13)
+      x = K[9 * v + 4];
+    else if (e == 14)
+      x = K[9 * v + 2];
+    else if (e == 15)
+      x = K[9 * v + 5];
+    else if (e < 19)
+      x = campos[3 * v + (e - 16)];
+    s_cam[k] = x;
+  }
+}
+
+__device__ __forceinline__ Cam cam_from_smem(const float *sc) {
+  Cam c;
+#pragma unroll
+  for (int k = 0; k < 12; ++k) c.W[k] = sc[k];
+  c.fx = sc[12];
+  c.fy = sc[13];
+  c.cx = sc[14];
+  c.cy = sc[15];
+  return c;
+}
+
+// Forward for Gaussian i = first + t and view v from the staged chunk (the
+// activated scale / quaternion / opacity and the world covariance computed
+// once for all views); returns its tile count.
+__device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S,
+                                           const float *s_cam, const float Cw[9], float op,
+                                           int t, int i, int v) {
+  const float *sc = s_cam + kCamFloats * v;
+  const Cam c = cam_from_smem(sc);
   const int64_t o = (int64_t)v * A.n + i;
   const float *m = S.means + 3 * t;
-  const float *s = S.scales + 3 * t;
-  const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
-  float sx = s[0], sy = s[1], sz = s[2], qx = q.x, qy = q.y, qz = q.z, qw = q.w, op = S.opac[t];
-  if (A.activate) {
-    const Activated a = activate_params(sx, sy, sz, qx, qy, qz, qw, op);
-    sx = a.sx; sy = a.sy; sz = a.sz;
-    qx = a.qx; qy = a.qy; qz = a.qz; qw = a.qw;
-    op = a.opac;
-  }
-  Projected p = project_one(c, A.width, A.height, A.near_plane, A.far_plane, A.min_opacity,
-                            A.min_radius, A.max_radius, m[0], m[1], m[2], sx, sy, sz, qx, qy, qz,
-                            qw, op);
+  Projected p = project_one_cw(c, A.width, A.height, A.near_plane, A.far_plane, A.min_opacity,
+                               A.min_radius, A.max_radius, m[0], m[1], m[2], Cw, op);
   float2 pt = make_float2(0.f, 0.f), rd = make_float2(0.f, 0.f);
   float depth = 0.f;
   float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = make_float4(0.f, 0.f, 0.f, 0.f);
   int count = 0;
   if (p.visible) {
-    ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), m[0], m[1], m[2]);
+    ViewDir d = view_dir(sc[16], sc[17], sc[18], m[0], m[1], m[2]);
     float b[16];
     sh_basis(d.x, d.y, d.z, b);
     const float *r = S.rest + 45 * t;
@@ -281,10 +310,26 @@ __device__ __forceinline__ int pre_fwd_one(const PreFwdArgs &A, const PreSmem &S
 // it), added to the global totals once per chunk: one global atomic per
 // view per chunk rather than per warp (same-address atomics from every warp
 // of every view serialise in L2).
-__device__ __forceinline__ void pre_fwd_views(const PreFwdArgs &A, const PreSmem &S, int t,
-                                              int i, bool active, uint32_t *s_tot) {
+__device__ __forceinline__ void pre_fwd_views(const PreFwdArgs &A, const PreSmem &S,
+                                              const float *s_cam, int t, int i, bool active,
+                                              uint32_t *s_tot) {
+  float Cw[9];
+  float op = 0.f;
+  if (active) {
+    const float *s = S.scales + 3 * t;
+    const float4 q = reinterpret_cast<const float4 *>(S.quats)[t];
+    float sx = s[0], sy = s[1], sz = s[2], qx = q.x, qy = q.y, qz = q.z, qw = q.w;
+    op = S.opac[t];
+    if (A.activate) {
+      const Activated a = activate_params(sx, sy, sz, qx, qy, qz, qw, op);
+      sx = a.sx; sy = a.sy; sz = a.sz;
+      qx = a.qx; qy = a.qy; qz = a.qz; qw = a.qw;
+      op = a.opac;
+    }
+    world_cov(sx, sy, sz, qx, qy, qz, qw, Cw);
+  }
   for (int v = 0; v < A.num_views; ++v) {
-    int count = active ? pre_fwd_one(A, S, t, i, v) : 0;
+    int count = active ? pre_fwd_one(A, S, s_cam, Cw, op, t, i, v) : 0;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) count += __shfl_xor_sync(0xffffffffu, count, o);
     if ((threadIdx.x & 31) == 0 && count) atomicAdd(s_tot + v, (uint32_t)count);
@@ -310,7 +355,9 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArg
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
   uint32_t *s_tot = reinterpret_cast<uint32_t *>(smem_raw + sizeof(PreSmem));
+  float *s_cam = reinterpret_cast<float *>(s_tot + A.num_views);
   zero_totals(A, s_tot);
+  stage_cameras(A.w2c, A.K, A.campos, A.num_views, s_cam);
   const int t = threadIdx.x;
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
@@ -322,7 +369,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArg
   stage(S.dc, A.dc + 3 * f, 3 * cnt);
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
-  pre_fwd_views(A, S, t, first + t, t < cnt, s_tot);
+  pre_fwd_views(A, S, s_cam, t, first + t, t < cnt, s_tot);
   flush_totals(A, s_tot);
 }
 
@@ -351,9 +398,11 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
   uint32_t *s_tot = reinterpret_cast<uint32_t *>(smem_raw + 2 * sizeof(PreSmem));
+  float *s_cam = reinterpret_cast<float *>(s_tot + A.num_views);
   __shared__ __align__(8) uint64_t bars[2];
   const int t = threadIdx.x;
   zero_totals(A, s_tot);
+  stage_cameras(A.w2c, A.K, A.campos, A.num_views, s_cam);
   if (t == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -382,7 +431,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_pipe_kernel(PreF
       return;
     }
     phase ^= 1u << s;
-    pre_fwd_views(A, stg[s], t, c * kPreBlock + t, true, s_tot);
+    pre_fwd_views(A, stg[s], s_cam, t, c * kPreBlock + t, true, s_tot);
     flush_totals(A, s_tot);  // per chunk: the 32-bit partials cannot overflow
     __syncthreads();  // every thread is done with stg[s] (and s_tot) before reuse
     zero_totals(A, s_tot);
@@ -407,60 +456,47 @@ struct PreBwdArgs {
   int num_views;
   int64_t n;
   int64_t gp_vstride, gs_vstride;
+  int vec_upstream;  // upstream gradients loadable as float2 / float4
 };
 
-// Gradients of one view for one Gaussian (activated parameters sx.., q, op):
-// w.r.t. the mean (projection and SH direction), the activated scale and
-// quaternion, the activated opacity, and the colour pre-activation gradient
-// g[3] with its SH basis b[16] (d colour / d sh coefficients).
-struct ViewGrads {
-  float gm[3], gsc[3], gq[4], gop, g[3], b[16];
+// One view's upstream values for one Gaussian: its culling mask, d loss /
+// d points_img, and d loss / d splat record (conic a, b, c, opacity; r, g, b).
+struct Upstream {
+  float2 gp;
+  float4 s0, s1;
+  uint32_t mask;
 };
 
-__device__ __forceinline__ void view_grads(const PreBwdArgs &A, int v, int64_t i, float px,
-                                           float py, float pz, float sx, float sy, float sz,
-                                           float4 q, const float *dcc, const float *r,
-                                           ViewGrads &G) {
-  Cam c = load_cam(A.w2c + 16 * v, A.K + 9 * v);
-  const float *campos = A.campos + 3 * v;
-  float3 pc = to_camera(c, px, py, pz);
-  float3 cov = image_cov(c, A.width, A.height, pc, sx, sy, sz, q.x, q.y, q.z, q.w);
+__device__ __forceinline__ Upstream load_upstream(const PreBwdArgs &A, int v, int64_t i) {
+  Upstream u;
+  u.mask = A.mask[v * A.n + i];
   const float *gp = A.g_points + v * A.gp_vstride + i * A.gp_stride;
   const float *gsp = A.g_splat + v * A.gs_vstride + i * A.gs_stride;
-  project_backward_one(c, A.width, A.height, pc, gp[0], gp[1], sx, sy, sz, q.x, q.y, q.z, q.w,
-                       cov, gsp[0], gsp[1], gsp[2], G.gm, G.gsc, G.gq);
-  G.gop = gsp[3];
-  ViewDir d = view_dir(__ldg(campos), __ldg(campos + 1), __ldg(campos + 2), px, py, pz);
-  sh_basis(d.x, d.y, d.z, G.b);
-#pragma unroll
-  for (int ch = 0; ch < 3; ++ch) {
-    float raw = G.b[0] * dcc[ch];
-#pragma unroll
-    for (int k = 0; k < 15; ++k) raw += G.b[k + 1] * r[k * 3 + ch];
-    float gc = gsp[4 + ch];
-    if (A.sh_sigmoid) {
-      float col = ref_sigmoid(raw);
-      gc *= col * (1.0f - col);
-    } else {
-      gc = (raw + 0.5f >= 0.0f) ? gc : 0.0f;  // clamp_min backward passes where >= 0
-    }
-    G.g[ch] = gc;
+  if (A.vec_upstream) {  // strides 2 and 8 floats, 8- and 16-byte aligned
+    u.gp = __ldg(reinterpret_cast<const float2 *>(gp));
+    u.s0 = __ldg(reinterpret_cast<const float4 *>(gsp));
+    u.s1 = __ldg(reinterpret_cast<const float4 *>(gsp) + 1);
+  } else {
+    u.gp = make_float2(gp[0], gp[1]);
+    u.s0 = make_float4(gsp[0], gsp[1], gsp[2], gsp[3]);
+    u.s1 = make_float4(gsp[4], gsp[5], gsp[6], 0.f);
   }
-  float3 gmsh = sh_dir_backward(d, G.g[0], G.g[1], G.g[2], [&](int k, int ch) { return r[k * 3 + ch]; });
-  G.gm[0] += gmsh.x;
-  G.gm[1] += gmsh.y;
-  G.gm[2] += gmsh.z;
+  return u;
 }
 
 // Backward for Gaussian i = first + t over every view: reads the staged
 // parameters and overwrites them in place with the summed gradients (zeros
-// for a Gaussian culled in every view). With several views the SH-rest
-// gradient is summed in rest_acc (this thread's 45 floats) while the staged
-// coefficients are still needed; the activation Jacobians (exp, quaternion
-// normalisation, sigmoid) are linear and applied once to the sums.
+// for a Gaussian culled in every view). Per view: the projection's and the
+// image covariance's chain down to d loss / d (world covariance) and the
+// mean, and the SH chain; once per Gaussian, after the views: the world
+// covariance to scale and rotation (linear, so applied to the sum over the
+// views) and the activation Jacobians (exp, quaternion normalisation,
+// sigmoid; also linear). With several views the SH-rest gradient is summed
+// in rest_acc (this thread's 45 floats) while the staged coefficients are
+// still needed.
 template <bool MULTI>
-__device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, float *rest_acc,
-                                            int t, int i) {
+__device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, const float *s_cam,
+                                            float *rest_acc, int t, int i) {
   float *m = S.means + 3 * t;
   float *s = S.scales + 3 * t;
   float *qq = S.quats + 4 * t;
@@ -477,7 +513,9 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, flo
     sz = act.sz;
     q = make_float4(act.qx, act.qy, act.qz, act.qw);
   }
-  float gm[3] = {0.f, 0.f, 0.f}, gsc[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
+  float Sg[6];
+  world_cov_sym(sx, sy, sz, q.x, q.y, q.z, q.w, Sg);
+  float gm[3] = {0.f, 0.f, 0.f}, gSg[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float gdc[3] = {0.f, 0.f, 0.f}, opac_grad = 0.f;
   bool any = false;
   const int views = MULTI ? A.num_views : 1;
@@ -485,33 +523,40 @@ __device__ __forceinline__ void pre_bwd_one(const PreBwdArgs &A, PreSmem &S, flo
 #pragma unroll
     for (int k = 0; k < 45; ++k) rest_acc[k] = 0.f;
   }
+  // The upstream gradients of view v + 1 are loaded while view v is computed
+  // (their loads do not wait on the view's mask test).
+  Upstream up = load_upstream(A, 0, i);
   for (int v = 0; v < views; ++v) {
-    if (!A.mask[v * A.n + i]) continue;
+    const Upstream cur = up;
+    if (v + 1 < views) up = load_upstream(A, v + 1, i);
+    if (!cur.mask) continue;
     any = true;
-    ViewGrads G;
-    view_grads(A, v, i, px, py, pz, sx, sy, sz, q, dcc, r, G);
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      gm[k] += G.gm[k];
-      gsc[k] += G.gsc[k];
-      gdc[k] += G.g[k] * G.b[0];
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) gq[k] += G.gq[k];
-    opac_grad += G.gop;
+    const float *sc = s_cam + kCamFloats * v;
+    const Cam c = cam_from_smem(sc);
+    view_proj_backward(c, A.width, A.height, to_camera(c, px, py, pz), Sg, cur.gp.x, cur.gp.y,
+                       cur.s0.x, cur.s0.y, cur.s0.z, gm, gSg);
+    opac_grad += cur.s0.w;
+    const ViewDir d = view_dir(sc[16], sc[17], sc[18], px, py, pz);
+    float b[16];
+    sh_basis(d.x, d.y, d.z, b);
+    float g[3];
+    sh_view_backward(d, b, dcc, [&](int k, int ch) { return r[k * 3 + ch]; }, cur.s1.x,
+                     cur.s1.y, cur.s1.z, A.sh_sigmoid, g, gm, gdc);
     if (MULTI) {
 #pragma unroll
       for (int k = 0; k < 15; ++k)
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) rest_acc[k * 3 + ch] += G.g[ch] * G.b[k + 1];
+        for (int ch = 0; ch < 3; ++ch) rest_acc[k * 3 + ch] += g[ch] * b[k + 1];
     } else {
 #pragma unroll
       for (int k = 0; k < 15; ++k)
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = G.g[ch] * G.b[k + 1];
+        for (int ch = 0; ch < 3; ++ch) r[k * 3 + ch] = g[ch] * b[k + 1];
     }
   }
+  float gsc[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
   if (any) {
+    cov_backward(gSg, sx, sy, sz, q.x, q.y, q.z, q.w, gsc, gq);
     if (A.activate) {
       // exp backward (scale), normalisation backward (quaternion)
       gsc[0] *= act.sx;
@@ -574,6 +619,9 @@ __global__ void __launch_bounds__(kPreBlock, MULTI ? GS_PRE_MULTI_MINB : 1)
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem &S = *reinterpret_cast<PreSmem *>(smem_raw);
   float *rest_acc = reinterpret_cast<float *>(smem_raw + sizeof(PreSmem));
+  float *s_cam = reinterpret_cast<float *>(smem_raw + sizeof(PreSmem) +
+                                           (MULTI ? kPreRestAccBytes : 0));
+  stage_cameras(A.w2c, A.K, A.campos, A.num_views, s_cam);
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
@@ -585,7 +633,7 @@ __global__ void __launch_bounds__(kPreBlock, MULTI ? GS_PRE_MULTI_MINB : 1)
   stage(S.rest, A.rest + 45 * f, 45 * cnt);
   __syncthreads();
   const int t = threadIdx.x;
-  if (t < cnt) pre_bwd_one<MULTI>(A, S, rest_acc + 45 * t, t, first + t);
+  if (t < cnt) pre_bwd_one<MULTI>(A, S, s_cam, rest_acc + 45 * t, t, first + t);
   __syncthreads();
   if (A.accumulate) {
     stage_add(A.g_means + 3 * f, S.means, 3 * cnt);
@@ -612,8 +660,11 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
   extern __shared__ __align__(16) unsigned char smem_raw[];
   PreSmem *stg = reinterpret_cast<PreSmem *>(smem_raw);
   float *rest_acc = reinterpret_cast<float *>(smem_raw + 2 * sizeof(PreSmem));
+  float *s_cam = reinterpret_cast<float *>(smem_raw + 2 * sizeof(PreSmem) +
+                                           (MULTI ? kPreRestAccBytes : 0));
   __shared__ __align__(8) uint64_t bars[2];
   const int t = threadIdx.x;
+  stage_cameras(A.w2c, A.K, A.campos, A.num_views, s_cam);
   if (t == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
@@ -644,7 +695,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_backward_pipe_kernel(Pre
     }
     phase ^= 1u << s;
     const int i0 = c * kPreBlock;
-    pre_bwd_one<MULTI>(A, stg[s], rest_acc + 45 * t, t, i0 + t);
+    pre_bwd_one<MULTI>(A, stg[s], s_cam, rest_acc + 45 * t, t, i0 + t);
     fence_proxy_async_smem();  // this thread's shared writes are visible to the bulk stores
     __syncthreads();
     if (t == 0) {
@@ -766,7 +817,8 @@ static int launch_preprocess_forward(const PreFwdArgs &A, int n, cudaStream_t st
                        aligned16(A.opac) && aligned16(A.dc) && aligned16(A.rest) &&
                        !(A.num_views > 1 && GS_PRE_FWD_MULTI_SIMPLE);
   const int full = pipe_ok ? n / kPreBlock : 0;
-  const size_t tot_bytes = sizeof(uint32_t) * (size_t)A.num_views;
+  // per-view pair totals and staged cameras after the stage(s)
+  const size_t tot_bytes = sizeof(uint32_t) * (size_t)A.num_views * (1 + kCamFloats);
   if (2 * sizeof(PreSmem) + tot_bytes > 200 * 1024) return GS_ERR_CAPACITY;  // views per launch
   if (full > 0) {
     const size_t smem = 2 * sizeof(PreSmem) + tot_bytes;
@@ -854,17 +906,13 @@ static int launch_preprocess_backward(const PreBwdArgs &A, int n, cudaStream_t s
                        aligned16(A.rest) && aligned16(A.g_means) && aligned16(A.g_scales) &&
                        aligned16(A.g_quats) && aligned16(A.g_dc) && aligned16(A.g_rest);
   const int full = (pipe_ok && !(MULTI && GS_PRE_MULTI_SIMPLE)) ? n / kPreBlock : 0;
-  const size_t extra = MULTI ? kPreRestAccBytes : 0;
+  const size_t extra =
+      (MULTI ? kPreRestAccBytes : 0) + sizeof(float) * kCamFloats * (size_t)A.num_views;
+  if (sizeof(PreSmem) + extra > 200 * 1024) return GS_ERR_CAPACITY;  // views per launch
   if (full > 0) {
     const size_t smem = 2 * sizeof(PreSmem) + extra;
-    static int attr_done[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-      cudaFuncSetAttribute(preprocess_backward_pipe_kernel<MULTI>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done[dev] = 1;
-    }
+    cudaFuncSetAttribute(preprocess_backward_pipe_kernel<MULTI>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int grid = pipe_grid(full, (const void *)preprocess_backward_pipe_kernel<MULTI>, smem);
     preprocess_backward_pipe_kernel<MULTI>
         <<<grid, kPreBlock, smem, st>>>(A, full, device_status_word());
@@ -873,14 +921,8 @@ static int launch_preprocess_backward(const PreBwdArgs &A, int n, cudaStream_t s
   const int base = full * kPreBlock;
   if (base < n) {
     const size_t smem = sizeof(PreSmem) + extra;
-    static int attr_done1[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done1[dev]) {
-      cudaFuncSetAttribute(preprocess_backward_kernel<MULTI>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_done1[dev] = 1;
-    }
+    cudaFuncSetAttribute(preprocess_backward_kernel<MULTI>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int blocks = (n - base + kPreBlock - 1) / kPreBlock;
     preprocess_backward_kernel<MULTI><<<blocks, kPreBlock, smem, st>>>(A, n, base);
     count_launch();
@@ -908,7 +950,11 @@ static int preprocess_backward_impl(int n, int num_views, const float *means,
                sh_sigmoid, activate, accumulate, mask, grad_points_img, gp_stride, grad_splat,
                gs_stride, grad_means, grad_scales, grad_quats, grad_opacities, grad_dc,
                grad_rest, num_views, (int64_t)n, (int64_t)n * gp_stride,
-               (int64_t)n * gs_stride};
+               (int64_t)n * gs_stride,
+               (gp_stride == 2 && gs_stride == 8 && ((uintptr_t)grad_points_img & 7) == 0 &&
+                ((uintptr_t)grad_splat & 15) == 0)
+                   ? 1
+                   : 0};
   return num_views > 1 ? launch_preprocess_backward<true>(A, n, st)
                        : launch_preprocess_backward<false>(A, n, st);
 }

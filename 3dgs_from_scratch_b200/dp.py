@@ -260,13 +260,32 @@ class FlatParams:
                  self.step_count, self._epoch, self.num_blocks, out,
                  nat.stream_ptr(self.device))
 
+    def merge_status(self):
+        """Every rank's device status word, max-reduced over the group and
+        merged into the local word (gs_status_export / gs_status_merge), so
+        that the status-gated Adam kernel skips or applies the update on all
+        ranks alike. No-op at world 1."""
+        import torch.distributed as dist
+
+        if self.device.type != "cuda" or not (dist.is_available() and dist.is_initialized()):
+            return
+        if dist.get_world_size(self.group) <= 1:
+            return
+        st = torch.zeros(1, dtype=torch.int32, device=self.device)
+        nat.call("gs_status_export", st.data_ptr(), nat.stream_ptr(self.device))
+        dist.all_reduce(st, op=dist.ReduceOp.MAX, group=self.group)
+        nat.call("gs_status_merge", st.data_ptr(), nat.stream_ptr(self.device))
+
     def step(self):
         """The step's gradient sum over the ranks and the Adam update: the
-        fused kernel with fused_dp, else NCCL all-reduce + one-launch Adam."""
+        fused kernel with fused_dp, else NCCL all-reduce + one-launch Adam.
+        Both skip the update on every rank when any rank's device status
+        word holds an error from earlier in the step."""
         if self.fused:
             self.fused_step()
         else:
             self.allreduce_grads(self.group)
+            self.merge_status()
             self.adam_step()
 
 

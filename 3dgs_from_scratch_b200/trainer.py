@@ -49,7 +49,7 @@ class NativeTrainer:
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 streams: int = 2, **render_opts):
+                 streams: int = 2, layout: str = "per_view", **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -70,6 +70,12 @@ class NativeTrainer:
         self.num_streams = int(streams)
         self._side = [torch.cuda.Stream(device=self.device) for _ in range(self.num_streams - 1)]
         self._ssim_scratch = [None] * self.num_streams
+        # "batched": every view's tile layout in one cooperative launch
+        # (gs_tile_layout_views); "per_view": one gs_tile_layout per view on
+        # the view's stream
+        if layout not in ("batched", "per_view"):
+            raise ValueError("layout must be 'batched' or 'per_view'")
+        self.layout = layout
         self.tx = (self.width + 15) // 16
         self.ty = (self.height + 15) // 16
 
@@ -145,6 +151,9 @@ class NativeTrainer:
         rc = nat.query("gs_check_status", st)
         if rc:
             raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+        self.last_totals = [int(x) for x in host_totals]
+        if self.layout == "batched":
+            self._layout_views(views, self.last_totals)
         self._fork()
         for v, s in enumerate(views):
             total = int(host_totals[v])
@@ -152,8 +161,9 @@ class NativeTrainer:
             s["stream"] = self._view_stream(v)
             with torch.cuda.stream(s["stream"]):
                 vst = nat.stream_ptr(dev)
-                s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
-                    s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
+                if self.layout != "batched":
+                    s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
+                        s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
                 s["image"] = torch.empty((H, W, 3), **f)
                 s["final_t"] = torch.empty((H * W,), **f)
                 s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
@@ -165,6 +175,34 @@ class NativeTrainer:
                          vst)
         self._join()
         return views
+
+    def _layout_views(self, views, totals):
+        """Every view's tile layout in one launch on the current stream: the
+        views' sorted id lists concatenated in one buffer, their per-tile
+        offsets (view-local) in one (views, tiles) array."""
+        import ctypes
+
+        dev = self.device
+        b = self._batch
+        V, n = len(views), self.n
+        tot_c = (ctypes.c_int64 * V)(*totals)
+        ktot = sum(totals)
+        ids = torch.empty((max(ktot, 1),), device=dev, dtype=torch.int32)
+        offsets = torch.empty((V, self.tx * self.ty), device=dev, dtype=torch.int32)
+        nbytes = int(nat.query("gs_tile_layout_views_scratch_bytes", n, V,
+                               ctypes.cast(tot_c, ctypes.c_void_p), self.width, self.height))
+        if nbytes == 0 and ktot > 0:
+            raise nat.NativeError("gs_tile_layout_views_scratch_bytes", nat.GS_ERR_CAPACITY)
+        scratch = torch.empty((max(nbytes, 1),), device=dev, dtype=torch.uint8)
+        nat.call("gs_tile_layout_views", n, V, b["points"].data_ptr(), b["radii"].data_ptr(),
+                 b["depths"].data_ptr(), b["counts"].data_ptr(),
+                 ctypes.cast(tot_c, ctypes.c_void_p), self.width, self.height, ids.data_ptr(),
+                 offsets.data_ptr(), scratch.data_ptr(), nbytes, nat.stream_ptr(dev))
+        start = 0
+        for v, s in enumerate(views):
+            s["offsets"] = offsets[v]
+            s["ids"] = ids[start:start + totals[v]]
+            start += totals[v]
 
     def _stage_targets(self, targets):
         """Targets held in host memory (pinned, for the copy to be
@@ -264,13 +302,28 @@ class NativeTrainer:
                  o["transmittance_threshold"], o["chi_squared_threshold"], g_points.data_ptr(),
                  g_splat.data_ptr(), st)
 
-    def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True, step_index=None):
+    def check_status(self):
+        """Synchronise the device and raise NativeError if a kernel of this
+        library recorded an error since the last check (the status word is
+        then cleared)."""
+        rc = nat.query("gs_check_status", nat.stream_ptr(self.device))
+        if rc:
+            raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+
+    def step(self, world_to_cameras, intrinsics, targets, optimizer_step=True, step_index=None,
+             check_status=True):
         """One training step over this rank's views: render, loss, backward
         (the first view overwrites the flat gradient, so no zeroing is needed
         between steps), then the gradient sum over the ranks and Adam
         (FlatParams.step: NCCL all-reduce + one-launch Adam, or with
         fused_dp the one-kernel reduce-scatter / sharded Adam / all-gather).
-        With a strategy and step_index, the densification schedule of
+        The optimizer kernels skip their update when the device status word
+        holds an error from this step (a bounded wait that gave up, on any
+        rank), so a step with an incomplete gradient leaves the parameters
+        unchanged; with check_status the word is read once after the
+        optimizer (one synchronisation) and the error raised in the same
+        step, else it surfaces at the next check (the next step's pair-count
+        read). With a strategy and step_index, the densification schedule of
         scripts/train.py:224-227 runs after the optimizer step (it may change
         the number of Gaussians). Targets in host memory are copied while the
         views are rendered. Returns the losses."""
@@ -279,6 +332,8 @@ class NativeTrainer:
         losses = self.loss_and_backward(views, targets, targets_ready=ready)
         if optimizer_step:
             self.fp.step()
-            if self.strategy is not None and step_index is not None:
-                self.strategy.adjust(self.fp, int(step_index))
+        if check_status:
+            self.check_status()
+        if optimizer_step and self.strategy is not None and step_index is not None:
+            self.strategy.adjust(self.fp, int(step_index))
         return losses

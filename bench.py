@@ -82,6 +82,8 @@ def parse():
                         "config 2 defaults to its batch of 32")
     p.add_argument("--streams", type=int, default=2,
                    help="CUDA streams the native trainer spreads a step's views over")
+    p.add_argument("--layout", choices=["batched", "per_view"], default="per_view",
+                   help="tile layout: every view in one cooperative launch, or one per view")
     p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="fused",
                    help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
                         "reduce-scatter / sharded Adam / all-gather kernel (multicast when "
@@ -171,7 +173,8 @@ class ClockSampler:
 class StageTimer:
     """CUDA events around each C-ABI call of interest, on the launching stream."""
 
-    WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_blend_forward", "gs_blend_backward",
+    WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_tile_layout_views",
+             "gs_blend_forward", "gs_blend_backward",
              "gs_preprocess_backward", "gs_l1_loss_grad", "gs_l1_ssim_loss_grad", "gs_adam_step",
              "gs_dp_adam_step", "gs_preprocess_forward_views", "gs_preprocess_backward_views")
 
@@ -367,7 +370,8 @@ def workload_config(args, cfg, views_per_rank):
                    "peer loads and stores)")),
             "l2": "inputs larger than L2 (236 MB params + 472 MB Adam state per rank)",
             "optimizer": "Adam, six groups in one flat buffer, one native launch",
-            "trainer": args.trainer, "streams": getattr(args, "streams", 1)}
+            "trainer": args.trainer, "streams": getattr(args, "streams", 1),
+            "layout": getattr(args, "layout", "batched")}
 
 
 # ---------------------------------------------------------------------------
@@ -434,14 +438,14 @@ class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
     def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl",
-                 streams=2):
+                 streams=2, layout="per_view"):
         self.cfg = cfg
         self.world = world
         self.device = device
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
         fused = {"nccl": False, "fused": "auto", "fused-p2p": "p2p"}[dp_mode]
         self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda,
-                                            fused_dp=fused, streams=streams)
+                                            fused_dp=fused, streams=streams, layout=layout)
         self.fp = self.nt.fp
         self.params = self.fp.params
         cams = bench_cameras(cfg, total_views)
@@ -467,7 +471,11 @@ class NativeBenchTrainer:
             tg = self.host_targets
         else:
             cams, K, tg = self.cams, self.K, self.targets
-        losses = self.nt.step(cams, K, tg)
+        # e2e reads the step's result back, so the status check after the
+        # optimizer rides on that synchronisation; the device-timed steps are
+        # queued back to back and their status is read at the next step's
+        # pair-count read and after the timed region
+        losses = self.nt.step(cams, K, tg, check_status=e2e)
         if e2e:
             self.host_loss.copy_(losses, non_blocking=True)
         return losses
@@ -568,7 +576,7 @@ def sub_config2(args, world, rank, device, steps=3, warmup=2):
     cfg = scenes.CONFIGS[2]
     total = 32
     tr = NativeBenchTrainer(cfg, None, total, world, rank, device, ssim_lambda=0.2,
-                            dp_mode=args.dp, streams=args.streams)
+                            dp_mode=args.dp, streams=args.streams, layout=args.layout)
     V = len(tr.targets)
     ms = timed_steps(tr.step, steps, warmup, world)
     with StageTimer() as st:
@@ -608,7 +616,8 @@ def sub_config4(args, world, rank, device, steps=2, warmup=1, chunk=8):
     cfg = scenes.CONFIGS[4]
     total = 256
     raw = scenes.make_gaussians(cfg, seed=0, device=device)
-    nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, streams=args.streams)
+    nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, streams=args.streams,
+                                   layout=args.layout)
     del raw
     mine = dp.shard_views(total, rank, world)
     cams = scenes.orbit_cameras(cfg, total)[mine].to(device)
@@ -853,7 +862,7 @@ def main():
     total_views, V, lam = view_plan(args, world, rank)
     if args.trainer == "native":
         tr = NativeBenchTrainer(cfg, args.n, total_views, world, rank, device, ssim_lambda=lam,
-                                dp_mode=args.dp, streams=args.streams)
+                                dp_mode=args.dp, streams=args.streams, layout=args.layout)
     else:
         if args.dp != "nccl":
             raise SystemExit("--dp fused needs --trainer native")
@@ -884,6 +893,9 @@ def main():
         barrier(world)
         torch.cuda.synchronize()
     launches = nat.launch_count() - launches0
+    rc = nat.query("gs_check_status", nat.stream_ptr())
+    if rc:
+        raise nat.NativeError("timed steps", rc, nat.lib().gs_last_cuda_error())
     ms_total = max_over_ranks(start.elapsed_time(end), world)
     ms_step = ms_total / args.steps
     value = total_views * args.steps / (ms_total / 1000.0)
@@ -963,6 +975,17 @@ def main():
         gbs = (LAYOUT_BYTES_PER_PAIR * K + 4 * T) / (stage_ms["gs_tile_layout"] * 1e-3) / 1e9
         roof["tile_layout"] = {"bound": "hbm", "ms": stage_ms["gs_tile_layout"], "achieved": gbs,
                                "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}
+    if stage_ms.get("gs_tile_layout_views"):
+        # one launch lays out every view of the step: the reference's bytes for
+        # each view's pairs (its 6-pass 64-bit sort basis) and tile offsets
+        ms = stage_ms["gs_tile_layout_views"]
+        ktot = sum(getattr(getattr(tr, "nt", None), "last_totals", None) or [K] * V)
+        gbs = (LAYOUT_BYTES_PER_PAIR * ktot + 4 * T * V) / (ms * 1e-3) / 1e9
+        roof["tile_layout"] = {"bound": "hbm", "ms": ms / V, "ms_per_launch": ms,
+                               "views_per_launch": V, "pairs_per_launch": int(ktot),
+                               "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                               "basis": "reference's bytes: (12 + 144 + 8) B per pair + "
+                                        "4 B per tile"}
     for key, nm, fl in (("blend_fwd", "gs_blend_forward", BLEND_FWD_FLOP_PER_PAIR),
                         ("blend_bwd", "gs_blend_backward", BLEND_BWD_FLOP_PER_PAIR)):
         if stage_ms.get(nm):

@@ -40,6 +40,7 @@ extern "C" {
 #define GS_ERR_CUDA 2               /* a CUDA call failed: see gs_last_cuda_error */
 #define GS_ERR_DEVICE_TIMEOUT 3     /* a bounded device-side wait gave up */
 #define GS_ERR_CAPACITY 4           /* scratch too small / count beyond 2^30 */
+#define GS_ERR_PEER 5               /* another rank reported an error in this step */
 
 /* Tile edge in pixels; the reference hard-codes 16 (src/cuda/wrapper.py:267). */
 #define GS_TILE 16
@@ -52,15 +53,34 @@ GS_API uint64_t gs_launch_count(void);
 
 /* Device status word: bounded spin-waits (the sort's decoupled look-back,
  * the scan's look-back) record GS_ERR_DEVICE_TIMEOUT here instead of
- * hanging. gs_check_status synchronises `stream`, returns and clears it. */
+ * hanging. gs_check_status synchronises `stream`, returns and clears it.
+ * The optimizer kernels (gs_adam_step, gs_dp_adam_step) read it first and
+ * skip their update while it is non-zero, so a step whose gradient may be
+ * incomplete leaves the parameters and moments unchanged. No counterpart in
+ * the reference (which has no device-side waits). */
 GS_API int gs_check_status(void *stream);
 GS_API int gs_sync(void *stream);
+
+/* The status word copied to dst (one uint32, device memory) on `stream`,
+ * not cleared; and the reverse merge: when *src is non-zero (e.g. the
+ * maximum of every rank's exported word, reduced over NCCL), the local word
+ * becomes GS_ERR_PEER unless it already holds a code. Data-parallel steps
+ * that use an NCCL all-reduce merge every rank's status before the
+ * optimizer, so that all ranks skip (or apply) the update together. No
+ * counterpart in the reference. */
+GS_API int gs_status_export(uint32_t *dst, void *stream);
+GS_API int gs_status_merge(const uint32_t *src, void *stream);
 
 /* Self-test of the bounded waits: launches one thread that polls the device
  * word *flag_dev (which the caller leaves 0) until the spin limit, then
  * returns the status it recorded -- GS_ERR_DEVICE_TIMEOUT -- with the CUDA
  * context intact. No counterpart in the reference (which has no waits). */
 GS_API int gs_selftest_bounded_wait(const uint32_t *flag_dev, void *stream);
+
+/* The same probe without the read-back: it leaves GS_ERR_DEVICE_TIMEOUT in
+ * the status word (as a kernel whose wait gave up would), for tests of the
+ * kernels gated on it. No counterpart in the reference. */
+GS_API int gs_selftest_set_timeout(const uint32_t *flag_dev, void *stream);
 
 /* ---- reference module functions (rasterizer.cpp:141-440) ---------------- */
 
@@ -146,6 +166,29 @@ GS_API int gs_tile_layout(int n, const float *points_img, const float *radii, co
                    const int32_t *counts, int64_t total, int width, int height,
                    int64_t *keys_sorted, int32_t *ids_sorted, int32_t *indexing_offset,
                    void *scratch, size_t scratch_bytes, void *stream);
+
+/* Scratch bytes for gs_tile_layout_views (0 on invalid arguments). totals
+ * is a HOST array of num_views pair counts. */
+GS_API size_t gs_tile_layout_views_scratch_bytes(int n, int num_views, const int64_t *totals,
+                                                 int width, int height);
+
+/* The tile layout of num_views views (1..64) of the same n Gaussians in one
+ * cooperative launch -- the reference's compute_tile_intersection
+ * (rasterizer.cpp:292-359: key emission, the CUB 64-bit sort and the tile
+ * ranges of kernel.cu:820-914,1341-1388) for every view of a training step
+ * at once, with the same per-tile order as gs_tile_layout (tile, then depth
+ * bits, ties by Gaussian id). Inputs are per view at view * n (points_img,
+ * radii as float2, depths, counts as written by
+ * gs_preprocess_forward_views); totals is a HOST array of the views' pair
+ * counts. Outputs: ids_sorted, the views' lists back to back (view v starts
+ * at totals[0] + ... + totals[v - 1]); indexing_offset, (num_views, tiles)
+ * start offsets local to each view's list. Grid-wide waits are bounded (a
+ * timeout is reported through the status word). */
+GS_API int gs_tile_layout_views(int n, int num_views, const float *points_img, const float *radii,
+                                const float *depths, const int32_t *counts, const int64_t *totals,
+                                int width, int height, int32_t *ids_sorted,
+                                int32_t *indexing_offset, void *scratch, size_t scratch_bytes,
+                                void *stream);
 
 /* Stable LSD radix sort of (uint64 key, int32 value) pairs on key bits
  * [0, end_bit). Replaces radix_sort_double_buffer (kernel.cu:1341-1388).
@@ -354,7 +397,9 @@ GS_API int gs_l1_ssim_loss_grad(int height, int width, const float *raw_image,
  * buffers 16-byte aligned. grad_shard_out (n / world floats, or NULL)
  * receives this rank's shard of the summed gradient. Waits for other ranks
  * are bounded (4 s); a rank that never arrives makes gs_check_status report
- * GS_ERR_DEVICE_TIMEOUT. */
+ * GS_ERR_DEVICE_TIMEOUT. Each rank publishes whether its status word holds
+ * an error when it arrives; if any does, every rank skips the update (a rank
+ * without an error of its own then records GS_ERR_PEER). */
 GS_API size_t gs_dp_flag_words(int num_blocks);
 GS_API int gs_dp_max_blocks(void);
 GS_API int gs_dp_adam_step(int world, int rank, void *const *grad_ptrs, void *const *param_ptrs,
