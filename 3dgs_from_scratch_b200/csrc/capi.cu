@@ -1,5 +1,6 @@
 // capi.cu -- status plumbing, launch accounting and small C-ABI utilities.
 #include <atomic>
+#include <mutex>
 
 #include "gs_common.cuh"
 
@@ -10,7 +11,6 @@ __device__ uint32_t g_status_word;
 
 static std::atomic<uint64_t> g_launches{0};
 static std::atomic<int> g_last_cuda_error{0};
-static uint32_t *g_status_ptr[64] = {nullptr};
 
 void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
@@ -22,16 +22,57 @@ int cuda_status(cudaError_t e) {
 
 int launch_status() { return cuda_status(cudaGetLastError()); }
 
-uint32_t *device_status_word() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
-  if (g_status_ptr[dev] == nullptr) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
-    g_status_ptr[dev] = reinterpret_cast<uint32_t *>(p);
+// The current CUDA context's process-unique id (cuCtxGetId), 0 when there is
+// no current context yet. Driver entry points are resolved once through the
+// runtime, so the library needs no link against libcuda.
+typedef int (*CtxGetCurrentFn)(void **);
+typedef int (*CtxGetIdFn)(void *, unsigned long long *);
+static CtxGetCurrentFn g_ctx_get_current = nullptr;
+static CtxGetIdFn g_ctx_get_id = nullptr;
+static std::once_flag g_ctx_once;
+
+static void resolve_context_api() {
+  void *f = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess && q == cudaDriverEntryPointSuccess)
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+  f = nullptr;
+  if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess && q == cudaDriverEntryPointSuccess)
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f);
+}
+
+unsigned long long current_context_id() {
+  std::call_once(g_ctx_once, resolve_context_api);
+  void *ctx = nullptr;
+  if (g_ctx_get_current == nullptr || g_ctx_get_current(&ctx) != 0 || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_get_id == nullptr || g_ctx_get_id(ctx, &id) != 0) return 0;
+  return id;
+}
+
+int symbol_address(const void *symbol, SymbolCache *cache, void **out) {
+  const unsigned long long ctx = current_context_id();
+  if (ctx != 0 && cache->context_id == ctx) {
+    *out = cache->address;
+    return GS_OK;
   }
-  return g_status_ptr[dev];
+  void *p = nullptr;
+  int rc = cuda_status(cudaGetSymbolAddress(&p, symbol));
+  if (rc) return rc;
+  // The lookup made the context current if it was not yet; cache against it.
+  cache->context_id = ctx != 0 ? ctx : current_context_id();
+  cache->address = p;
+  *out = p;
+  return GS_OK;
+}
+
+uint32_t *device_status_word() {
+  thread_local SymbolCache cache;
+  void *p = nullptr;
+  if (symbol_address(&g_status_word, &cache, &p) != GS_OK) return nullptr;
+  return reinterpret_cast<uint32_t *>(p);
 }
 
 }  // namespace gs

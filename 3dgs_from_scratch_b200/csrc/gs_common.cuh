@@ -38,6 +38,21 @@ int cuda_status(cudaError_t e);                 // maps and records a CUDA error
 int launch_status();                            // cudaGetLastError after launches
 uint32_t *device_status_word();                 // per-device status word (device ptr)
 
+// Device address of a __device__ symbol in the current context. Host code
+// cannot use the symbol itself as a pointer; the address is looked up with
+// cudaGetSymbolAddress and cached per host thread (the caller passes a
+// thread_local cache) against the context's process-unique id, so a context
+// torn down and re-created (cudaDeviceReset) or a switch of device gets a
+// fresh lookup.
+struct SymbolCache {
+  unsigned long long context_id = 0;
+  void *address = nullptr;
+};
+int symbol_address(const void *symbol, SymbolCache *cache, void **out);
+// Process-unique id of the current CUDA context (0 when none is current yet);
+// per-context set-up (function attributes, constant uploads) is keyed on it.
+unsigned long long current_context_id();
+
 // Bounded spin limit for look-back waits. A predecessor that is resident
 // publishes within microseconds; this bound (~ tens of ms) only ends a wait
 // that can never finish, which then records GS_ERR_DEVICE_TIMEOUT.

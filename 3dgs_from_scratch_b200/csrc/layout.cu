@@ -534,10 +534,14 @@ struct LayoutPlan {
 
 template <typename KT>
 int layout_grid(size_t smem) {
-  static int cached[64] = {0};
+  // the shared-memory opt-in is per context: redone (with the occupancy
+  // query) once per host thread and context
+  thread_local unsigned long long cached_ctx = 0;
+  thread_local int cached = 0;
+  const unsigned long long ctx = current_context_id();
+  if (ctx != 0 && cached_ctx == ctx && cached) return cached;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
   if (cudaFuncSetAttribute(layout::layout_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
     return 0;
@@ -547,7 +551,8 @@ int layout_grid(size_t smem) {
     return 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
   int g = sms * (per_sm < 3 ? per_sm : 3);
-  if (dev >= 0 && dev < 64) cached[dev] = g;
+  cached = g;
+  cached_ctx = ctx;
   return g;
 }
 

@@ -320,16 +320,15 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
   }
 }
 
-static int g_win_ready[64] = {0};
-
 // The normalised window exp(-(i - 5)^2 / (2 * 1.5^2)) / sum, computed in
-// double and rounded to fp32, uploaded once per device.
+// double and rounded to fp32, uploaded once per host thread and context (a
+// synchronous copy: the first call on a thread must not be inside a stream
+// capture).
 static int ensure_window() {
-  int dev = 0;
-  int rc = cuda_status(cudaGetDevice(&dev));
-  if (rc) return rc;
-  if (dev < 0 || dev >= 64) return GS_ERR_INVALID_ARGUMENT;
-  if (g_win_ready[dev]) return GS_OK;
+  thread_local unsigned long long ready_ctx = 0;
+  const unsigned long long ctx = current_context_id();
+  if (ctx != 0 && ready_ctx == ctx) return GS_OK;
+  int rc;
   double w[kSsimWin], sum = 0.0;
   for (int i = 0; i < kSsimWin; ++i) {
     const double d = (double)(i - kSsimR);
@@ -340,7 +339,7 @@ static int ensure_window() {
   for (int i = 0; i < kSsimWin; ++i) wf[i] = (float)(w[i] / sum);
   rc = cuda_status(cudaMemcpyToSymbol(c_ssim_win, wf, sizeof(wf)));
   if (rc) return rc;
-  g_win_ready[dev] = 1;
+  ready_ctx = ctx != 0 ? ctx : current_context_id();
   return GS_OK;
 }
 

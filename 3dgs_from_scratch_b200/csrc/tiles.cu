@@ -154,7 +154,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
     }
     if (lane == 0) {
       s_prefix = prefix;
-      if (tile == num_tiles - 1) *total = (int64_t)(prefix + agg);
+      if (tile == num_tiles - 1) {
+        *total = (int64_t)(prefix + agg);
+        // the int32 offsets wrapped: the total (int64) stays exact, the
+        // offsets past INT32_MAX do not
+        if (prefix + agg > (uint64_t)INT32_MAX) atomicCAS(status, 0u, (uint32_t)GS_ERR_CAPACITY);
+      }
     }
   }
   __syncthreads();
@@ -601,14 +606,16 @@ static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *v
     sort_histogram_kernel<KT><<<hblocks, 256, 0, st>>>(keys, n, passes, end_bit, hist);
     count_launch();
   }
-  static int attr_done[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
+  // the dynamic shared-memory opt-in is per context: set once per host
+  // thread and context
+  thread_local unsigned long long attr_ctx = 0;
   const size_t smem = sizeof(SortSmem<KT, ITEMS>);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(onesweep_pass_kernel<KT, ITEMS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_done[dev] = 1;
+  const unsigned long long ctx = current_context_id();
+  if (ctx == 0 || attr_ctx != ctx) {
+    rc = cuda_status(cudaFuncSetAttribute(onesweep_pass_kernel<KT, ITEMS>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (rc) return rc;
+    attr_ctx = ctx;
   }
   KT *kin = keys, *kout = keys_alt;
   int32_t *vin = vals, *vout = vals_alt;
@@ -837,22 +844,15 @@ constexpr int kNoAllocScanMaxN = 1 << 24;  // 16,777,216 counts
 constexpr int kNoAllocScanWords = (kNoAllocScanMaxN + kScanTile - 1) / kScanTile + 1;
 static __device__ __align__(256) uint64_t g_noalloc_scan_words[kNoAllocScanWords];
 
-static uint64_t *g_noalloc_scan_ptr[64] = {nullptr};
-
-// Device address of g_noalloc_scan_words for the current device, looked up
-// once per device (host code may not use the symbol itself as a pointer).
+// Device address of g_noalloc_scan_words in the current context (host code
+// may not use the symbol itself as a pointer): cudaGetSymbolAddress, cached
+// per host thread against the context's id.
 static int noalloc_scan_words(uint64_t **out) {
-  int dev = 0;
-  int rc = cuda_status(cudaGetDevice(&dev));
+  thread_local SymbolCache cache;
+  void *p = nullptr;
+  int rc = symbol_address(&g_noalloc_scan_words, &cache, &p);
   if (rc) return rc;
-  if (dev < 0 || dev >= 64) return GS_ERR_INVALID_ARGUMENT;
-  if (g_noalloc_scan_ptr[dev] == nullptr) {
-    void *p = nullptr;
-    rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scan_words));
-    if (rc) return rc;
-    g_noalloc_scan_ptr[dev] = reinterpret_cast<uint64_t *>(p);
-  }
-  *out = g_noalloc_scan_ptr[dev];
+  *out = reinterpret_cast<uint64_t *>(p);
   return GS_OK;
 }
 

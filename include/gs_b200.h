@@ -126,22 +126,28 @@ GS_API int gs_count_tiles(int n, const float *points_img, const float *radii, co
                    int width, int height, int32_t *counts, void *stream);
 
 /* Exclusive scan of n int32 counts into `offsets`, total into *total_dev
- * (device int64). Scratch: gs_scan_scratch_bytes(n). */
+ * (device int64). Scratch: gs_scan_scratch_bytes(n). The offsets are int32:
+ * once the running total passes INT32_MAX they wrap, *total_dev stays exact,
+ * and the kernel records GS_ERR_CAPACITY in the device status word
+ * (gs_check_status), so callers with large totals check either. */
 GS_API size_t gs_scan_scratch_bytes(int n);
 GS_API int gs_exclusive_scan(int n, const int32_t *counts, int32_t *offsets, int64_t *total_dev,
                       void *scratch, size_t scratch_bytes, void *stream);
 
-/* Same exclusive scan as gs_exclusive_scan, for callers that pass their
- * input and output buffers but may not allocate device memory (e.g. a host
- * application that owns all GPU memory through its own allocator, or a frame
- * loop that must not call cudaMalloc/cudaFree, which synchronise the device).
- * It allocates nothing: the look-back state lives in a fixed 64 KiB device
- * array inside the library, so n is limited to 16,777,216 (larger n returns
- * GS_ERR_CAPACITY). The first call on a device looks up that array's address
- * (cudaGetSymbolAddress) and should come before any stream capture. All calls
- * share the one array: calls whose kernels overlap on the GPU race, so issue
- * them on one stream or otherwise serialise them. No counterpart in the
- * reference, which allocates its scan output with torch (rasterizer.cpp:319). */
+/* Same exclusive scan as gs_exclusive_scan (int32 offsets that wrap past
+ * INT32_MAX with GS_ERR_CAPACITY in the status word, exact int64 total), for
+ * callers that pass their input and output buffers but may not allocate
+ * device memory (e.g. a host application that owns all GPU memory through its
+ * own allocator, or a frame loop that must not call cudaMalloc/cudaFree,
+ * which synchronise the device). It allocates nothing: the look-back state
+ * lives in a fixed device array inside the library of 8,193 64-bit words
+ * (65,544 bytes: 2^24 / 2048 tile words plus one ticket word), so n is
+ * limited to 16,777,216 (larger n returns GS_ERR_CAPACITY). The array's
+ * address is looked up (cudaGetSymbolAddress) on a host thread's first call
+ * in a context, so that first call should come before any stream capture.
+ * All calls share the one array: calls whose kernels overlap on the GPU race,
+ * so issue them on one stream or otherwise serialise them. This entry point
+ * has no counterpart in the reference. */
 GS_API int gs_exclusive_scan_noalloc(int n, const int32_t *counts, int32_t *offsets,
                                      int64_t *total_dev, void *stream);
 

@@ -55,6 +55,29 @@ def test_noalloc_scan_matches_allocating_scan_twice():
         assert torch.equal(out.long(), expect)
 
 
+def test_noalloc_scan_allocates_nothing_and_launches_once():
+    """The property the entry point exists for: after a warm-up call, a call
+    leaves the device's free memory unchanged and adds exactly one kernel
+    launch (the scan; the clearing of the array is a memset)."""
+    nat = importlib.import_module("3dgs_from_scratch_b200._native")
+    n = 2_000_003
+    counts = torch.ones(n, dtype=torch.int32, device=DEV)
+    out = torch.empty(n, dtype=torch.int32, device=DEV)
+    total = torch.zeros(1, dtype=torch.int64, device=DEV)
+    args = (n, counts.data_ptr(), out.data_ptr(), total.data_ptr(), nat.stream_ptr())
+    assert nat.query("gs_exclusive_scan_noalloc", *args) == 0  # warm-up (symbol lookup)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    launches0 = nat.launch_count()
+    assert nat.query("gs_exclusive_scan_noalloc", *args) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert nat.launch_count() - launches0 == 1
+    assert free1 == free0
+    assert int(total.item()) == n
+    assert int(out[-1].item()) == n - 1
+
+
 def test_noalloc_scan_limits():
     nat = importlib.import_module("3dgs_from_scratch_b200._native")
     total = torch.full((1,), 7, dtype=torch.int64, device=DEV)
