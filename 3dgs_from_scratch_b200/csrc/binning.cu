@@ -1,0 +1,437 @@
+// binning.cu -- the tile layout by binning: per-tile buckets, then a sort of
+// each bucket on its own.
+//
+// The reference orders the (tile, Gaussian) pairs with one stable sort of 64-bit
+// keys (tile << 32 | depth bits) over every pair of the view
+// (ruguangyou/3dgs_from_scratch src/cuda/kernel.cu:820-873 key emission and
+// the CUB sort of kernel.cu:1341-1388), then finds the tile ranges
+// (kernel.cu:875-914). Within a tile that order is: depth bits ascending, ties
+// by Gaussian id (the emission order, kept by the stable sort) -- i.e. the
+// order of the unique 64-bit key (depth bits << 32 | id). This file gets the
+// same lists without any sort over all pairs:
+//   1. bin_count_kernel: every Gaussian adds one to the counter of each tile
+//      its rectangle covers (a Gaussian per thread; rectangles of more than
+//      kSmallRect tiles by the whole warp);
+//   2. bin_scan_kernel (one block): exclusive scan of the tile counters --
+//      the per-tile start offsets (indexing_offset), the total, and the
+//      capacity check (beyond the capacity every list is left empty and
+//      GS_ERR_CAPACITY recorded);
+//   3. bin_scatter_kernel: every Gaussian takes a slot in each of its tiles'
+//      buckets with an atomic cursor and writes its id there (the bucket is
+//      then complete but in arbitrary order);
+//   4. bin_sort_kernel: one block per tile sorts its bucket by the key
+//      (depth bits << 32 | id), built from the view's depths: buckets of up
+//      to kChunk entries in registers and shared memory (a sorting network on
+//      each thread's 8 keys, then merge-path merges of sorted runs); larger
+//      buckets as sorted chunks merged run by run through global scratch.
+// Every key is unique, so any correct sort yields the reference's order bit
+// for bit. No host synchronisation: the pair count stays on the device.
+#include "gs_common.cuh"
+
+namespace gs {
+namespace binning {
+
+constexpr int kThreads = 256;
+constexpr int kItems = 8;
+constexpr int kChunk = kThreads * kItems;  // 2048 keys sorted on chip
+constexpr int kSmallRect = 8;
+constexpr uint64_t kPad = ~0ull;  // sorts after every real key
+
+struct Ctl {
+  int32_t overflow;  // set by the scan when the total exceeds the capacity
+  int32_t pad;
+};
+
+// The tiles of one Gaussian's rectangle, row-major, q-th of them.
+__device__ __forceinline__ int rect_tile(const TileRect &r, int q, int tx) {
+  const int w = r.x1 - r.x0 + 1;
+  const int row = q / w, col = q - row * w;
+  return (r.y0 + row) * tx + r.x0 + col;
+}
+
+// Visits every (Gaussian, tile) pair of [0, n): small rectangles by their
+// own thread, larger ones by the whole warp (lane q takes the rectangle's
+// q-th, q+32-th, ... tile). f(tile, gaussian). Called by whole warps.
+template <typename F>
+__device__ __forceinline__ void for_each_pair(int n, const float2 *__restrict__ points,
+                                              const float2 *__restrict__ radii,
+                                              const int32_t *__restrict__ counts, int width,
+                                              int height, F f) {
+  const int lane = threadIdx.x & 31;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int tx = tiles_x_of(width);
+  TileRect r{0, -1, 0, -1, true};
+  int area = 0;
+  if (i < n && counts[i] > 0) {
+    const float2 p = points[i], rd = radii[i];
+    r = tile_rect(p.x, p.y, rd.x, rd.y, width, height);
+    if (!r.empty) area = (r.x1 - r.x0 + 1) * (r.y1 - r.y0 + 1);
+  }
+  const bool big = area > kSmallRect;
+  if (area > 0 && !big)
+    for (int q = 0; q < area; ++q) f(rect_tile(r, q, tx), i);
+  uint32_t todo = __ballot_sync(0xffffffffu, big);
+  while (todo) {
+    const int j = __ffs(todo) - 1;
+    todo &= todo - 1;
+    TileRect rj;
+    rj.x0 = __shfl_sync(0xffffffffu, r.x0, j);
+    rj.x1 = __shfl_sync(0xffffffffu, r.x1, j);
+    rj.y0 = __shfl_sync(0xffffffffu, r.y0, j);
+    rj.y1 = __shfl_sync(0xffffffffu, r.y1, j);
+    const int aj = __shfl_sync(0xffffffffu, area, j);
+    const int gj = blockIdx.x * blockDim.x + (threadIdx.x & ~31) + j;
+    for (int q = lane; q < aj; q += 32) f(rect_tile(rj, q, tx), gj);
+  }
+}
+
+__global__ void __launch_bounds__(256) bin_count_kernel(int n, const float2 *__restrict__ points,
+                                                        const float2 *__restrict__ radii,
+                                                        const int32_t *__restrict__ counts,
+                                                        int width, int height,
+                                                        uint32_t *__restrict__ tile_count) {
+  for_each_pair(n, points, radii, counts, width, height,
+                [&](int tile, int) { atomicAdd(tile_count + tile, 1u); });
+}
+
+// One block of 1024 threads: exclusive scan of the T tile counters into
+// offsets[0..T-1], offsets[T] = total, cursor = offsets; *total_dev = total.
+// A total beyond `capacity` leaves offsets (and the cursors) zero, raises
+// ctl->overflow and records GS_ERR_CAPACITY.
+constexpr int kScanThreads = 1024;
+constexpr int kScanPer = 4;
+
+__device__ __forceinline__ long long block_excl_scan_ll(long long x, long long *s_warp,
+                                                        long long &block_total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  long long incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const long long w = s_warp[lane];
+    long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    s_warp[lane] = wi - w;
+    if (lane == 31) s_warp[32] = wi;
+  }
+  __syncthreads();
+  const long long r = incl - x + s_warp[warp];
+  block_total = s_warp[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kScanThreads) bin_scan_kernel(
+    const uint32_t *__restrict__ tile_count, int T, int64_t capacity,
+    int32_t *__restrict__ offsets, uint32_t *__restrict__ cursor, int64_t *__restrict__ total_dev,
+    Ctl *ctl, uint32_t *status) {
+  __shared__ long long s_warp[33];
+  const int t = threadIdx.x;
+  // pass 1: the total
+  long long sum = 0;
+  for (int k = t; k < T; k += kScanThreads) sum += tile_count[k];
+  long long total = 0;
+  block_excl_scan_ll(sum, s_warp, total);
+  const bool over = total > capacity;
+  if (t == 0) {
+    *total_dev = total;
+    ctl->overflow = over ? 1 : 0;
+    if (over) atomicCAS(status, 0u, (uint32_t)GS_ERR_CAPACITY);
+  }
+  if (over) {  // block-uniform
+    for (int k = t; k <= T; k += kScanThreads) offsets[k] = 0;
+    return;
+  }
+  // pass 2: the offsets, kScanPer consecutive counters per thread per round
+  long long carry = 0;
+  for (int base = 0; base < T; base += kScanThreads * kScanPer) {
+    const int k0 = base + t * kScanPer;
+    uint32_t v[kScanPer];
+    long long s = 0;
+#pragma unroll
+    for (int q = 0; q < kScanPer; ++q) {
+      v[q] = (k0 + q < T) ? tile_count[k0 + q] : 0u;
+      s += v[q];
+    }
+    long long round_total = 0;
+    long long run = carry + block_excl_scan_ll(s, s_warp, round_total);
+#pragma unroll
+    for (int q = 0; q < kScanPer; ++q) {
+      if (k0 + q < T) {
+        offsets[k0 + q] = (int32_t)run;
+        cursor[k0 + q] = (uint32_t)run;
+      }
+      run += v[q];
+    }
+    carry += round_total;
+  }
+  if (t == 0) offsets[T] = (int32_t)total;
+}
+
+__global__ void __launch_bounds__(256) bin_scatter_kernel(int n, const float2 *__restrict__ points,
+                                                          const float2 *__restrict__ radii,
+                                                          const int32_t *__restrict__ counts,
+                                                          int width, int height, int64_t capacity,
+                                                          uint32_t *__restrict__ cursor,
+                                                          int32_t *__restrict__ ids,
+                                                          const Ctl *ctl) {
+  if (ctl->overflow) return;  // grid-uniform
+  for_each_pair(n, points, radii, counts, width, height, [&](int tile, int g) {
+    const uint32_t pos = atomicAdd(cursor + tile, 1u);
+    if ((int64_t)pos < capacity) ids[pos] = g;  // always true unless the inputs changed
+  });
+}
+
+// ---- per-tile sort ---------------------------------------------------------
+
+__device__ __forceinline__ void cswap(uint64_t &a, uint64_t &b) {
+  const uint64_t lo = a < b ? a : b, hi = a < b ? b : a;
+  a = lo;
+  b = hi;
+}
+
+// Batcher's odd-even merge sort network for 8 keys (19 comparators).
+__device__ __forceinline__ void sort8(uint64_t k[8]) {
+  cswap(k[0], k[1]); cswap(k[2], k[3]); cswap(k[4], k[5]); cswap(k[6], k[7]);
+  cswap(k[0], k[2]); cswap(k[1], k[3]); cswap(k[4], k[6]); cswap(k[5], k[7]);
+  cswap(k[1], k[2]); cswap(k[5], k[6]);
+  cswap(k[0], k[4]); cswap(k[1], k[5]); cswap(k[2], k[6]); cswap(k[3], k[7]);
+  cswap(k[2], k[4]); cswap(k[3], k[5]);
+  cswap(k[1], k[2]); cswap(k[3], k[4]); cswap(k[5], k[6]);
+}
+
+// Merge path: the number of elements taken from A (sorted, length la) among
+// the first `diag` outputs of merge(A, B) (B sorted, length lb), ties to A.
+template <typename LoadA, typename LoadB>
+__device__ __forceinline__ int merge_path(LoadA a, int la, LoadB b, int lb, int diag) {
+  int lo = diag > lb ? diag - lb : 0;
+  int hi = diag < la ? diag : la;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (a(mid) <= b(diag - 1 - mid))
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// kItems outputs of merge(A, B) starting at (ai, bi).
+template <typename LoadA, typename LoadB>
+__device__ __forceinline__ void merge_items(LoadA a, int la, LoadB b, int lb, int ai, int bi,
+                                            uint64_t out[kItems]) {
+  uint64_t ka = ai < la ? a(ai) : kPad, kb = bi < lb ? b(bi) : kPad;
+#pragma unroll
+  for (int q = 0; q < kItems; ++q) {
+    const bool takeA = (bi >= lb) || (ai < la && ka <= kb);
+    out[q] = takeA ? ka : kb;
+    if (takeA) {
+      ++ai;
+      ka = ai < la ? a(ai) : kPad;
+    } else {
+      ++bi;
+      kb = bi < lb ? b(bi) : kPad;
+    }
+  }
+}
+
+// Sorts the block's kChunk keys (kItems per thread, thread t holding
+// positions t*kItems..) up to runs of `span` (a power of two >= kItems,
+// <= kChunk): on return thread t holds positions t*kItems.. of the sorted
+// chunk. s_keys: kChunk keys of shared memory. Two barriers per merge level.
+__device__ __forceinline__ void block_sort(uint64_t k[kItems], int span, uint64_t *s_keys) {
+  sort8(k);
+  const int t = threadIdx.x;
+  for (int run = kItems; run < span; run <<= 1) {
+#pragma unroll
+    for (int q = 0; q < kItems; ++q) s_keys[t * kItems + q] = k[q];
+    __syncthreads();
+    const int pair = 2 * run;
+    const int start = (t * kItems) / pair * pair;
+    const int diag = t * kItems - start;
+    const uint64_t *A = s_keys + start, *B = s_keys + start + run;
+    auto la = [&](int i) { return A[i]; };
+    auto lb = [&](int i) { return B[i]; };
+    const int ai = merge_path(la, run, lb, run, diag);
+    merge_items(la, run, lb, run, ai, diag - ai, k);
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ uint64_t key_of(int id, const float *__restrict__ depths, int n) {
+  const uint32_t d = (id >= 0 && id < n) ? __float_as_uint(depths[id]) : 0xffffffffu;
+  return ((uint64_t)d << 32) | (uint32_t)id;
+}
+
+__device__ __forceinline__ int next_pow2(int x) {
+  int p = kItems;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// One block per tile: sorts the tile's bucket ids[off[t] .. off[t+1]) in
+// place by (depth bits, id). Buckets above kChunk: sorted chunks written to
+// keys_a, merged run by run between keys_a and keys_b (global scratch at the
+// bucket's own offsets), the ids taken from the last run.
+__global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__restrict__ offsets,
+                                                            const float *__restrict__ depths,
+                                                            int n, int32_t *__restrict__ ids,
+                                                            uint64_t *__restrict__ keys_a,
+                                                            uint64_t *__restrict__ keys_b) {
+  __shared__ uint64_t s_keys[kChunk];
+  const int tile = blockIdx.x;
+  const int beg = offsets[tile], L = offsets[tile + 1] - beg;
+  if (L <= 1) return;  // block-uniform
+  const int t = threadIdx.x;
+  uint64_t k[kItems];
+  if (L <= kChunk) {
+    const int span = next_pow2(L);
+    // A warp whose positions are all padding only takes part in the barriers
+    // (two per merge level). The test is per warp, so that every barrier is
+    // reached by whole warps; threads of an active warp past `span` merge
+    // padding (or stale shared memory), and their results are dropped.
+    if ((t & ~31) * kItems >= span) {
+      for (int run = kItems; run < span; run <<= 1) {
+        __syncthreads();
+        __syncthreads();
+      }
+      return;
+    }
+#pragma unroll
+    for (int q = 0; q < kItems; ++q) {
+      const int p = t * kItems + q;
+      k[q] = p < L ? key_of(ids[beg + p], depths, n) : kPad;
+    }
+    block_sort(k, span, s_keys);
+#pragma unroll
+    for (int q = 0; q < kItems; ++q) {
+      const int p = t * kItems + q;
+      if (p < L) ids[beg + p] = (int32_t)(uint32_t)k[q];
+    }
+    return;
+  }
+  // large bucket: sorted chunks of kChunk into keys_a
+  uint64_t *ka = keys_a + beg, *kb = keys_b + beg;
+  for (int c0 = 0; c0 < L; c0 += kChunk) {
+#pragma unroll
+    for (int q = 0; q < kItems; ++q) {
+      const int p = c0 + t * kItems + q;
+      k[q] = p < L ? key_of(ids[beg + p], depths, n) : kPad;
+    }
+    block_sort(k, kChunk, s_keys);
+#pragma unroll
+    for (int q = 0; q < kItems; ++q) {
+      const int p = c0 + t * kItems + q;
+      if (p < L) ka[p] = k[q];
+    }
+  }
+  __syncthreads();
+  // merge runs of kChunk, 2 kChunk, ... (ping-pong ka <-> kb)
+  for (int run = kChunk; run < L; run <<= 1) {
+    for (int out0 = 0; out0 < L; out0 += kChunk) {
+      const int p0 = out0 + t * kItems;  // this thread's first output position
+      if (p0 < L) {
+        const int start = p0 / (2 * run) * (2 * run);
+        const int la_n = min(run, L - start);
+        const int lb_n = max(0, min(run, L - start - run));
+        const uint64_t *A = ka + start, *B = ka + start + run;
+        auto la = [&](int i) { return A[i]; };
+        auto lb = [&](int i) { return B[i]; };
+        const int diag = p0 - start;
+        const int ai = merge_path(la, la_n, lb, lb_n, diag);
+        merge_items(la, la_n, lb, lb_n, ai, diag - ai, k);
+#pragma unroll
+        for (int q = 0; q < kItems; ++q)
+          if (p0 + q < L) kb[p0 + q] = k[q];
+      }
+    }
+    __syncthreads();  // the level's writes are visible to the block
+    uint64_t *tmp = ka;
+    ka = kb;
+    kb = tmp;
+  }
+  for (int p = t; p < L; p += kThreads) ids[beg + p] = (int32_t)(uint32_t)ka[p];
+}
+
+}  // namespace binning
+
+// Scratch of gs_tile_bins, carved in this order.
+struct BinScratch {
+  size_t ctl, count, cursor, keys_a, keys_b, total;
+};
+
+static inline size_t bin_align(size_t x) { return (x + 255) / 256 * 256; }
+
+static BinScratch bin_scratch(int64_t capacity, int num_tiles) {
+  const size_t cap = (size_t)(capacity > 0 ? capacity : 1);
+  BinScratch L;
+  L.ctl = 0;
+  L.count = bin_align(sizeof(binning::Ctl));
+  L.cursor = bin_align(L.count + 4 * (size_t)num_tiles);
+  L.keys_a = bin_align(L.cursor + 4 * (size_t)num_tiles);
+  L.keys_b = bin_align(L.keys_a + 8 * cap);
+  L.total = bin_align(L.keys_b + 8 * cap);
+  return L;
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" size_t gs_tile_bins_scratch_bytes(int n, int64_t capacity, int width, int height) {
+  if (n < 0 || capacity < 0 || width <= 0 || height <= 0) return 0;
+  return bin_scratch(capacity, tiles_x_of(width) * tiles_y_of(height)).total;
+}
+
+extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
+                            const float *depths, const int32_t *counts, int64_t capacity,
+                            int width, int height, int32_t *ids_sorted, int32_t *indexing_offset,
+                            int64_t *total_dev, void *scratch, size_t scratch_bytes,
+                            void *stream) {
+  using namespace gs::binning;
+  if (n < 0 || width <= 0 || height <= 0 || capacity < 0 || total_dev == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)total_dev & 7))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (capacity >= (1ll << 31) - 1) return GS_ERR_CAPACITY;  // int32 offsets
+  const int T = tiles_x_of(width) * tiles_y_of(height);
+  if (T > (1 << 24)) return GS_ERR_CAPACITY;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const BinScratch L = bin_scratch(capacity, T);
+  if (scratch == nullptr || scratch_bytes < L.total) return GS_ERR_CAPACITY;
+  unsigned char *p = reinterpret_cast<unsigned char *>(scratch);
+  Ctl *ctl = reinterpret_cast<Ctl *>(p + L.ctl);
+  uint32_t *tcount = reinterpret_cast<uint32_t *>(p + L.count);
+  uint32_t *cursor = reinterpret_cast<uint32_t *>(p + L.cursor);
+  int rc = cuda_status(cudaMemsetAsync(p, 0, L.keys_a, st));  // ctl and the tile counters
+  if (rc) return rc;
+  const float2 *pts = reinterpret_cast<const float2 *>(points_img);
+  const float2 *rad = reinterpret_cast<const float2 *>(radii);
+  const int gblocks = (n + 255) / 256;
+  if (n > 0) {
+    bin_count_kernel<<<gblocks, 256, 0, st>>>(n, pts, rad, counts, width, height, tcount);
+    count_launch();
+  }
+  bin_scan_kernel<<<1, kScanThreads, 0, st>>>(tcount, T, capacity, indexing_offset, cursor,
+                                              total_dev, ctl, device_status_word());
+  count_launch();
+  if (n > 0) {
+    bin_scatter_kernel<<<gblocks, 256, 0, st>>>(n, pts, rad, counts, width, height, capacity,
+                                                cursor, ids_sorted, ctl);
+    count_launch();
+    bin_sort_kernel<<<T, kThreads, 0, st>>>(indexing_offset, depths, n, ids_sorted,
+                                            reinterpret_cast<uint64_t *>(p + L.keys_a),
+                                            reinterpret_cast<uint64_t *>(p + L.keys_b));
+    count_launch();
+  }
+  return launch_status();
+}

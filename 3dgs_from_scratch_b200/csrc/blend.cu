@@ -266,7 +266,10 @@ __global__ void __launch_bounds__(kBlendThreads, GS_FWD_MINB) blend_forward_kern
   const bool in1 = (u < width) && (v1 < height);
 
   const int s = offsets[tile];
-  const int e = (tile + 1 < num_tiles) ? offsets[tile + 1] : (int)total;
+  // total < 0: the offsets hold num_tiles + 1 entries, the last one the end
+  // of the last tile's list (the capacity form of the tile layout)
+  const int e = (tile + 1 < num_tiles) ? offsets[tile + 1]
+                                       : (total >= 0 ? (int)total : offsets[num_tiles]);
 
 #if GS_FWD_F32X2
   FwdPx2 P{(float)u, make_float2((float)v0, (float)v1), make_float2(1.f, 1.f),
@@ -873,7 +876,7 @@ extern "C" int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, i
                                 float alpha_threshold, float transmittance_threshold,
                                 float chi_squared_threshold, float *image, float *final_t,
                                 int32_t *pixel_end, void *stream) {
-  if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < 0 || total >= (1ll << 31))
+  if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15)) return GS_ERR_INVALID_ARGUMENT;
   if (num_tiles == 0) return GS_OK;
@@ -894,7 +897,7 @@ extern "C" int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, 
                                  int height, float alpha_threshold,
                                  float transmittance_threshold, float chi_squared_threshold,
                                  float *grad_points_img, float *grad_splat, void *stream) {
-  if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < 0 || total >= (1ll << 31))
+  if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15) || ((uintptr_t)grad_points_img & 7) ||
       ((uintptr_t)grad_splat & 15))

@@ -48,9 +48,13 @@ struct FlatLayout {
 
 __global__ void __launch_bounds__(256) densify_accumulate_kernel(
     int n, const float2 *__restrict__ g_points, const float2 *__restrict__ radii, float half_w,
-    float half_h, float *__restrict__ grad_accum, float *__restrict__ count) {
+    float half_h, float *__restrict__ grad_accum, float *__restrict__ count,
+    const uint32_t *__restrict__ status) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  // a step whose status word holds an error (e.g. a pair count beyond the
+  // layout capacity, after which the step is repeated) adds no statistics
+  if (status && ld_volatile_u32(status) != 0u) return;
   const float2 r = radii[i];
   if (!(r.x > 0.0f && r.y > 0.0f)) return;  // strategy.py:68
   const float2 g = g_points[i];
@@ -204,7 +208,7 @@ extern "C" int gs_densify_accumulate(int n, const float *grad_points, const floa
   if (n == 0) return GS_OK;
   densify_accumulate_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(
       n, reinterpret_cast<const float2 *>(grad_points), reinterpret_cast<const float2 *>(radii),
-      (float)(width / 2.0), (float)(height / 2.0), grad_accum, count);
+      (float)(width / 2.0), (float)(height / 2.0), grad_accum, count, device_status_word());
   count_launch();
   return launch_status();
 }

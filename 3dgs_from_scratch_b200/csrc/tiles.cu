@@ -172,6 +172,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(int n, const int32_t
   }
 }
 
+// Item count of the capacity form of the layout: *count_dev when it fits the
+// capacity, else 0 (the lists are then empty and GS_ERR_CAPACITY is recorded
+// by the pair emission).
+__device__ __forceinline__ int64_t capped_count(const int64_t *count_dev, int64_t capacity) {
+  const int64_t c = *count_dev;
+  return (c >= 0 && c <= capacity) ? c : 0;
+}
+
 // ---- onesweep radix sort -----------------------------------------------------
 
 constexpr int kSortThreads = 256;
@@ -276,16 +284,22 @@ __global__ void __launch_bounds__(kSortThreads, SortItems<KT>::min_blocks) onesw
     const KT *__restrict__ keys_in, const int32_t *__restrict__ vals_in,
     KT *__restrict__ keys_out, int32_t *__restrict__ vals_out, int64_t n, int shift,
     uint32_t dmask, const uint32_t *__restrict__ hist, uint32_t *__restrict__ lookback,
-    uint32_t *__restrict__ ticket, uint32_t *status) {
+    uint32_t *__restrict__ ticket, uint32_t *status, const int64_t *__restrict__ n_dev) {
   constexpr int kTileItems = kSortThreads * ITEMS;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SortSmem<KT, ITEMS> &S = *reinterpret_cast<SortSmem<KT, ITEMS> *>(smem_raw);
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
+  // capacity form: n is the capacity the grid was sized for, *n_dev the
+  // item count (0 when it exceeds the capacity)
+  if (n_dev) n = capped_count(n_dev, n);
   if (t == 0) S.tile = (int)atomicAdd(ticket, 1u);
   for (int k = t; k < kSortWarps * 256; k += kSortThreads) (&S.whist[0][0])[k] = 0;
   __syncthreads();
   const int tile = S.tile;
+  // tiles are ticketed in order, so the tiles past the items form the tail
+  // of the ticket sequence: no tile that holds items looks back at them
+  if ((int64_t)tile * kTileItems >= n) return;
   const int64_t base = (int64_t)tile * kTileItems + (int64_t)warp * (32 * ITEMS);
 
   // Load warp-striped: item k of lane l is element base + k*32 + l.
@@ -449,7 +463,20 @@ __global__ void __launch_bounds__(256) emit_pairs_kernel(int n, const int32_t *_
                                                          int width, int height, int64_t total,
                                                          int tpasses, KT *__restrict__ keys,
                                                          int32_t *__restrict__ vals,
-                                                         uint32_t *__restrict__ hist) {
+                                                         uint32_t *__restrict__ hist,
+                                                         const int64_t *__restrict__ total_dev,
+                                                         uint32_t *status) {
+  // capacity form: `total` is the capacity of keys / vals and *total_dev the
+  // scan's pair total; beyond the capacity nothing is emitted and the
+  // status word records GS_ERR_CAPACITY
+  if (total_dev) {
+    const int64_t real = *total_dev;
+    if (real > total || real < 0) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(status, 0u, (uint32_t)GS_ERR_CAPACITY);
+      return;
+    }
+    total = real;
+  }
   __shared__ uint32_t s_hist[3 * 256];
   for (int k = threadIdx.x; k < tpasses * 256; k += blockDim.x) s_hist[k] = 0;
   __syncthreads();
@@ -505,8 +532,15 @@ __global__ void __launch_bounds__(256) emit_pairs_kernel(int n, const int32_t *_
 template <typename KT>
 __global__ void __launch_bounds__(256) ranges_kernel(const KT *__restrict__ tiles_sorted,
                                                      int64_t n, int num_tiles,
-                                                     int32_t *__restrict__ offsets) {
+                                                     int32_t *__restrict__ offsets,
+                                                     const int64_t *__restrict__ n_dev) {
   constexpr int kPer = 8;
+  // capacity form: the count from the device, and offsets[num_tiles] = the
+  // end of the last tile's list
+  if (n_dev) {
+    n = capped_count(n_dev, n);
+    if (blockIdx.x == 0 && threadIdx.x == 0) offsets[num_tiles] = (int32_t)n;
+  }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * kPer;
   for (int64_t k0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kPer; k0 < n; k0 += stride) {
     KT v[kPer];
@@ -586,7 +620,8 @@ static int sm_count() {
 template <typename KT>
 static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *vals_alt,
                     int end_bit, void *scratch, cudaStream_t st, const int32_t *vals_first = nullptr,
-                    bool identity_first = false, const uint32_t *hist_given = nullptr) {
+                    bool identity_first = false, const uint32_t *hist_given = nullptr,
+                    const int64_t *n_dev = nullptr) {
   constexpr int ITEMS = SortItems<KT>::value;
   const int passes = (end_bit + 7) / 8;
   if (n <= 0 || passes <= 0) return GS_OK;
@@ -624,7 +659,7 @@ static int run_sort(int64_t n, KT *keys, int32_t *vals, KT *keys_alt, int32_t *v
     const int32_t *vsrc = (p == 0) ? (identity_first ? nullptr : (vals_first ? vals_first : vin)) : vin;
     onesweep_pass_kernel<KT, ITEMS><<<L.tiles, kSortThreads, smem, st>>>(
         kin, vsrc, kout, vout, n, 8 * p, (1u << bits) - 1u, hist + 256 * p,
-        lookback + (size_t)p * L.tiles * 256, tickets + p, device_status_word());
+        lookback + (size_t)p * L.tiles * 256, tickets + p, device_status_word(), n_dev);
     count_launch();
     KT *tk = kin;
     kin = kout;
@@ -675,7 +710,10 @@ template <typename KT>
 static int tile_layout_impl(int n, const float2 *points, const float2 *radii, const float *depths,
                             const int32_t *counts, int64_t total, int width, int height,
                             uint64_t *keys_sorted, int32_t *ids_sorted, int32_t *indexing_offset,
-                            unsigned char *p, const LayoutScratch &L, cudaStream_t st) {
+                            unsigned char *p, const LayoutScratch &L, cudaStream_t st,
+                            bool capped = false, int64_t *total_out = nullptr) {
+  // capped: `total` is the capacity of the pair buffers; the pair count is
+  // the scan's device total, read by the kernels (no host synchronisation)
   const int num_tiles = tiles_x_of(width) * tiles_y_of(height);
   uint32_t *dk_a = reinterpret_cast<uint32_t *>(p + L.dkeys_a);
   uint32_t *dk_b = reinterpret_cast<uint32_t *>(p + L.dkeys_b);
@@ -699,8 +737,8 @@ static int tile_layout_impl(int n, const float2 *points, const float2 *radii, co
   const int stiles = (n + kScanTile - 1) / kScanTile;
   rc = cuda_status(cudaMemsetAsync(sort_scratch, 0, (size_t)(stiles + 1) * 8, st));
   if (rc) return rc;
-  scan_kernel<<<stiles, kScanThreads, 0, st>>>(n, counts, order, offs,
-                                               reinterpret_cast<int64_t *>(p + L.total8),
+  int64_t *tot_dev = total_out ? total_out : reinterpret_cast<int64_t *>(p + L.total8);
+  scan_kernel<<<stiles, kScanThreads, 0, st>>>(n, counts, order, offs, tot_dev,
                                                reinterpret_cast<uint64_t *>(sort_scratch), stiles,
                                                device_status_word());
   count_launch();
@@ -717,16 +755,19 @@ static int tile_layout_impl(int n, const float2 *points, const float2 *radii, co
   int32_t *v1 = (tpasses & 1) ? ids_sorted : tv_b;
   emit_pairs_kernel<KT><<<(n + 255) / 256, 256, 0, st>>>(n, order, counts, offs, points, radii,
                                                          width, height, total, tpasses, k0, v0,
-                                                         thist);
+                                                         thist, capped ? tot_dev : nullptr,
+                                                         device_status_word());
   count_launch();
   // 4. stable sort by tile id; the sorted ids land in (tk_a, ids_sorted)
-  rc = run_sort<KT>(total, k0, v0, k1, v1, tbits, sort_scratch, st, nullptr, false, thist);
+  rc = run_sort<KT>(total, k0, v0, k1, v1, tbits, sort_scratch, st, nullptr, false, thist,
+                    capped ? tot_dev : nullptr);
   if (rc) return rc;
   // 5. tile ranges
   {
     const int64_t want = (total + 256 * 8 - 1) / (256 * 8);
     const int grid = (int)(want < (int64_t)sm_count() * 16 ? want : (int64_t)sm_count() * 16);
-    ranges_kernel<KT><<<grid, 256, 0, st>>>(tk_a, total, num_tiles, indexing_offset);
+    ranges_kernel<KT><<<grid, 256, 0, st>>>(tk_a, total, num_tiles, indexing_offset,
+                                            capped ? tot_dev : nullptr);
     count_launch();
   }
   if (keys_sorted) {
@@ -829,6 +870,39 @@ extern "C" int gs_tile_layout(int n, const float *points_img, const float *radii
                                       ids_sorted, indexing_offset, p, L, st);
   return tile_layout_impl<uint32_t>(n, pts, rad, depths, counts, total, width, height, ks,
                                     ids_sorted, indexing_offset, p, L, st);
+}
+
+extern "C" int gs_tile_layout_capped(int n, const float *points_img, const float *radii,
+                                     const float *depths, const int32_t *counts,
+                                     int64_t capacity, int width, int height,
+                                     int32_t *ids_sorted, int32_t *indexing_offset,
+                                     int64_t *total_dev, void *scratch, size_t scratch_bytes,
+                                     void *stream) {
+  if (n < 0 || width <= 0 || height <= 0 || capacity < 0) return GS_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)points_img & 7) || ((uintptr_t)radii & 7) || ((uintptr_t)total_dev & 7))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (total_dev == nullptr) return GS_ERR_INVALID_ARGUMENT;
+  if (capacity >= (int64_t)kLbValue) return GS_ERR_CAPACITY;
+  cudaStream_t st = as_stream(stream);
+  const int num_tiles = tiles_x_of(width) * tiles_y_of(height);
+  if (num_tiles > (1 << 24)) return GS_ERR_CAPACITY;
+  // num_tiles start offsets and the end of the last list, zero until written
+  int rc = cuda_status(
+      cudaMemsetAsync(indexing_offset, 0, (size_t)(num_tiles + 1) * sizeof(int32_t), st));
+  if (rc) return rc;
+  rc = cuda_status(cudaMemsetAsync(total_dev, 0, sizeof(int64_t), st));
+  if (rc || n == 0) return rc;
+  const int64_t cap = capacity > 0 ? capacity : 1;
+  const LayoutScratch L = layout_scratch(n, cap, num_tiles);
+  if (scratch == nullptr || scratch_bytes < L.total) return GS_ERR_CAPACITY;
+  unsigned char *p = reinterpret_cast<unsigned char *>(scratch);
+  const float2 *pts = reinterpret_cast<const float2 *>(points_img);
+  const float2 *rad = reinterpret_cast<const float2 *>(radii);
+  if (num_tiles <= 65536)
+    return tile_layout_impl<uint16_t>(n, pts, rad, depths, counts, cap, width, height, nullptr,
+                                      ids_sorted, indexing_offset, p, L, st, true, total_dev);
+  return tile_layout_impl<uint32_t>(n, pts, rad, depths, counts, cap, width, height, nullptr,
+                                    ids_sorted, indexing_offset, p, L, st, true, total_dev);
 }
 
 // ---- exclusive scan without caller-provided scratch -----------------------

@@ -49,7 +49,7 @@ class NativeTrainer:
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 streams: int = 2, layout: str = "per_view", **render_opts):
+                 streams: int = 2, layout: str = "capped", **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -73,9 +73,18 @@ class NativeTrainer:
         # "batched": every view's tile layout in one cooperative launch
         # (gs_tile_layout_views); "per_view": one gs_tile_layout per view on
         # the view's stream
-        if layout not in ("batched", "per_view"):
-            raise ValueError("layout must be 'batched' or 'per_view'")
+        # "binned": per-view layouts by per-tile binning (gs_tile_bins);
+        # "capped": per-view layouts by the two radix sorts
+        # (gs_tile_layout_capped). Both write into buffers of a fixed
+        # capacity and keep the pair counts on the device (no host
+        # synchronisation in a step; a count beyond the capacity fails the
+        # step, which step() repeats with grown buffers).
+        if layout not in ("binned", "capped", "batched", "per_view"):
+            raise ValueError("layout must be 'binned', 'capped', 'batched' or 'per_view'")
         self.layout = layout
+        self._capacity_form = layout in ("binned", "capped")
+        self._capacity_entry = "gs_tile_bins" if layout == "binned" else "gs_tile_layout_capped"
+        self._cap = None  # (capacity, (views, n), buffers) of the capacity form
         self.tx = (self.width + 15) // 16
         self.ty = (self.height + 15) // 16
 
@@ -145,36 +154,97 @@ class NativeTrainer:
             s = {k: t[v] for k, t in batch.items()}
             s.update(w2c=w2c[v], K=Ks[v], campos=campos[v])
             views.append(s)
-        self._batch = dict(batch, w2c=w2c, K=Ks, campos=campos)
-        # one host synchronisation for every view's pair count
-        host_totals = totals.cpu()
-        rc = nat.query("gs_check_status", st)
-        if rc:
-            raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
-        self.last_totals = [int(x) for x in host_totals]
-        if self.layout == "batched":
-            self._layout_views(views, self.last_totals)
+        self._batch = dict(batch, w2c=w2c, K=Ks, campos=campos, totals=totals)
+        T = self.tx * self.ty
+        capped = self._capacity_form and self._cap is not None and self._cap[1] == (V, n)
+        if not capped:
+            # one host synchronisation for every view's pair count
+            host_totals = totals.cpu()
+            rc = nat.query("gs_check_status", st)
+            if rc:
+                raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+            self.last_totals = [int(x) for x in host_totals]
+            if self._capacity_form:
+                self._grow_capacity(V, self.last_totals)
+                capped = True
+            elif self.layout == "batched":
+                self._layout_views(views, self.last_totals)
         self._fork()
         for v, s in enumerate(views):
-            total = int(host_totals[v])
-            s["total"] = total
             s["stream"] = self._view_stream(v)
             with torch.cuda.stream(s["stream"]):
                 vst = nat.stream_ptr(dev)
-                if self.layout != "batched":
-                    s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
-                        s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
+                if capped:
+                    # capacity form: the pair count stays on the device (no
+                    # host synchronisation); the lists' end is offsets[T]
+                    k = v % self.num_streams
+                    cap, _, bufs = self._cap
+                    s["ids"], s["offsets"] = bufs["ids"][v], bufs["offsets"][v]
+                    s["total_dev"] = bufs["totals"][v:v + 1]
+                    scratch = bufs["scratch"][k]
+                    nat.call(self._capacity_entry, n, s["points"].data_ptr(),
+                             s["radii"].data_ptr(), s["depths"].data_ptr(),
+                             s["counts"].data_ptr(), cap, W, H, s["ids"].data_ptr(),
+                             s["offsets"].data_ptr(), s["total_dev"].data_ptr(),
+                             scratch.data_ptr(), scratch.numel(), vst)
+                    s["total"] = -1
+                else:
+                    total = self.last_totals[v]
+                    s["total"] = total
+                    if self.layout != "batched":
+                        s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
+                            s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
                 s["image"] = torch.empty((H, W, 3), **f)
                 s["final_t"] = torch.empty((H * W,), **f)
                 s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
-                nat.call("gs_blend_forward", s["offsets"].shape[0], s["offsets"].data_ptr(),
-                         total, s["ids"].data_ptr(), n, s["points"].data_ptr(),
-                         s["splat"].data_ptr(), W, H, o["alpha_threshold"],
-                         o["transmittance_threshold"], o["chi_squared_threshold"],
-                         s["image"].data_ptr(), s["final_t"].data_ptr(), s["pixel_end"].data_ptr(),
-                         vst)
+                nat.call("gs_blend_forward", T, s["offsets"].data_ptr(), s["total"],
+                         s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(),
+                         W, H, o["alpha_threshold"], o["transmittance_threshold"],
+                         o["chi_squared_threshold"], s["image"].data_ptr(),
+                         s["final_t"].data_ptr(), s["pixel_end"].data_ptr(), vst)
         self._join()
         return views
+
+    def render_views(self, world_to_cameras, intrinsics):
+        """Forward-only rendering (inference): forward_views followed by one
+        read of the status word; a view whose pair count exceeded the layout
+        capacity is rendered again with grown buffers, any other error is
+        raised. Returns the per-view state list (state["image"] is the raw
+        blended image)."""
+        for _ in range(3):
+            views = self.forward_views(world_to_cameras, intrinsics)
+            rc = nat.query("gs_check_status", nat.stream_ptr(self.device))
+            if rc == nat.GS_OK:
+                return views
+            if rc != nat.GS_ERR_CAPACITY or not self._capacity_form:
+                raise nat.NativeError("gs_check_status", rc, nat.lib().gs_last_cuda_error())
+            self.last_totals = [int(x) for x in self._batch["totals"].cpu()]
+            self._grow_capacity(len(views), self.last_totals)
+        raise nat.NativeError("gs_check_status", nat.GS_ERR_CAPACITY)
+
+    def _grow_capacity(self, V, totals):
+        """Pair buffers of the capacity form for V views of the current n:
+        every view's list capacity is the largest pair count seen, plus
+        headroom for the counts to drift between steps (25% + 64 Ki pairs,
+        rounded up to 64 Ki). Buffers are kept across steps and rebuilt only
+        when V, n or the needed capacity change."""
+        dev = self.device
+        n, T = self.n, self.tx * self.ty
+        need = max(list(totals) + [0])
+        cap = (int(need * 1.25) + 2 * 65536) // 65536 * 65536
+        old = self._cap
+        if old is not None and old[1] == (V, n) and old[0] >= need:
+            return
+        query = ("gs_tile_bins_scratch_bytes" if self.layout == "binned"
+                 else "gs_tile_layout_scratch_bytes")
+        nbytes = int(nat.query(query, n, cap, self.width, self.height))
+        bufs = dict(
+            ids=[torch.empty((cap,), device=dev, dtype=torch.int32) for _ in range(V)],
+            offsets=[torch.empty((T + 1,), device=dev, dtype=torch.int32) for _ in range(V)],
+            totals=torch.zeros((V,), device=dev, dtype=torch.int64),
+            scratch=[torch.empty((max(nbytes, 1),), device=dev, dtype=torch.uint8)
+                     for _ in range(self.num_streams)])
+        self._cap = (cap, (V, n), bufs)
 
     def _layout_views(self, views, totals):
         """Every view's tile layout in one launch on the current stream: the
@@ -295,7 +365,7 @@ class NativeTrainer:
             nat.call("gs_l1_loss_grad", H * W * 3, s["image"].data_ptr(), tgt.data_ptr(),
                      int(tgt.dtype == torch.uint8), grad_img.data_ptr(), loss_slot.data_ptr(),
                      st)
-        nat.call("gs_blend_backward", s["offsets"].shape[0], s["offsets"].data_ptr(),
+        nat.call("gs_blend_backward", self.tx * self.ty, s["offsets"].data_ptr(),
                  s["total"], s["ids"].data_ptr(), n, s["points"].data_ptr(),
                  s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
                  s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
@@ -318,22 +388,59 @@ class NativeTrainer:
         (FlatParams.step: NCCL all-reduce + one-launch Adam, or with
         fused_dp the one-kernel reduce-scatter / sharded Adam / all-gather).
         The optimizer kernels skip their update when the device status word
-        holds an error from this step (a bounded wait that gave up, on any
-        rank), so a step with an incomplete gradient leaves the parameters
-        unchanged; with check_status the word is read once after the
-        optimizer (one synchronisation) and the error raised in the same
-        step, else it surfaces at the next check (the next step's pair-count
-        read). With a strategy and step_index, the densification schedule of
-        scripts/train.py:224-227 runs after the optimizer step (it may change
-        the number of Gaussians). Targets in host memory are copied while the
-        views are rendered. Returns the losses."""
+        holds an error from this step (a bounded wait that gave up, or a pair
+        count beyond the layout's capacity, on any rank), so a failed step
+        leaves the parameters unchanged. With check_status the word is read
+        once after the optimizer (one synchronisation): a capacity error
+        grows the pair buffers and repeats the step (on every rank), any
+        other error is raised in the same step. Without check_status the step
+        queues with no synchronisation at all and an error surfaces at the
+        next check (check_status(), or a later step's), the updates of the
+        steps in between skipped. With a strategy and step_index, the
+        densification schedule of scripts/train.py:224-227 runs after the
+        optimizer step (it may change the number of Gaussians). Targets in
+        host memory are copied while the views are rendered. Returns the
+        losses."""
         targets, ready = self._stage_targets(targets)
-        views = self.forward_views(world_to_cameras, intrinsics)
-        losses = self.loss_and_backward(views, targets, targets_ready=ready)
-        if optimizer_step:
-            self.fp.step()
-        if check_status:
-            self.check_status()
+        for attempt in range(3):
+            views = self.forward_views(world_to_cameras, intrinsics)
+            losses = self.loss_and_backward(views, targets, targets_ready=ready)
+            if optimizer_step:
+                self.fp.step()
+            if not check_status:
+                break
+            rc = nat.query("gs_check_status", nat.stream_ptr(self.device))
+            if not self._repeat_for_capacity(rc, len(views)):
+                break
+            if optimizer_step:  # the skipped update does not count as an Adam step
+                self.fp.step_count -= 1
         if optimizer_step and self.strategy is not None and step_index is not None:
             self.strategy.adjust(self.fp, int(step_index))
         return losses
+
+    def _repeat_for_capacity(self, rc, V):
+        """After a step's status read: True when the step must be repeated
+        because a view's pair count exceeded the layout capacity on this or
+        (world > 1) any rank -- the buffers are then grown to the counts of
+        the failed step; raises for any other error; False when the step
+        succeeded everywhere."""
+        cap_err = rc == nat.GS_ERR_CAPACITY
+        other = rc not in (nat.GS_OK, nat.GS_ERR_CAPACITY, nat.GS_ERR_PEER)
+        if self.fp.world > 1:
+            import torch.distributed as dist
+
+            flags = torch.tensor([int(cap_err), int(other), int(rc != nat.GS_OK)],
+                                 dtype=torch.int32, device=self.device)
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.fp.group)
+            any_cap, any_other, any_err = (int(x) for x in flags.cpu())
+        else:
+            any_cap, any_other, any_err = int(cap_err), int(other), int(rc != nat.GS_OK)
+        if not any_err:
+            return False
+        if any_other or not any_cap:
+            raise nat.NativeError("gs_check_status", rc or nat.GS_ERR_PEER,
+                                  nat.lib().gs_last_cuda_error())
+        if self._capacity_form:
+            self.last_totals = [int(x) for x in self._batch["totals"].cpu()]
+            self._grow_capacity(V, self.last_totals)
+        return True

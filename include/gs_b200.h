@@ -173,6 +173,39 @@ GS_API int gs_tile_layout(int n, const float *points_img, const float *radii, co
                    int64_t *keys_sorted, int32_t *ids_sorted, int32_t *indexing_offset,
                    void *scratch, size_t scratch_bytes, void *stream);
 
+/* The tile layout of gs_tile_layout without a host-side pair count, so that
+ * a step's layouts queue behind its preprocess with no synchronisation (the
+ * reference reads the count with a blocking .item() between the two,
+ * rasterizer.cpp:319-322). The pair count is the scan of `counts` on the
+ * device, written to *total_dev (int64); every kernel reads it there.
+ * ids_sorted holds `capacity` entries and scratch is
+ * gs_tile_layout_scratch_bytes(n, capacity, width, height). indexing_offset
+ * holds num_tiles + 1 entries: the start offsets and, last, the end of the
+ * last tile's list (pass total = -1 to gs_blend_forward / _backward). When
+ * the count exceeds `capacity` nothing is emitted (every list is empty),
+ * *total_dev still holds the count, and GS_ERR_CAPACITY is recorded in the
+ * device status word -- the optimizer kernels then skip the step's update,
+ * and the caller grows the buffers and repeats the step. */
+GS_API int gs_tile_layout_capped(int n, const float *points_img, const float *radii,
+                                 const float *depths, const int32_t *counts, int64_t capacity,
+                                 int width, int height, int32_t *ids_sorted,
+                                 int32_t *indexing_offset, int64_t *total_dev, void *scratch,
+                                 size_t scratch_bytes, void *stream);
+
+/* The same per-tile lists and offsets as gs_tile_layout_capped (same
+ * arguments and contract: capacity, the device total, num_tiles + 1
+ * offsets, nothing emitted and GS_ERR_CAPACITY recorded beyond the
+ * capacity), built by binning instead of sorting all pairs: per-tile
+ * counters, their scan, an atomic scatter of every Gaussian's id into its
+ * tiles' buckets, and a sort of each bucket on its own by (depth bits, id)
+ * -- the order the reference's stable 64-bit sort gives within a tile
+ * (kernel.cu:820-914,1341-1388). Scratch: gs_tile_bins_scratch_bytes. */
+GS_API size_t gs_tile_bins_scratch_bytes(int n, int64_t capacity, int width, int height);
+GS_API int gs_tile_bins(int n, const float *points_img, const float *radii, const float *depths,
+                        const int32_t *counts, int64_t capacity, int width, int height,
+                        int32_t *ids_sorted, int32_t *indexing_offset, int64_t *total_dev,
+                        void *scratch, size_t scratch_bytes, void *stream);
+
 /* Scratch bytes for gs_tile_layout_views (0 on invalid arguments). totals
  * is a HOST array of num_views pair counts. */
 GS_API size_t gs_tile_layout_views_scratch_bytes(int n, int num_views, const int64_t *totals,
@@ -254,7 +287,9 @@ GS_API int gs_preprocess_forward(int n, const float *means, const float *scales,
 
 /* Blend forward over the splat records; also writes each pixel's final
  * transmittance and end index (one past its last contributing list entry).
- * Every pixel of the image (H,W,3) is written. */
+ * Every pixel of the image (H,W,3) is written. total is the number of list
+ * entries, or -1 when indexing_offset holds num_tiles + 1 entries whose last
+ * is the end of the last tile's list (as gs_tile_layout_capped writes it). */
 GS_API int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                      const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                      int width, int height, float alpha_threshold,
@@ -262,7 +297,8 @@ GS_API int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, int64
                      float *image, float *final_t, int32_t *pixel_end, void *stream);
 
 /* Blend backward: gradient outputs (grad_points_img (N,2), grad_splat (N,8))
- * must be zeroed by the caller (they are accumulated). */
+ * must be zeroed by the caller (they are accumulated). total as for
+ * gs_blend_forward (-1: the end is indexing_offset[num_tiles]). */
 GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                       const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                       const float *grad_image, const float *final_t,
@@ -423,7 +459,9 @@ GS_API int gs_dp_adam_step(int world, int rank, void *const *grad_ptrs, void *co
  * in the same layout. */
 
 /* strategy.py:48-72 for one view: where both radii are positive,
- * grad_accum[i] += |(g_u * width / 2, g_v * height / 2)|, count[i] += 1. */
+ * grad_accum[i] += |(g_u * width / 2, g_v * height / 2)|, count[i] += 1.
+ * Adds nothing while the device status word holds an error (a failed step,
+ * which the caller repeats). */
 GS_API int gs_densify_accumulate(int n, const float *grad_points, const float *radii, int width,
                                  int height, float *grad_accum, float *count, void *stream);
 
