@@ -21,9 +21,13 @@
 //      then complete but in arbitrary order);
 //   4. bin_sort_kernel: one block per tile sorts its bucket by the key
 //      (depth bits << 32 | id), built from the view's depths: buckets of up
-//      to kChunk entries in registers and shared memory (a sorting network on
-//      each thread's 8 keys, then merge-path merges of sorted runs); larger
-//      buckets as sorted chunks merged run by run through global scratch.
+//      to 2048 entries by 256 threads, up to 8192 by 1024 threads, in
+//      registers and shared memory (a sorting network on each thread's 8
+//      keys, then merge-path merges of sorted runs); longer buckets as
+//      sorted chunks merged run by run through global scratch.
+// With up to kMaxPrivTiles tiles, steps 1 and 3 keep the tile counters in
+// shared memory per block (bin_hist_kernel, bin_colscan_kernel,
+// bin_place_kernel) instead of global atomics.
 // Every key is unique, so any correct sort yields the reference's order bit
 // for bit. No host synchronisation: the pair count stays on the device.
 #include "gs_common.cuh"
@@ -31,15 +35,13 @@
 namespace gs {
 namespace binning {
 
-constexpr int kThreads = 256;
 constexpr int kItems = 8;
-constexpr int kChunk = kThreads * kItems;  // 2048 keys sorted on chip
 constexpr int kSmallRect = 8;
 constexpr uint64_t kPad = ~0ull;  // sorts after every real key
 
 struct Ctl {
-  int32_t overflow;  // set by the scan when the total exceeds the capacity
-  int32_t pad;
+  int32_t overflow;   // set by the scan when the total exceeds the capacity
+  int32_t num_long;   // buckets longer than the short sort's chunk, listed in long_tiles
 };
 
 // The tiles of one Gaussian's rectangle, row-major, q-th of them.
@@ -49,20 +51,20 @@ __device__ __forceinline__ int rect_tile(const TileRect &r, int q, int tx) {
   return (r.y0 + row) * tx + r.x0 + col;
 }
 
-// Visits every (Gaussian, tile) pair of [0, n): small rectangles by their
-// own thread, larger ones by the whole warp (lane q takes the rectangle's
-// q-th, q+32-th, ... tile). f(tile, gaussian). Called by whole warps.
+// Visits every (Gaussian, tile) pair of Gaussian i (valid: i < n): small
+// rectangles by the calling thread, larger ones by the whole warp (lane q
+// takes the rectangle's q-th, q+32-th, ... tile). f(tile, gaussian). Called
+// by whole warps (every lane, valid or not).
 template <typename F>
-__device__ __forceinline__ void for_each_pair(int n, const float2 *__restrict__ points,
-                                              const float2 *__restrict__ radii,
-                                              const int32_t *__restrict__ counts, int width,
-                                              int height, F f) {
+__device__ __forceinline__ void pairs_of(int i, bool valid, const float2 *__restrict__ points,
+                                         const float2 *__restrict__ radii,
+                                         const int32_t *__restrict__ counts, int width,
+                                         int height, F f) {
   const int lane = threadIdx.x & 31;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int tx = tiles_x_of(width);
   TileRect r{0, -1, 0, -1, true};
   int area = 0;
-  if (i < n && counts[i] > 0) {
+  if (valid && counts[i] > 0) {
     const float2 p = points[i], rd = radii[i];
     r = tile_rect(p.x, p.y, rd.x, rd.y, width, height);
     if (!r.empty) area = (r.x1 - r.x0 + 1) * (r.y1 - r.y0 + 1);
@@ -80,9 +82,19 @@ __device__ __forceinline__ void for_each_pair(int n, const float2 *__restrict__ 
     rj.y0 = __shfl_sync(0xffffffffu, r.y0, j);
     rj.y1 = __shfl_sync(0xffffffffu, r.y1, j);
     const int aj = __shfl_sync(0xffffffffu, area, j);
-    const int gj = blockIdx.x * blockDim.x + (threadIdx.x & ~31) + j;
+    const int gj = __shfl_sync(0xffffffffu, i, j);
     for (int q = lane; q < aj; q += 32) f(rect_tile(rj, q, tx), gj);
   }
+}
+
+// One Gaussian per thread over the grid.
+template <typename F>
+__device__ __forceinline__ void for_each_pair(int n, const float2 *__restrict__ points,
+                                              const float2 *__restrict__ radii,
+                                              const int32_t *__restrict__ counts, int width,
+                                              int height, F f) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  pairs_of(i, i < n, points, radii, counts, width, height, f);
 }
 
 __global__ void __launch_bounds__(256) bin_count_kernel(int n, const float2 *__restrict__ points,
@@ -191,6 +203,93 @@ __global__ void __launch_bounds__(256) bin_scatter_kernel(int n, const float2 *_
   });
 }
 
+// ---- privatised binning (no global atomics) -----------------------------------
+//
+// With up to kMaxPrivTiles tiles, every block keeps all the tile counters in
+// shared memory: block b counts the pairs of its contiguous Gaussian range
+// (bin_hist_kernel, one row hist[b][0..T) per block), a column scan turns the
+// rows into each block's base within every tile (bin_colscan_kernel), and the
+// placement (bin_place_kernel) hands out slots from shared-memory cursors
+// started at offsets[t] + hist[b][t]. The global atomics of the direct kernels
+// above, ~600 on each tile counter at config 1, serialise in L2; here each
+// tile counter in global memory is read and written once per block.
+constexpr int kPrivThreads = 512;
+constexpr int kMaxPrivTiles = 24576;  // 96 KB of shared counters
+
+__device__ __forceinline__ void block_gaussian_range(int n, int &lo, int &hi) {
+  const int per = (n + gridDim.x - 1) / gridDim.x;
+  lo = min(n, blockIdx.x * per);
+  hi = min(n, lo + per);
+}
+
+__global__ void __launch_bounds__(kPrivThreads) bin_hist_kernel(
+    int n, const float2 *__restrict__ points, const float2 *__restrict__ radii,
+    const int32_t *__restrict__ counts, int width, int height, int T,
+    uint32_t *__restrict__ hist) {
+  extern __shared__ uint32_t s_cnt[];
+  for (int k = threadIdx.x; k < T; k += kPrivThreads) s_cnt[k] = 0u;
+  __syncthreads();
+  int lo, hi;
+  block_gaussian_range(n, lo, hi);
+  for (int base = lo; base < hi; base += kPrivThreads) {  // block-uniform trip count
+    const int i = base + threadIdx.x;
+    pairs_of(i, i < hi, points, radii, counts, width, height,
+             [&](int tile, int) { atomicAdd(s_cnt + tile, 1u); });
+  }
+  __syncthreads();
+  uint32_t *row = hist + (size_t)blockIdx.x * T;
+  for (int k = threadIdx.x; k < T; k += kPrivThreads) row[k] = s_cnt[k];
+}
+
+// The rows become exclusive prefixes over the blocks, the column totals the
+// tiles' counts. A block takes 32 tiles (a warp's lanes, coalesced across
+// each row) and splits the rows into kColSlices slices, one per warp: slice
+// sums, their prefix over the slices in shared memory, then the rewrite.
+constexpr int kColSlices = 16;
+
+__global__ void __launch_bounds__(32 * kColSlices) bin_colscan_kernel(
+    int T, int B, uint32_t *__restrict__ hist, uint32_t *__restrict__ tile_count) {
+  __shared__ uint32_t s_part[kColSlices][32];
+  const int lane = threadIdx.x & 31, slice = threadIdx.x >> 5;
+  const int t = blockIdx.x * 32 + lane;
+  const int per = (B + kColSlices - 1) / kColSlices;
+  const int b0 = min(B, slice * per), b1 = min(B, b0 + per);
+  uint32_t sum = 0;
+  if (t < T)
+    for (int b = b0; b < b1; ++b) sum += hist[(size_t)b * T + t];
+  s_part[slice][lane] = sum;
+  __syncthreads();
+  uint32_t run = 0;
+  for (int q = 0; q < slice; ++q) run += s_part[q][lane];
+  if (t < T) {
+    for (int b = b0; b < b1; ++b) {
+      const uint32_t v = hist[(size_t)b * T + t];
+      hist[(size_t)b * T + t] = run;
+      run += v;
+    }
+    if (slice == kColSlices - 1) tile_count[t] = run;
+  }
+}
+
+__global__ void __launch_bounds__(kPrivThreads) bin_place_kernel(
+    int n, const float2 *__restrict__ points, const float2 *__restrict__ radii,
+    const int32_t *__restrict__ counts, int width, int height, int T,
+    const uint32_t *__restrict__ hist, const int32_t *__restrict__ offsets,
+    int32_t *__restrict__ ids, const Ctl *ctl) {
+  if (ctl->overflow) return;  // grid-uniform
+  extern __shared__ uint32_t s_cur[];
+  const uint32_t *row = hist + (size_t)blockIdx.x * T;
+  for (int k = threadIdx.x; k < T; k += kPrivThreads) s_cur[k] = (uint32_t)offsets[k] + row[k];
+  __syncthreads();
+  int lo, hi;
+  block_gaussian_range(n, lo, hi);
+  for (int base = lo; base < hi; base += kPrivThreads) {
+    const int i = base + threadIdx.x;
+    pairs_of(i, i < hi, points, radii, counts, width, height,
+             [&](int tile, int g) { ids[atomicAdd(s_cur + tile, 1u)] = g; });
+  }
+}
+
 // ---- per-tile sort ---------------------------------------------------------
 
 __device__ __forceinline__ void cswap(uint64_t &a, uint64_t &b) {
@@ -244,23 +343,32 @@ __device__ __forceinline__ void merge_items(LoadA a, int la, LoadB b, int lb, in
   }
 }
 
-// Sorts the block's kChunk keys (kItems per thread, thread t holding
-// positions t*kItems..) up to runs of `span` (a power of two >= kItems,
-// <= kChunk): on return thread t holds positions t*kItems.. of the sorted
-// chunk. s_keys: kChunk keys of shared memory. Two barriers per merge level.
+// Shared-memory slot of logical position p of a THREADS * kItems chunk:
+// item q of every thread is one contiguous row, so that the threads' stores
+// of their q-th keys, and the reads of neighbouring merge positions by
+// neighbouring threads, fall in distinct banks.
+template <int THREADS>
+__device__ __forceinline__ int slot_of(int p) {
+  return (p & (kItems - 1)) * THREADS + (p >> 3);
+}
+
+// Sorts the block's THREADS * kItems keys (kItems per thread, thread t
+// holding positions t*kItems..) up to runs of `span` (a power of two >=
+// kItems, <= THREADS * kItems): on return thread t holds positions
+// t*kItems.. of the sorted chunk. Two barriers per merge level.
+template <int THREADS>
 __device__ __forceinline__ void block_sort(uint64_t k[kItems], int span, uint64_t *s_keys) {
   sort8(k);
   const int t = threadIdx.x;
   for (int run = kItems; run < span; run <<= 1) {
 #pragma unroll
-    for (int q = 0; q < kItems; ++q) s_keys[t * kItems + q] = k[q];
+    for (int q = 0; q < kItems; ++q) s_keys[q * THREADS + t] = k[q];
     __syncthreads();
     const int pair = 2 * run;
     const int start = (t * kItems) / pair * pair;
     const int diag = t * kItems - start;
-    const uint64_t *A = s_keys + start, *B = s_keys + start + run;
-    auto la = [&](int i) { return A[i]; };
-    auto lb = [&](int i) { return B[i]; };
+    auto la = [&](int i) { return s_keys[slot_of<THREADS>(start + i)]; };
+    auto lb = [&](int i) { return s_keys[slot_of<THREADS>(start + run + i)]; };
     const int ai = merge_path(la, run, lb, run, diag);
     merge_items(la, run, lb, run, ai, diag - ai, k);
     __syncthreads();
@@ -278,22 +386,20 @@ __device__ __forceinline__ int next_pow2(int x) {
   return p;
 }
 
-// One block per tile: sorts the tile's bucket ids[off[t] .. off[t+1]) in
-// place by (depth bits, id). Buckets above kChunk: sorted chunks written to
-// keys_a, merged run by run between keys_a and keys_b (global scratch at the
-// bucket's own offsets), the ids taken from the last run.
-__global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__restrict__ offsets,
-                                                            const float *__restrict__ depths,
-                                                            int n, int32_t *__restrict__ ids,
-                                                            uint64_t *__restrict__ keys_a,
-                                                            uint64_t *__restrict__ keys_b) {
-  __shared__ uint64_t s_keys[kChunk];
-  const int tile = blockIdx.x;
-  const int beg = offsets[tile], L = offsets[tile + 1] - beg;
-  if (L <= 1) return;  // block-uniform
+// The whole block sorts the bucket ids[beg .. beg + L) in place by (depth
+// bits, id). Buckets of up to THREADS * kItems entries are sorted on chip;
+// longer ones as sorted chunks of that size written to keys_a, merged run by
+// run between keys_a and keys_b (global scratch at the bucket's own
+// offsets), the ids taken from the last run. Every thread returns after the
+// same barriers.
+template <int THREADS>
+__device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, int n,
+                            int32_t *__restrict__ ids, uint64_t *__restrict__ keys_a,
+                            uint64_t *__restrict__ keys_b, uint64_t *s_keys) {
+  constexpr int kCh = THREADS * kItems;
   const int t = threadIdx.x;
   uint64_t k[kItems];
-  if (L <= kChunk) {
+  if (L <= kCh) {
     const int span = next_pow2(L);
     // A warp whose positions are all padding only takes part in the barriers
     // (two per merge level). The test is per warp, so that every barrier is
@@ -311,7 +417,7 @@ __global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__res
       const int p = t * kItems + q;
       k[q] = p < L ? key_of(ids[beg + p], depths, n) : kPad;
     }
-    block_sort(k, span, s_keys);
+    block_sort<THREADS>(k, span, s_keys);
 #pragma unroll
     for (int q = 0; q < kItems; ++q) {
       const int p = t * kItems + q;
@@ -319,15 +425,15 @@ __global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__res
     }
     return;
   }
-  // large bucket: sorted chunks of kChunk into keys_a
+  // long bucket: sorted chunks of kCh into keys_a
   uint64_t *ka = keys_a + beg, *kb = keys_b + beg;
-  for (int c0 = 0; c0 < L; c0 += kChunk) {
+  for (int c0 = 0; c0 < L; c0 += kCh) {
 #pragma unroll
     for (int q = 0; q < kItems; ++q) {
       const int p = c0 + t * kItems + q;
       k[q] = p < L ? key_of(ids[beg + p], depths, n) : kPad;
     }
-    block_sort(k, kChunk, s_keys);
+    block_sort<THREADS>(k, kCh, s_keys);
 #pragma unroll
     for (int q = 0; q < kItems; ++q) {
       const int p = c0 + t * kItems + q;
@@ -335,9 +441,9 @@ __global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__res
     }
   }
   __syncthreads();
-  // merge runs of kChunk, 2 kChunk, ... (ping-pong ka <-> kb)
-  for (int run = kChunk; run < L; run <<= 1) {
-    for (int out0 = 0; out0 < L; out0 += kChunk) {
+  // merge runs of kCh, 2 kCh, ... (ping-pong ka <-> kb)
+  for (int run = kCh; run < L; run <<= 1) {
+    for (int out0 = 0; out0 < L; out0 += kCh) {
       const int p0 = out0 + t * kItems;  // this thread's first output position
       if (p0 < L) {
         const int start = p0 / (2 * run) * (2 * run);
@@ -359,25 +465,75 @@ __global__ void __launch_bounds__(kThreads) bin_sort_kernel(const int32_t *__res
     ka = kb;
     kb = tmp;
   }
-  for (int p = t; p < L; p += kThreads) ids[beg + p] = (int32_t)(uint32_t)ka[p];
+  for (int p = t; p < L; p += THREADS) ids[beg + p] = (int32_t)(uint32_t)ka[p];
 }
+
+// One block per tile sorts buckets of up to kSortSmall * kItems entries;
+// longer buckets are listed (ctl->num_long, long_tiles) for
+// bin_sort_long_kernel.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) bin_sort_kernel(const int32_t *__restrict__ offsets,
+                                                           const float *__restrict__ depths,
+                                                           int n, int32_t *__restrict__ ids,
+                                                           Ctl *ctl,
+                                                           int32_t *__restrict__ long_tiles) {
+  extern __shared__ uint64_t s_keys[];  // THREADS * kItems keys
+  const int tile = blockIdx.x;
+  const int beg = offsets[tile], L = offsets[tile + 1] - beg;
+  if (L <= 1) return;  // block-uniform
+  if (L > THREADS * kItems) {
+    if (threadIdx.x == 0) long_tiles[atomicAdd(&ctl->num_long, 1)] = tile;
+    return;
+  }
+  sort_bucket<THREADS>(beg, L, depths, n, ids, nullptr, nullptr, s_keys);
+}
+
+// The listed long buckets, a block at a time over the list.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) bin_sort_long_kernel(
+    const int32_t *__restrict__ offsets, const float *__restrict__ depths, int n,
+    int32_t *__restrict__ ids, const Ctl *ctl, const int32_t *__restrict__ long_tiles,
+    uint64_t *__restrict__ keys_a, uint64_t *__restrict__ keys_b) {
+  extern __shared__ uint64_t s_keys[];  // THREADS * kItems keys
+  const int count = ctl->num_long;
+  for (int q = blockIdx.x; q < count; q += gridDim.x) {  // block-uniform
+    const int tile = long_tiles[q];
+    const int beg = offsets[tile], L = offsets[tile + 1] - beg;
+    sort_bucket<THREADS>(beg, L, depths, n, ids, keys_a, keys_b, s_keys);
+    __syncthreads();  // s_keys is reused by the next bucket
+  }
+}
+
+constexpr int kSortSmall = 256;   // buckets up to 2048 entries
+constexpr int kSortLarge = 1024;  // longer buckets: on chip up to 8192 entries
 
 }  // namespace binning
 
 // Scratch of gs_tile_bins, carved in this order.
 struct BinScratch {
-  size_t ctl, count, cursor, keys_a, keys_b, total;
+  size_t ctl, count, cursor, longs, hist, keys_a, keys_b, total;
+  int blocks;  // blocks of the privatised binning (0: direct global atomics)
 };
 
 static inline size_t bin_align(size_t x) { return (x + 255) / 256 * 256; }
 
+static int bin_sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
 static BinScratch bin_scratch(int64_t capacity, int num_tiles) {
   const size_t cap = (size_t)(capacity > 0 ? capacity : 1);
   BinScratch L;
+  L.blocks = num_tiles <= binning::kMaxPrivTiles ? 2 * bin_sm_count() : 0;
   L.ctl = 0;
   L.count = bin_align(sizeof(binning::Ctl));
   L.cursor = bin_align(L.count + 4 * (size_t)num_tiles);
-  L.keys_a = bin_align(L.cursor + 4 * (size_t)num_tiles);
+  L.longs = bin_align(L.cursor + 4 * (size_t)num_tiles);
+  L.hist = bin_align(L.longs + 4 * (size_t)num_tiles);
+  L.keys_a = bin_align(L.hist + 4 * (size_t)num_tiles * (size_t)L.blocks);
   L.keys_b = bin_align(L.keys_a + 8 * cap);
   L.total = bin_align(L.keys_b + 8 * cap);
   return L;
@@ -412,12 +568,26 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
   Ctl *ctl = reinterpret_cast<Ctl *>(p + L.ctl);
   uint32_t *tcount = reinterpret_cast<uint32_t *>(p + L.count);
   uint32_t *cursor = reinterpret_cast<uint32_t *>(p + L.cursor);
-  int rc = cuda_status(cudaMemsetAsync(p, 0, L.keys_a, st));  // ctl and the tile counters
+  uint32_t *hist = reinterpret_cast<uint32_t *>(p + L.hist);
+  // ctl and the tile counters start at zero
+  int rc = cuda_status(cudaMemsetAsync(p, 0, L.cursor, st));
   if (rc) return rc;
   const float2 *pts = reinterpret_cast<const float2 *>(points_img);
   const float2 *rad = reinterpret_cast<const float2 *>(radii);
   const int gblocks = (n + 255) / 256;
-  if (n > 0) {
+  const size_t priv_smem = sizeof(uint32_t) * (size_t)T;
+  if (n > 0 && L.blocks > 0) {
+    if (priv_smem > 48 * 1024) {
+      cudaFuncSetAttribute(bin_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)priv_smem);
+      cudaFuncSetAttribute(bin_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)priv_smem);
+    }
+    bin_hist_kernel<<<L.blocks, kPrivThreads, priv_smem, st>>>(n, pts, rad, counts, width,
+                                                                height, T, hist);
+    bin_colscan_kernel<<<(T + 31) / 32, 32 * kColSlices, 0, st>>>(T, L.blocks, hist, tcount);
+    count_launch(2);
+  } else if (n > 0) {
     bin_count_kernel<<<gblocks, 256, 0, st>>>(n, pts, rad, counts, width, height, tcount);
     count_launch();
   }
@@ -425,13 +595,26 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
                                               total_dev, ctl, device_status_word());
   count_launch();
   if (n > 0) {
-    bin_scatter_kernel<<<gblocks, 256, 0, st>>>(n, pts, rad, counts, width, height, capacity,
-                                                cursor, ids_sorted, ctl);
+    if (L.blocks > 0) {
+      bin_place_kernel<<<L.blocks, kPrivThreads, priv_smem, st>>>(
+          n, pts, rad, counts, width, height, T, hist, indexing_offset, ids_sorted, ctl);
+    } else {
+      bin_scatter_kernel<<<gblocks, 256, 0, st>>>(n, pts, rad, counts, width, height, capacity,
+                                                  cursor, ids_sorted, ctl);
+    }
     count_launch();
-    bin_sort_kernel<<<T, kThreads, 0, st>>>(indexing_offset, depths, n, ids_sorted,
-                                            reinterpret_cast<uint64_t *>(p + L.keys_a),
-                                            reinterpret_cast<uint64_t *>(p + L.keys_b));
-    count_launch();
+    uint64_t *ka = reinterpret_cast<uint64_t *>(p + L.keys_a);
+    uint64_t *kb = reinterpret_cast<uint64_t *>(p + L.keys_b);
+    int32_t *longs = reinterpret_cast<int32_t *>(p + L.longs);
+    const size_t smem_small = sizeof(uint64_t) * kSortSmall * kItems;
+    const size_t smem_large = sizeof(uint64_t) * kSortLarge * kItems;
+    cudaFuncSetAttribute(bin_sort_long_kernel<kSortLarge>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_large);
+    bin_sort_kernel<kSortSmall><<<T, kSortSmall, smem_small, st>>>(indexing_offset, depths, n,
+                                                                   ids_sorted, ctl, longs);
+    bin_sort_long_kernel<kSortLarge><<<2 * bin_sm_count(), kSortLarge, smem_large, st>>>(
+        indexing_offset, depths, n, ids_sorted, ctl, longs, ka, kb);
+    count_launch(2);
   }
   return launch_status();
 }

@@ -9,9 +9,11 @@ views sharded across ranks:
 
 * activations fused into the preprocess kernels (their Jacobians in the
   preprocess backward), so gradients come out w.r.t. the raw parameters;
-* every view's preprocess is queued before one host synchronisation that
-  reads all the views' pair counts (the reference synchronises once per
-  view, rasterizer.cpp:322);
+* no host synchronisation inside a step: the tile layouts take the pair
+  counts from the device (the reference reads each view's count with a
+  blocking .item(), rasterizer.cpp:322) and write into buffers of a fixed
+  capacity, sized at the first step and grown when a step overflows them
+  (the overflowing step is skipped on device and repeated);
 * the clamp*255 of render() and the loss with its gradient in one kernel
   (L1, or with ssim_lambda > 0 the reference's (1 - lambda) L1 +
   lambda (1 - SSIM) of scripts/train.py:186-203, in two kernels);
@@ -49,7 +51,7 @@ class NativeTrainer:
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 streams: int = 2, layout: str = "capped", **render_opts):
+                 streams: int = 2, layout: str = "binned", **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -72,7 +74,7 @@ class NativeTrainer:
         self._ssim_scratch = [None] * self.num_streams
         # "batched": every view's tile layout in one cooperative launch
         # (gs_tile_layout_views); "per_view": one gs_tile_layout per view on
-        # the view's stream
+        # the view's stream (both sized by a host read of the pair counts);
         # "binned": per-view layouts by per-tile binning (gs_tile_bins);
         # "capped": per-view layouts by the two radix sorts
         # (gs_tile_layout_capped). Both write into buffers of a fixed

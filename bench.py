@@ -83,7 +83,7 @@ def parse():
     p.add_argument("--streams", type=int, default=2,
                    help="CUDA streams the native trainer spreads a step's views over")
     p.add_argument("--layout", choices=["binned", "capped", "batched", "per_view"],
-                   default="capped",
+                   default="binned",
                    help="tile layout: one per view into fixed-capacity buffers with the pair "
                         "counts kept on the device (no host synchronisation in a step), by "
                         "per-tile binning or by two radix sorts; every view in one cooperative "
@@ -443,7 +443,7 @@ class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
     def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl",
-                 streams=2, layout="capped"):
+                 streams=2, layout="binned"):
         self.cfg = cfg
         self.world = world
         self.device = device
