@@ -38,6 +38,7 @@ SIGNATURES = {
     "gs_version": (I, []),
     "gs_last_cuda_error": (I, []),
     "gs_launch_count": (ctypes.c_uint64, []),
+    "gs_note_launches": (None, [I64]),
     "gs_check_status": (I, [P]),
     "gs_sync": (I, [P]),
     "gs_selftest_bounded_wait": (I, [P, P]),
@@ -70,6 +71,9 @@ SIGNATURES = {
     "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P]),
     "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P]),
     "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
+    "gs_adam_table_bytes": (SZ, []),
+    "gs_adam_table": (I, [I64, I, P, P, P, F, F, I64, P, SZ]),
+    "gs_adam_step_table": (I, [I64, P, P, P, P, P, F, F, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
     "gs_ssim_scratch_bytes": (SZ, [I, I, I]),
     "gs_densify_accumulate": (I, [I, P, P, I, I, P, P, P]),

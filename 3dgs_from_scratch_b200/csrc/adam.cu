@@ -34,6 +34,28 @@ __global__ void __launch_bounds__(256) adam_kernel(float4 *__restrict__ p, const
   }
 }
 
+// The same update with the group table (and its folded bias corrections)
+// read from device memory, so that a captured launch (CUDA graph) applies
+// the step whose table the host uploaded before the replay.
+__global__ void __launch_bounds__(256) adam_table_kernel(float4 *__restrict__ p,
+                                                         const float4 *__restrict__ g,
+                                                         float4 *__restrict__ m,
+                                                         float4 *__restrict__ v, int64_t n4,
+                                                         const AdamGroups *__restrict__ Gd,
+                                                         float b1, float b2,
+                                                         const uint32_t *status) {
+  if (ld_volatile_u32(status) != 0u) return;
+  const AdamGroups G = *Gd;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
+    adam_float4(G, 4 * i, pp, gg, mm, vv, b1, b2);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
 int build_adam_groups(int64_t n, int num_groups, const int64_t *group_ends, const float *lrs,
                       const float *eps, float beta1, float beta2, int64_t step, AdamGroups *G) {
   if (num_groups < 1 || num_groups > kAdamMaxGroups || step < 1 || group_ends == nullptr ||
@@ -90,6 +112,45 @@ extern "C" int gs_adam_step(int64_t n, float *params, const float *grads, float 
       reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
       reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), n4, G, beta1,
       beta2, status);
+  count_launch();
+  return launch_status();
+}
+
+extern "C" size_t gs_adam_table_bytes(void) { return sizeof(AdamGroups); }
+
+extern "C" int gs_adam_table(int64_t n, int num_groups, const int64_t *group_ends,
+                             const float *lrs, const float *eps, float beta1, float beta2,
+                             int64_t step, void *table_host, size_t table_bytes) {
+  if (table_host == nullptr || table_bytes < sizeof(AdamGroups) || n < 0 || (n & 3))
+    return GS_ERR_INVALID_ARGUMENT;
+  return build_adam_groups(n, num_groups, group_ends, lrs, eps, beta1, beta2, step,
+                           reinterpret_cast<AdamGroups *>(table_host));
+}
+
+static int adam_grid(int64_t n4) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n4 + 255) / 256;
+  return (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+}
+
+extern "C" int gs_adam_step_table(int64_t n, float *params, const float *grads, float *exp_avg,
+                                  float *exp_avg_sq, const void *table_dev, float beta1,
+                                  float beta2, void *stream) {
+  if (n < 0 || (n & 3) || table_dev == nullptr || ((uintptr_t)table_dev & 7))
+    return GS_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)params | (uintptr_t)grads | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq) & 15))
+    return GS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return GS_OK;
+  uint32_t *status = device_status_word();
+  if (status == nullptr) return GS_ERR_CUDA;
+  const int64_t n4 = n / 4;
+  adam_table_kernel<<<adam_grid(n4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
+      reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), n4,
+      reinterpret_cast<const AdamGroups *>(table_dev), beta1, beta2, status);
   count_launch();
   return launch_status();
 }

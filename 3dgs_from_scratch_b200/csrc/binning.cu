@@ -570,7 +570,7 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
   uint32_t *cursor = reinterpret_cast<uint32_t *>(p + L.cursor);
   uint32_t *hist = reinterpret_cast<uint32_t *>(p + L.hist);
   // ctl and the tile counters start at zero
-  int rc = cuda_status(cudaMemsetAsync(p, 0, L.cursor, st));
+  int rc = zero_async(p, L.cursor, st);
   if (rc) return rc;
   const float2 *pts = reinterpret_cast<const float2 *>(points_img);
   const float2 *rad = reinterpret_cast<const float2 *>(radii);

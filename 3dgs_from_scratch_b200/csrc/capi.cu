@@ -68,6 +68,23 @@ int symbol_address(const void *symbol, SymbolCache *cache, void **out) {
   return GS_OK;
 }
 
+__global__ void zero_words_kernel(uint32_t *__restrict__ p, size_t words) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words;
+       i += (size_t)gridDim.x * blockDim.x)
+    p[i] = 0u;
+}
+
+int zero_async(void *p, size_t bytes, cudaStream_t st) {
+  if (bytes == 0) return GS_OK;
+  if (((uintptr_t)p & 3) || (bytes & 3)) return cuda_status(cudaMemsetAsync(p, 0, bytes, st));
+  const size_t words = bytes / 4;
+  const size_t want = (words + 255) / 256;
+  const unsigned grid = (unsigned)(want < 1024 ? want : 1024);
+  zero_words_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<uint32_t *>(p), words);
+  count_launch();
+  return launch_status();
+}
+
 uint32_t *device_status_word() {
   thread_local SymbolCache cache;
   void *p = nullptr;
@@ -84,6 +101,13 @@ extern "C" int gs_version(void) { return 1; }
 extern "C" int gs_last_cuda_error(void) { return g_last_cuda_error.load(); }
 
 extern "C" uint64_t gs_launch_count(void) { return g_launches.load(); }
+
+// Launches recorded into a CUDA graph run at each replay, not at capture: the
+// caller takes them off at capture (negative n) and adds them per replay, so
+// that the launch count stays the number of this library's kernels that ran.
+extern "C" void gs_note_launches(int64_t n) {
+  g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed);
+}
 
 extern "C" int gs_sync(void *stream) {
   return cuda_status(cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)));

@@ -37,6 +37,9 @@ void count_launch(int n = 1);
 int cuda_status(cudaError_t e);                 // maps and records a CUDA error
 int launch_status();                            // cudaGetLastError after launches
 uint32_t *device_status_word();                 // per-device status word (device ptr)
+// Zero-fill of device memory by a kernel (a memset inside a CUDA graph can be
+// queued on a copy engine behind a large host transfer; a kernel is not).
+int zero_async(void *p, size_t bytes, cudaStream_t st);
 
 // Device address of a __device__ symbol in the current context. Host code
 // cannot use the symbol itself as a pointer; the address is looked up with

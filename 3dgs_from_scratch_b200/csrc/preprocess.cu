@@ -855,7 +855,7 @@ static int preprocess_forward_impl(int n, int num_views, const float *means, con
       ((uintptr_t)totals & 7))
     return GS_ERR_INVALID_ARGUMENT;
   cudaStream_t st = as_stream(stream);
-  int rc = cuda_status(cudaMemsetAsync(totals, 0, sizeof(int64_t) * num_views, st));
+  int rc = zero_async(totals, sizeof(int64_t) * num_views, st);
   if (rc || n == 0) return rc;
   if (tile_counts == nullptr) return GS_ERR_INVALID_ARGUMENT;
   PreFwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, w2c, K, campos, near_plane,

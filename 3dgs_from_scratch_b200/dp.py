@@ -238,6 +238,56 @@ class FlatParams:
                  ctypes.cast(eps_c, ctypes.c_void_p), self.betas[0], self.betas[1],
                  self.step_count, nat.stream_ptr(self.device))
 
+    # ---- the optimizer step inside a CUDA graph (world 1) -------------------
+    #
+    # A captured launch keeps the arguments it was captured with, so the step
+    # count (through Adam's bias corrections) cannot be an argument: the
+    # graph's Adam launch reads its group table from a device buffer, and
+    # upload_table() copies the table of the coming step there (from a ring
+    # of pinned host buffers, each reused only after its copy completed)
+    # before every replay.
+    _RING = 8
+
+    def table_adam_step(self):
+        """The Adam launch of a graph: reads the table last uploaded."""
+        if self.exp_avg is None or self.fused:
+            raise RuntimeError("table_adam_step needs the Adam state of a one-GPU FlatParams")
+        nat.call("gs_adam_step_table", self.padded, self.data.data_ptr(), self.grad.data_ptr(),
+                 self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(),
+                 self._table_dev.data_ptr(), self.betas[0], self.betas[1],
+                 nat.stream_ptr(self.device))
+
+    def prepare_table(self):
+        """Adam state and the device table buffer, allocated before a capture."""
+        if self.exp_avg is None:
+            self.exp_avg = torch.zeros_like(self.data)
+            self.exp_avg_sq = torch.zeros_like(self.data)
+        if getattr(self, "_table_dev", None) is None:
+            nb = int(nat.query("gs_adam_table_bytes"))
+            self._table_dev = torch.zeros(-(-nb // 8), dtype=torch.int64, device=self.device)
+            self._table_host = [torch.zeros(-(-nb // 8), dtype=torch.int64).pin_memory()
+                                for _ in range(self._RING)]
+            self._table_done = [None] * self._RING
+            self._table_slot = 0
+
+    def upload_table(self, step):
+        """Copies the group table of Adam step `step` to the device buffer,
+        on the current stream (ahead of the replay that reads it)."""
+        k = self._table_slot
+        self._table_slot = (k + 1) % self._RING
+        if self._table_done[k] is not None:
+            self._table_done[k].synchronize()  # the slot's previous copy has read it
+        host = self._table_host[k]
+        ends_c, lrs_c, eps_c = self._group_table()
+        nat.call("gs_adam_table", self.padded, len(GROUPS), ctypes.cast(ends_c, ctypes.c_void_p),
+                 ctypes.cast(lrs_c, ctypes.c_void_p), ctypes.cast(eps_c, ctypes.c_void_p),
+                 self.betas[0], self.betas[1], int(step), host.data_ptr(),
+                 host.numel() * 8)
+        self._table_dev.copy_(host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._table_done[k] = ev
+
     def fused_step(self, grad_shard_out=None):
         """The fused data-parallel optimizer step (see the class docstring).
         grad_shard_out, if given, receives this rank's shard of the summed

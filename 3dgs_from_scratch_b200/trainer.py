@@ -420,6 +420,110 @@ class NativeTrainer:
             self.strategy.adjust(self.fp, int(step_index))
         return losses
 
+    # ---- the step replayed from CUDA graphs ----------------------------------
+
+    def graph_capable(self):
+        """Steps can be replayed from CUDA graphs: one GPU (world 1, the
+        one-launch Adam), a capacity-form layout, no densification."""
+        return self.fp.world == 1 and self._capacity_form and self.strategy is None
+
+    def step_graph(self, world_to_cameras, intrinsics, targets, check_status=False):
+        """One training step (the same as step()) replayed from two CUDA
+        graphs captured on first use: the forward of every view, then the
+        loss, the backward and Adam. Per call the host only copies the
+        inputs into the graphs' static buffers -- cameras on the current
+        stream, targets on a copy stream that overlaps the forward replay --
+        uploads Adam's group table for the coming step, and launches the two
+        graphs, so the GPU is not left waiting on Python between steps. The
+        first call on a new shape runs an ordinary step(), which sizes the
+        layout buffers and Adam's state; a pair count beyond the capacity
+        (seen with check_status) grows the buffers, re-captures and repeats
+        the step. Falls back to step() when graph_capable() is False.
+        Returns the per-view losses (a static device tensor, overwritten by
+        the next call)."""
+        if not self.graph_capable():
+            return self.step(world_to_cameras, intrinsics, targets, check_status=check_status)
+        w2c = world_to_cameras.to(torch.float32)
+        V = w2c.shape[0]
+        Ks = intrinsics.to(torch.float32)
+        if Ks.dim() == 2:
+            Ks = Ks.unsqueeze(0).expand(V, 3, 3)
+        key = (V, self.n, tuple(t.dtype for t in targets), tuple(targets[0].shape))
+        g = getattr(self, "_graph", None)
+        if g is None or g["key"] != key or g["cap"] != (self._cap[0] if self._cap else None):
+            self._graph = None
+            if self._cap is None or self._cap[1] != (V, self.n) or self.fp.exp_avg is None:
+                return self.step(world_to_cameras, intrinsics, targets, check_status=True)
+            self._capture(w2c, Ks, targets, key)
+            g = self._graph
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+        cs = self._copy_stream
+        cur = torch.cuda.current_stream(self.device)
+        # Inputs on the copy stream, once the previous replay has read them:
+        # the cameras first -- the forward waits for them alone -- then the
+        # targets and Adam's table for the coming step, overlapping the
+        # forward. (Queued behind the large target copy on the same copy
+        # engine, a small camera copy on the compute stream would hold the
+        # forward back for the whole transfer.)
+        if g.get("bwd_done") is not None:
+            cs.wait_event(g["bwd_done"])
+        with torch.cuda.stream(cs):
+            g["w2c"].copy_(w2c, non_blocking=True)
+            g["K"].copy_(Ks, non_blocking=True)
+            cams_ready = cs.record_event()
+            for src, dst in zip(targets, g["targets"]):
+                dst.copy_(src, non_blocking=True)
+            self.fp.upload_table(self.fp.step_count + 1)
+            inputs_ready = cs.record_event()
+        cur.wait_event(cams_ready)
+        g["fwd"].replay()
+        cur.wait_event(inputs_ready)
+        g["bwd"].replay()
+        g["bwd_done"] = cur.record_event()
+        nat.lib().gs_note_launches(g["kernels"])
+        self.fp.step_count += 1
+        if check_status:
+            rc = nat.query("gs_check_status", nat.stream_ptr(self.device))
+            if self._repeat_for_capacity(rc, V):
+                # the step overflowed the layout buffers and skipped its
+                # update: the grown buffers redo it in one ordinary step, the
+                # next call captures again
+                self.fp.step_count -= 1
+                self._graph = None
+                return self.step(world_to_cameras, intrinsics, targets, check_status=True)
+        return g["losses"]
+
+    def _capture(self, w2c, Ks, targets, key):
+        """Captures the forward graph and the loss / backward / Adam graph
+        over static input buffers (sharing one memory pool, so the views the
+        forward leaves behind stay valid for the backward)."""
+        dev = self.device
+        self.fp.prepare_table()
+        g = {"key": key, "cap": self._cap[0],
+             "w2c": torch.empty(w2c.shape, device=dev, dtype=torch.float32),
+             "K": torch.empty(Ks.shape, device=dev, dtype=torch.float32),
+             "targets": [torch.empty(t.shape, device=dev, dtype=t.dtype) for t in targets]}
+        g["w2c"].copy_(w2c)
+        g["K"].copy_(Ks)
+        for src, dst in zip(targets, g["targets"]):
+            dst.copy_(src)
+        self.fp.upload_table(self.fp.step_count + 1)
+        torch.cuda.synchronize(dev)
+        fwd, bwd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        n0 = nat.launch_count()
+        with torch.cuda.graph(fwd):
+            views = self.forward_views(g["w2c"], g["K"])
+        with torch.cuda.graph(bwd, pool=fwd.pool()):
+            g["losses"] = self.loss_and_backward(views, g["targets"])
+            self.fp.table_adam_step()
+        # launches recorded into the graphs, counted again at every replay
+        g["kernels"] = nat.launch_count() - n0
+        nat.lib().gs_note_launches(-g["kernels"])
+        g["views"], g["fwd"], g["bwd"] = views, fwd, bwd
+        torch.cuda.synchronize(dev)
+        self._graph = g
+
     def _repeat_for_capacity(self, rc, V):
         """After a step's status read: True when the step must be repeated
         because a view's pair count exceeded the layout capacity on this or

@@ -80,6 +80,9 @@ def parse():
     p.add_argument("--global-views", type=int, default=None,
                    help="views per step over all ranks, sharded (strong scaling); "
                         "config 2 defaults to its batch of 32")
+    p.add_argument("--no-graph", action="store_true",
+                   help="run the native step eagerly instead of replaying it from CUDA graphs "
+                        "(graphs are used on one GPU)")
     p.add_argument("--streams", type=int, default=2,
                    help="CUDA streams the native trainer spreads a step's views over")
     p.add_argument("--layout", choices=["binned", "capped", "batched", "per_view"],
@@ -443,10 +446,11 @@ class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
     def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl",
-                 streams=2, layout="binned"):
+                 streams=2, layout="binned", graph=True):
         self.cfg = cfg
         self.world = world
         self.device = device
+        self.graph = graph
         raw = scenes.make_gaussians(cfg, seed=0, n=n, device=device)
         fused = {"nccl": False, "fused": "auto", "fused-p2p": "p2p"}[dp_mode]
         self.nt = trainer_mod.NativeTrainer(raw, cfg.width, cfg.height, ssim_lambda=ssim_lambda,
@@ -463,24 +467,33 @@ class NativeBenchTrainer:
                         for _ in range(views)]
         self.host_targets = [(t.cpu().round().clamp(0, 255).to(torch.uint8)).pin_memory()
                              for t in self.targets]
+        # the device-resident targets are the same uint8 images (what a data
+        # loader hands over), so both timings run the same loss
+        self.targets = [t.to(device) for t in self.host_targets]
         self.host_cams = self.cams.cpu().pin_memory()
         self.host_K = self.K.cpu().pin_memory()
         self.host_loss = torch.zeros(len(self.targets), dtype=torch.float64).pin_memory()
 
     def step(self, e2e=False, check=False):
         if e2e:
-            # cameras copied here; the pinned host targets go to the trainer, which
-            # copies them on a copy stream while the views are rendered
-            cams = self.host_cams.to(self.device, non_blocking=True)
-            K = self.host_K.to(self.device, non_blocking=True)
+            # the pinned host cameras and targets go to the trainer, which
+            # copies them (the targets on a copy stream while the views are
+            # rendered); the eager step takes device cameras
+            if self.graph:
+                cams, K = self.host_cams, self.host_K
+            else:
+                cams = self.host_cams.to(self.device, non_blocking=True)
+                K = self.host_K.to(self.device, non_blocking=True)
             tg = self.host_targets
         else:
             cams, K, tg = self.cams, self.K, self.targets
         # e2e reads the step's result back, so the status check after the
         # optimizer rides on that synchronisation; the device-timed steps are
-        # queued back to back and their status is read at the next step's
-        # pair-count read and after the timed region
-        losses = self.nt.step(cams, K, tg, check_status=e2e or check)
+        # queued back to back with no host synchronisation and their status
+        # is read after the timed region. With graph (one GPU) the step is
+        # replayed from CUDA graphs.
+        run = self.nt.step_graph if self.graph else self.nt.step
+        losses = run(cams, K, tg, check_status=e2e or check)
         if e2e:
             self.host_loss.copy_(losses, non_blocking=True)
         return losses
@@ -581,7 +594,8 @@ def sub_config2(args, world, rank, device, steps=3, warmup=2):
     cfg = scenes.CONFIGS[2]
     total = 32
     tr = NativeBenchTrainer(cfg, None, total, world, rank, device, ssim_lambda=0.2,
-                            dp_mode=args.dp, streams=args.streams, layout=args.layout)
+                            dp_mode=args.dp, streams=args.streams, layout=args.layout,
+                            graph=not args.no_graph)
     V = len(tr.targets)
     ms = timed_steps(tr.step, steps, warmup, world)
     with StageTimer() as st:
@@ -867,7 +881,8 @@ def main():
     total_views, V, lam = view_plan(args, world, rank)
     if args.trainer == "native":
         tr = NativeBenchTrainer(cfg, args.n, total_views, world, rank, device, ssim_lambda=lam,
-                                dp_mode=args.dp, streams=args.streams, layout=args.layout)
+                                dp_mode=args.dp, streams=args.streams, layout=args.layout,
+                                graph=not args.no_graph)
     else:
         if args.dp != "nccl":
             raise SystemExit("--dp fused needs --trainer native")
@@ -912,34 +927,21 @@ def main():
     value = total_views * args.steps / (ms_total / 1000.0)
     unit = "frames/s" if render_mode else "views/s"
 
-    # Per-stage times come from separate steps after the timed region, with
-    # every view on one stream (in the timed steps views overlap on two
-    # streams, which would fold one view's kernels into another's interval).
-    nt = getattr(tr, "nt", None)
-    saved_streams = nt.num_streams if nt is not None else None
-    if nt is not None:
-        nt.num_streams = 1
-    with StageTimer() as stages:
-        for _ in range(min(args.steps, 3)):
-            run_step()
-        torch.cuda.synchronize()
-    if nt is not None:
-        nt.num_streams = saved_streams
-    barrier(world)
-    stage_ms = stages.mean_ms()
-
+    # e2e right after the device-timed steps (same thermal state), then the
+    # per-stage breakdown
     e2e = None
     if not args.no_e2e:
         for _ in range(2):
             run_step(e2e=True)
         torch.cuda.synchronize()
         barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            run_step(e2e=True)
-            torch.cuda.current_stream().synchronize()  # the step's result is on the host
-        barrier(world)
-        sec = max_over_ranks(time.perf_counter() - t0, world)
+        with ClockSampler(local) as clk_e2e:
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                run_step(e2e=True)
+                torch.cuda.current_stream().synchronize()  # the step's result is on the host
+            barrier(world)
+            sec = max_over_ranks(time.perf_counter() - t0, world)
         if render_mode:
             h2d = V * (16 + 9) * 4
             d2h = V * cfg.width * cfg.height * 3
@@ -948,7 +950,27 @@ def main():
             d2h = V * 8
         e2e = {"value": total_views * args.steps / sec, "unit": unit,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "timing": "wall clock, max over ranks"}
+               "timing": "wall clock, max over ranks, right after the device-timed steps",
+               "clocks": clk_e2e.summary()}
+
+    # Per-stage times come from separate steps after the timed region, with
+    # every view on one stream (in the timed steps views overlap on two
+    # streams, which would fold one view's kernels into another's interval).
+    nt = getattr(tr, "nt", None)
+    saved_streams = nt.num_streams if nt is not None else None
+    saved_graph = getattr(tr, "graph", False)
+    if nt is not None:
+        nt.num_streams = 1
+        tr.graph = False  # stage events need the launches one by one
+    with StageTimer() as stages:
+        for _ in range(min(args.steps, 3)):
+            run_step()
+        torch.cuda.synchronize()
+    if nt is not None:
+        nt.num_streams = saved_streams
+        tr.graph = saved_graph
+    barrier(world)
+    stage_ms = stages.mean_ms()
 
     # roofline of the dominant stage
     hbm, bf16, src = peaks()

@@ -50,6 +50,10 @@ extern "C" {
 GS_API int gs_version(void);
 GS_API int gs_last_cuda_error(void);
 GS_API uint64_t gs_launch_count(void);
+/* Adds n (may be negative) to the launch count. Launches recorded into a
+ * CUDA graph run at each replay, not at capture: a caller that captures
+ * takes them off (negative n) and adds them at every replay. */
+GS_API void gs_note_launches(int64_t n);
 
 /* Device status word: bounded spin-waits (the sort's decoupled look-back,
  * the scan's look-back) record GS_ERR_DEVICE_TIMEOUT here instead of
@@ -373,6 +377,21 @@ GS_API int gs_adam_step(int64_t n, float *params, const float *grads, float *exp
                         float *exp_avg_sq, int num_groups, const int64_t *group_ends,
                         const float *lrs, const float *eps, float beta1, float beta2,
                         int64_t step, void *stream);
+
+/* gs_adam_step split for replay from a CUDA graph: gs_adam_table fills a
+ * host buffer of gs_adam_table_bytes() with the group table of step `step`
+ * (the same bias corrections gs_adam_step folds in), the caller copies it to
+ * device memory (8-byte aligned) before the launch, and gs_adam_step_table
+ * applies the update reading the table there -- so a captured launch applies
+ * whatever step the latest upload describes. Same update, bit for bit, and
+ * the same status gating as gs_adam_step. */
+GS_API size_t gs_adam_table_bytes(void);
+GS_API int gs_adam_table(int64_t n, int num_groups, const int64_t *group_ends, const float *lrs,
+                         const float *eps, float beta1, float beta2, int64_t step,
+                         void *table_host, size_t table_bytes);
+GS_API int gs_adam_step_table(int64_t n, float *params, const float *grads, float *exp_avg,
+                              float *exp_avg_sq, const void *table_dev, float beta1, float beta2,
+                              void *stream);
 
 /* The reference's per-view training loss on the raw blended image (H*W*3 =
  * n floats): rendered = clamp(raw, 0, 1) * 255 (wrapper.py:294),
