@@ -49,9 +49,11 @@ class NativeTrainer:
     """Gaussians as raw parameters (means, log-scales, raw quaternions,
     opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
 
+    AUTO_BIN_PAIRS_PER_TILE = 1024
+
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 streams: int = 2, layout: str = "binned", **render_opts):
+                 streams: int = 2, layout: str = "auto", **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -81,11 +83,15 @@ class NativeTrainer:
         # capacity and keep the pair counts on the device (no host
         # synchronisation in a step; a count beyond the capacity fails the
         # step, which step() repeats with grown buffers).
-        if layout not in ("binned", "capped", "batched", "per_view"):
-            raise ValueError("layout must be 'binned', 'capped', 'batched' or 'per_view'")
+        # "auto" picks one of the two at every sizing of the buffers: binning
+        # while the views average at most AUTO_BIN_PAIRS_PER_TILE pairs per
+        # tile (its per-tile sorts are cheap for short lists), the two sorts
+        # above (long lists, e.g. configurations 2-4).
+        if layout not in ("auto", "binned", "capped", "batched", "per_view"):
+            raise ValueError("layout must be 'auto', 'binned', 'capped', 'batched' or 'per_view'")
         self.layout = layout
-        self._capacity_form = layout in ("binned", "capped")
-        self._capacity_entry = "gs_tile_bins" if layout == "binned" else "gs_tile_layout_capped"
+        self._capacity_form = layout in ("auto", "binned", "capped")
+        self._capacity_entry = "gs_tile_layout_capped" if layout == "capped" else "gs_tile_bins"
         self._cap = None  # (capacity, (views, n), buffers) of the capacity form
         self.tx = (self.width + 15) // 16
         self.ty = (self.height + 15) // 16
@@ -237,7 +243,10 @@ class NativeTrainer:
         old = self._cap
         if old is not None and old[1] == (V, n) and old[0] >= need:
             return
-        query = ("gs_tile_bins_scratch_bytes" if self.layout == "binned"
+        if self.layout == "auto":
+            binned = need <= self.AUTO_BIN_PAIRS_PER_TILE * T
+            self._capacity_entry = "gs_tile_bins" if binned else "gs_tile_layout_capped"
+        query = ("gs_tile_bins_scratch_bytes" if self._capacity_entry == "gs_tile_bins"
                  else "gs_tile_layout_scratch_bytes")
         nbytes = int(nat.query(query, n, cap, self.width, self.height))
         bufs = dict(
@@ -472,12 +481,13 @@ class NativeTrainer:
             g["w2c"].copy_(w2c, non_blocking=True)
             g["K"].copy_(Ks, non_blocking=True)
             cams_ready = cs.record_event()
+        cur.wait_event(cams_ready)
+        g["fwd"].replay()  # queued before the rest of the host work of the step
+        with torch.cuda.stream(cs):
             for src, dst in zip(targets, g["targets"]):
                 dst.copy_(src, non_blocking=True)
             self.fp.upload_table(self.fp.step_count + 1)
             inputs_ready = cs.record_event()
-        cur.wait_event(cams_ready)
-        g["fwd"].replay()
         cur.wait_event(inputs_ready)
         g["bwd"].replay()
         g["bwd_done"] = cur.record_event()

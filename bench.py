@@ -85,12 +85,13 @@ def parse():
                         "(graphs are used on one GPU)")
     p.add_argument("--streams", type=int, default=2,
                    help="CUDA streams the native trainer spreads a step's views over")
-    p.add_argument("--layout", choices=["binned", "capped", "batched", "per_view"],
-                   default="binned",
+    p.add_argument("--layout", choices=["auto", "binned", "capped", "batched", "per_view"],
+                   default="auto",
                    help="tile layout: one per view into fixed-capacity buffers with the pair "
                         "counts kept on the device (no host synchronisation in a step), by "
-                        "per-tile binning or by two radix sorts; every view in one cooperative "
-                        "launch; or one per view sized by a host read of the pair counts")
+                        "per-tile binning or by two radix sorts (auto: binning for short "
+                        "per-tile lists); every view in one cooperative launch; or one per "
+                        "view sized by a host read of the pair counts")
     p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p"], default="fused",
                    help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
                         "reduce-scatter / sharded Adam / all-gather kernel (multicast when "
@@ -446,7 +447,7 @@ class NativeBenchTrainer:
     """The same step as Trainer, run by trainer.NativeTrainer."""
 
     def __init__(self, cfg, n, total_views, world, rank, device, ssim_lambda=0.0, dp_mode="nccl",
-                 streams=2, layout="binned", graph=True):
+                 streams=2, layout="auto", graph=True):
         self.cfg = cfg
         self.world = world
         self.device = device
