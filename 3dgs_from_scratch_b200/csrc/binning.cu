@@ -355,7 +355,20 @@ __device__ __forceinline__ int slot_of(int p) {
 // Sorts the block's THREADS * kItems keys (kItems per thread, thread t
 // holding positions t*kItems..) up to runs of `span` (a power of two >=
 // kItems, <= THREADS * kItems): on return thread t holds positions
-// t*kItems.. of the sorted chunk. Two barriers per merge level.
+// t*kItems.. of the sorted chunk. Two barriers per merge level: warp
+// barriers while the merged runs fit in a warp, block barriers above.
+// A merge level whose merged runs (2 * run keys) fit in one warp's
+// 32 * kItems positions only exchanges keys within the warp: it needs a warp
+// barrier, not a block barrier.
+__device__ __forceinline__ bool warp_level(int run) { return 2 * run <= 32 * kItems; }
+
+__device__ __forceinline__ void level_sync(int run) {
+  if (warp_level(run))
+    __syncwarp();
+  else
+    __syncthreads();
+}
+
 template <int THREADS>
 __device__ __forceinline__ void block_sort(uint64_t k[kItems], int span, uint64_t *s_keys) {
   sort8(k);
@@ -363,7 +376,7 @@ __device__ __forceinline__ void block_sort(uint64_t k[kItems], int span, uint64_
   for (int run = kItems; run < span; run <<= 1) {
 #pragma unroll
     for (int q = 0; q < kItems; ++q) s_keys[q * THREADS + t] = k[q];
-    __syncthreads();
+    level_sync(run);
     const int pair = 2 * run;
     const int start = (t * kItems) / pair * pair;
     const int diag = t * kItems - start;
@@ -371,7 +384,7 @@ __device__ __forceinline__ void block_sort(uint64_t k[kItems], int span, uint64_
     auto lb = [&](int i) { return s_keys[slot_of<THREADS>(start + run + i)]; };
     const int ai = merge_path(la, run, lb, run, diag);
     merge_items(la, run, lb, run, ai, diag - ai, k);
-    __syncthreads();
+    level_sync(run);
   }
 }
 
@@ -401,14 +414,17 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
   uint64_t k[kItems];
   if (L <= kCh) {
     const int span = next_pow2(L);
-    // A warp whose positions are all padding only takes part in the barriers
-    // (two per merge level). The test is per warp, so that every barrier is
-    // reached by whole warps; threads of an active warp past `span` merge
-    // padding (or stale shared memory), and their results are dropped.
+    // A warp whose positions are all padding only takes part in the block
+    // barriers (two per merge level above the warp levels). The test is per
+    // warp, so that every barrier is reached by whole warps; threads of an
+    // active warp past `span` merge padding (or stale shared memory), and
+    // their results are dropped.
     if ((t & ~31) * kItems >= span) {
       for (int run = kItems; run < span; run <<= 1) {
-        __syncthreads();
-        __syncthreads();
+        if (!warp_level(run)) {
+          __syncthreads();
+          __syncthreads();
+        }
       }
       return;
     }
@@ -468,24 +484,191 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
   for (int p = t; p < L; p += THREADS) ids[beg + p] = (int32_t)(uint32_t)ka[p];
 }
 
-// One block per tile sorts buckets of up to kSortSmall * kItems entries;
-// longer buckets are listed (ctl->num_long, long_tiles) for
-// bin_sort_long_kernel.
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS) bin_sort_kernel(const int32_t *__restrict__ offsets,
-                                                           const float *__restrict__ depths,
-                                                           int n, int32_t *__restrict__ ids,
-                                                           Ctl *ctl,
-                                                           int32_t *__restrict__ long_tiles) {
-  extern __shared__ uint64_t s_keys[];  // THREADS * kItems keys
+// ---- short buckets: block radix sort on the depth bits -----------------------
+//
+// A bucket of up to kRadChunk entries is sorted by one 256-thread block as a
+// stable LSD radix sort of its 32-bit depth keys (8-bit digits) in shared
+// memory, over only the low bits in which the bucket's keys differ (their
+// XOR with the first key, OR-reduced: typically 3 passes). Each pass ranks
+// the digits warp by warp -- lanes with equal digits found with one ballot
+// per digit bit, items taken in position order (position 256 w + 32 k +
+// lane), so the ranking is stable -- scans the per-warp digit counts and
+// scatters into the other buffer. Equal depth keys keep the bucket's
+// (arbitrary) order, so runs of equal keys are then put in id order: the
+// (depth bits, id) order of the reference's stable 64-bit sort.
+constexpr int kRadThreads = 256;
+constexpr int kRadWarps = kRadThreads / 32;
+constexpr int kRadItems = 8;
+constexpr int kRadChunk = kRadThreads * kRadItems;  // 2048
+
+struct RadSmem {
+  uint32_t key[2][kRadChunk];
+  int32_t val[2][kRadChunk];
+  uint32_t whist[kRadWarps][256];
+  uint32_t gbase[256];
+  uint32_t tmp[kRadWarps + 1];
+  uint32_t diff;
+};
+
+__device__ __forceinline__ uint32_t rad_block_excl_scan(uint32_t x, uint32_t *s_tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_tmp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = lane < kRadWarps ? s_tmp[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < kRadWarps; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    if (lane < kRadWarps) s_tmp[lane] = wi - w;
+  }
+  __syncthreads();
+  const uint32_t r = incl - x + s_tmp[warp];
+  __syncthreads();
+  return r;
+}
+
+__device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ depths, int n,
+                                  int32_t *__restrict__ ids, RadSmem &S) {
+  const int t = threadIdx.x, warp = t >> 5;
+  const uint32_t lane = t & 31;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  // positions [0, P): whole warps' worth of items, the tail padded with the
+  // largest key (sorts after every real key; stable, so real keys stay first)
+  const int active_warps = (L + 32 * kRadItems - 1) / (32 * kRadItems);
+  const int P = active_warps * 32 * kRadItems;
+  if (t == 0) S.diff = 0u;
+  __syncthreads();
+  uint32_t dif = 0;
+  uint32_t k0 = 0;
+  {
+    const int id0 = ids[beg];
+    k0 = (id0 >= 0 && id0 < n) ? __float_as_uint(depths[id0]) : 0xffffffffu;
+  }
+  for (int p = t; p < P; p += kRadThreads) {
+    uint32_t key = 0xffffffffu;
+    int32_t val = -1;
+    if (p < L) {
+      val = ids[beg + p];
+      key = (val >= 0 && val < n) ? __float_as_uint(depths[val]) : 0xffffffffu;
+      dif |= key ^ k0;
+    }
+    S.key[0][p] = key;
+    S.val[0][p] = val;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dif |= __shfl_xor_sync(0xffffffffu, dif, o);
+  if (lane == 0 && dif) atomicOr(&S.diff, dif);
+  __syncthreads();
+  const uint32_t diff = S.diff;
+  const int bits = diff ? 32 - __clz(diff) : 0;
+  const int passes = (bits + 7) / 8;
+  int cur = 0;
+  for (int pass = 0; pass < passes; ++pass) {  // block-uniform
+    const int shift = 8 * pass;
+    for (int k = t; k < kRadWarps * 256; k += kRadThreads) (&S.whist[0][0])[k] = 0u;
+    __syncthreads();
+    uint32_t key[kRadItems], rank[kRadItems];
+    int32_t val[kRadItems];
+    const bool wact = warp < active_warps;
+    if (wact) {
+      uint32_t lead_old[kRadItems];
+      uint8_t leader_of[kRadItems];
+#pragma unroll
+      for (int q = 0; q < kRadItems; ++q) {
+        const int p = warp * 32 * kRadItems + q * 32 + (int)lane;
+        key[q] = S.key[cur][p];
+        val[q] = S.val[cur][p];
+        const uint32_t d = (key[q] >> shift) & 0xffu;
+        uint32_t peers = 0xffffffffu;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const bool bit = (d >> b) & 1u;
+          const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+          peers &= bit ? bal : ~bal;
+        }
+        const uint32_t leader = 31 - __clz(peers);
+        uint32_t old = 0;
+        if (lane == leader) old = atomicAdd(&S.whist[warp][d], (uint32_t)__popc(peers));
+        rank[q] = (uint32_t)__popc(peers & lt_mask);
+        lead_old[q] = old;
+        leader_of[q] = (uint8_t)leader;
+      }
+#pragma unroll
+      for (int q = 0; q < kRadItems; ++q)
+        rank[q] += __shfl_sync(0xffffffffu, lead_old[q], leader_of[q]);
+    }
+    __syncthreads();
+    {  // thread t owns digit t: warp prefixes, then the digit prefix
+      const int d = t;
+      uint32_t c = 0;
+#pragma unroll
+      for (int w = 0; w < kRadWarps; ++w) {
+        const uint32_t x = S.whist[w][d];
+        S.whist[w][d] = c;
+        c += x;
+      }
+      S.gbase[d] = rad_block_excl_scan(c, S.tmp);
+    }
+    __syncthreads();
+    if (wact) {
+#pragma unroll
+      for (int q = 0; q < kRadItems; ++q) {
+        const uint32_t d = (key[q] >> shift) & 0xffu;
+        const uint32_t pos = S.gbase[d] + S.whist[warp][d] + rank[q];
+        S.key[cur ^ 1][pos] = key[q];
+        S.val[cur ^ 1][pos] = val[q];
+      }
+    }
+    __syncthreads();
+    cur ^= 1;
+  }
+  // runs of equal depth keys in id order, each by the thread at its start
+  for (int p = t; p < L; p += kRadThreads) {
+    const uint32_t kp = S.key[cur][p];
+    if ((p == 0 || S.key[cur][p - 1] != kp) && p + 1 < L && S.key[cur][p + 1] == kp) {
+      int e = p + 1;
+      while (e < L && S.key[cur][e] == kp) ++e;
+      for (int i = p + 1; i < e; ++i) {  // insertion sort of [p, e) by id
+        const int32_t v = S.val[cur][i];
+        int j = i - 1;
+        while (j >= p && S.val[cur][j] > v) {
+          S.val[cur][j + 1] = S.val[cur][j];
+          --j;
+        }
+        S.val[cur][j + 1] = v;
+      }
+    }
+  }
+  __syncthreads();
+  for (int p = t; p < L; p += kRadThreads) ids[beg + p] = S.val[cur][p];
+}
+
+// One block per tile sorts buckets of up to kRadChunk entries; longer
+// buckets are listed (ctl->num_long, long_tiles) for bin_sort_long_kernel.
+__global__ void __launch_bounds__(kRadThreads) bin_sort_kernel(const int32_t *__restrict__ offsets,
+                                                               const float *__restrict__ depths,
+                                                               int n, int32_t *__restrict__ ids,
+                                                               Ctl *ctl,
+                                                               int32_t *__restrict__ long_tiles) {
+  extern __shared__ __align__(16) unsigned char rad_raw[];
+  RadSmem &S = *reinterpret_cast<RadSmem *>(rad_raw);
   const int tile = blockIdx.x;
   const int beg = offsets[tile], L = offsets[tile + 1] - beg;
   if (L <= 1) return;  // block-uniform
-  if (L > THREADS * kItems) {
+  if (L > kRadChunk) {
     if (threadIdx.x == 0) long_tiles[atomicAdd(&ctl->num_long, 1)] = tile;
     return;
   }
-  sort_bucket<THREADS>(beg, L, depths, n, ids, nullptr, nullptr, s_keys);
+  radix_sort_bucket(beg, L, depths, n, ids, S);
 }
 
 // The listed long buckets, a block at a time over the list.
@@ -504,8 +687,7 @@ __global__ void __launch_bounds__(THREADS) bin_sort_long_kernel(
   }
 }
 
-constexpr int kSortSmall = 256;   // buckets up to 2048 entries
-constexpr int kSortLarge = 1024;  // longer buckets: on chip up to 8192 entries
+constexpr int kSortLarge = 1024;  // buckets above kRadChunk: on chip up to 8192 entries
 
 }  // namespace binning
 
@@ -606,12 +788,14 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
     uint64_t *ka = reinterpret_cast<uint64_t *>(p + L.keys_a);
     uint64_t *kb = reinterpret_cast<uint64_t *>(p + L.keys_b);
     int32_t *longs = reinterpret_cast<int32_t *>(p + L.longs);
-    const size_t smem_small = sizeof(uint64_t) * kSortSmall * kItems;
+    const size_t smem_small = sizeof(RadSmem);
     const size_t smem_large = sizeof(uint64_t) * kSortLarge * kItems;
     cudaFuncSetAttribute(bin_sort_long_kernel<kSortLarge>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_large);
-    bin_sort_kernel<kSortSmall><<<T, kSortSmall, smem_small, st>>>(indexing_offset, depths, n,
-                                                                   ids_sorted, ctl, longs);
+    cudaFuncSetAttribute(bin_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_small);
+    bin_sort_kernel<<<T, kRadThreads, smem_small, st>>>(indexing_offset, depths, n, ids_sorted,
+                                                        ctl, longs);
     bin_sort_long_kernel<kSortLarge><<<2 * bin_sm_count(), kSortLarge, smem_large, st>>>(
         indexing_offset, depths, n, ids_sorted, ctl, longs, ka, kb);
     count_launch(2);

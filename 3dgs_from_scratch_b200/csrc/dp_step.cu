@@ -45,9 +45,15 @@
 
 namespace gs {
 
-constexpr int kDpThreads = 512;
+#ifndef GS_DP_THREADS
+#define GS_DP_THREADS 512
+#endif
+#ifndef GS_DP_UNROLL
+#define GS_DP_UNROLL 4
+#endif
+constexpr int kDpThreads = GS_DP_THREADS;
 constexpr int kDpMaxWorld = 8;
-constexpr int kDpUnroll = 4;                            // float4s in flight per thread
+constexpr int kDpUnroll = GS_DP_UNROLL;                 // float4s in flight per thread
 constexpr unsigned long long kDpTimeoutNs = 4000000000ull;  // 4 s per wait
 
 struct DpPeers {
