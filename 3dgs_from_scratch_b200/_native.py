@@ -74,6 +74,7 @@ SIGNATURES = {
     "gs_adam_table_bytes": (SZ, []),
     "gs_adam_table": (I, [I64, I, P, P, P, F, F, I64, P, SZ]),
     "gs_adam_step_table": (I, [I64, P, P, P, P, P, F, F, P]),
+    "gs_adam_step_ranges": (I, [P, P, P, P, I, P, P, P, F, F, P]),
     "gs_adam_step": (I, [I64, P, P, P, P, I, P, P, P, F, F, I64, P]),
     "gs_ssim_scratch_bytes": (SZ, [I, I, I]),
     "gs_densify_accumulate": (I, [I, P, P, I, I, P, P, P]),
@@ -92,6 +93,8 @@ SIGNATURES = {
                                    P, P, P, P, P, P]),
     "gs_preprocess_forward_views": (I, [I, I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I,
                                         I, P, P, P, P, P, P, P, P]),
+    "gs_preprocess_backward_views_range": (I, [I, I, I, I, P, P, P, P, P, P, P, P, P, I, I, I,
+                                                I, I, P, P, I, P, I, P, P, P, P, P, P, P]),
     "gs_preprocess_backward_views": (I, [I, I, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P, I,
                                          P, I, P, P, P, P, P, P, P]),
 }

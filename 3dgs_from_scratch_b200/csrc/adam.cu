@@ -56,6 +56,44 @@ __global__ void __launch_bounds__(256) adam_table_kernel(float4 *__restrict__ p,
   }
 }
 
+// Adam over up to kAdamMaxGroups disjoint element ranges of the flat buffer,
+// range r belonging to group r of the device table (the step's bias
+// corrections): a slice of every group -- e.g. the parameters of a range of
+// Gaussians, each group holding them contiguously -- updated as soon as its
+// gradient is complete.
+struct AdamRanges {
+  int64_t start4[kAdamMaxGroups];   // first float4 of each range
+  int64_t prefix4[kAdamMaxGroups + 1];
+  int count;
+};
+
+__global__ void __launch_bounds__(256) adam_ranges_kernel(float4 *__restrict__ p,
+                                                          const float4 *__restrict__ g,
+                                                          float4 *__restrict__ m,
+                                                          float4 *__restrict__ v, AdamRanges R,
+                                                          const AdamGroups *__restrict__ Gd,
+                                                          float b1, float b2,
+                                                          const uint32_t *status) {
+  if (ld_volatile_u32(status) != 0u) return;
+  const int64_t total = R.prefix4[R.count];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total; k += stride) {
+    int r = 0;
+#pragma unroll
+    for (int q = 1; q < kAdamMaxGroups; ++q) r += (q < R.count && k >= R.prefix4[q]) ? 1 : 0;
+    const int64_t i = R.start4[r] + (k - R.prefix4[r]);
+    float4 pp = p[i], gg = g[i], mm = m[i], vv = v[i];
+    const float st = Gd->step_size[r], ib = Gd->inv_bc2_sqrt[r], ep = Gd->eps[r];
+    adam_one(pp.x, gg.x, mm.x, vv.x, b1, b2, st, ib, ep);
+    adam_one(pp.y, gg.y, mm.y, vv.y, b1, b2, st, ib, ep);
+    adam_one(pp.z, gg.z, mm.z, vv.z, b1, b2, st, ib, ep);
+    adam_one(pp.w, gg.w, mm.w, vv.w, b1, b2, st, ib, ep);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
 int build_adam_groups(int64_t n, int num_groups, const int64_t *group_ends, const float *lrs,
                       const float *eps, float beta1, float beta2, int64_t step, AdamGroups *G) {
   if (num_groups < 1 || num_groups > kAdamMaxGroups || step < 1 || group_ends == nullptr ||
@@ -150,6 +188,40 @@ extern "C" int gs_adam_step_table(int64_t n, float *params, const float *grads, 
   adam_table_kernel<<<adam_grid(n4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
       reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), n4,
+      reinterpret_cast<const AdamGroups *>(table_dev), beta1, beta2, status);
+  count_launch();
+  return launch_status();
+}
+
+extern "C" int gs_adam_step_ranges(float *params, const float *grads, float *exp_avg,
+                                   float *exp_avg_sq, int num_ranges, const int64_t *starts,
+                                   const int64_t *counts, const void *table_dev, float beta1,
+                                   float beta2, void *stream) {
+  if (num_ranges < 1 || num_ranges > kAdamMaxGroups || starts == nullptr || counts == nullptr ||
+      table_dev == nullptr || ((uintptr_t)table_dev & 7))
+    return GS_ERR_INVALID_ARGUMENT;
+  if ((((uintptr_t)params | (uintptr_t)grads | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq) & 15))
+    return GS_ERR_INVALID_ARGUMENT;
+  AdamRanges R{};
+  R.count = num_ranges;
+  R.prefix4[0] = 0;
+  for (int r = 0; r < num_ranges; ++r) {
+    if (starts[r] < 0 || counts[r] < 0 || (starts[r] & 3) || (counts[r] & 3))
+      return GS_ERR_INVALID_ARGUMENT;
+    R.start4[r] = starts[r] / 4;
+    R.prefix4[r + 1] = R.prefix4[r] + counts[r] / 4;
+  }
+  for (int r = num_ranges; r < kAdamMaxGroups; ++r) {
+    R.start4[r] = 0;
+    R.prefix4[r + 1] = R.prefix4[num_ranges];
+  }
+  if (R.prefix4[num_ranges] == 0) return GS_OK;
+  uint32_t *status = device_status_word();
+  if (status == nullptr) return GS_ERR_CUDA;
+  adam_ranges_kernel<<<adam_grid(R.prefix4[num_ranges]), 256, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<float4 *>(params), reinterpret_cast<const float4 *>(grads),
+      reinterpret_cast<float4 *>(exp_avg), reinterpret_cast<float4 *>(exp_avg_sq), R,
       reinterpret_cast<const AdamGroups *>(table_dev), beta1, beta2, status);
   count_launch();
   return launch_status();

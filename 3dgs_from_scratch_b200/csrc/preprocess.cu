@@ -930,6 +930,9 @@ static int launch_preprocess_backward(const PreBwdArgs &A, int n, cudaStream_t s
   return launch_status();
 }
 
+// n Gaussians; the per-view upstream arrays (mask, grad_points_img,
+// grad_splat) hold view_stride Gaussians per view (>= n: a sub-range of the
+// views' arrays when the pointers are offset to its first Gaussian).
 static int preprocess_backward_impl(int n, int num_views, const float *means,
                                     const float *scales, const float *quats,
                                     const float *opacities, const float *sh_dc,
@@ -940,8 +943,10 @@ static int preprocess_backward_impl(int n, int num_views, const float *means,
                                     const float *grad_splat, int gs_stride, float *grad_means,
                                     float *grad_scales, float *grad_quats,
                                     float *grad_opacities, float *grad_dc, float *grad_rest,
-                                    void *stream) {
-  if (n < 0 || num_views < 1 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7)
+                                    void *stream, int64_t view_stride = -1) {
+  if (view_stride < 0) view_stride = n;
+  if (n < 0 || num_views < 1 || width <= 0 || height <= 0 || gp_stride < 2 || gs_stride < 7 ||
+      view_stride < n)
     return GS_ERR_INVALID_ARGUMENT;
   if (activate && opacities == nullptr) return GS_ERR_INVALID_ARGUMENT;
   if (n == 0) return GS_OK;
@@ -949,8 +954,8 @@ static int preprocess_backward_impl(int n, int num_views, const float *means,
   PreBwdArgs A{means, scales, quats, opacities, sh_dc, sh_rest, w2c, K, campos, width, height,
                sh_sigmoid, activate, accumulate, mask, grad_points_img, gp_stride, grad_splat,
                gs_stride, grad_means, grad_scales, grad_quats, grad_opacities, grad_dc,
-               grad_rest, num_views, (int64_t)n, (int64_t)n * gp_stride,
-               (int64_t)n * gs_stride,
+               grad_rest, num_views, view_stride, view_stride * gp_stride,
+               view_stride * gs_stride,
                (gp_stride == 2 && gs_stride == 8 && ((uintptr_t)grad_points_img & 7) == 0 &&
                 ((uintptr_t)grad_splat & 15) == 0)
                    ? 1
@@ -990,4 +995,26 @@ extern "C" int gs_preprocess_backward_views(
                                   sh_sigmoid, activate, accumulate, mask, grad_points_img,
                                   gp_stride, grad_splat, gs_stride, grad_means, grad_scales,
                                   grad_quats, grad_opacities, grad_dc, grad_rest, stream);
+}
+
+extern "C" int gs_preprocess_backward_views_range(
+    int n_total, int first, int count, int num_views, const float *means, const float *scales,
+    const float *quats, const float *opacities, const float *sh_dc, const float *sh_rest,
+    const float *world_to_cameras, const float *intrinsics, const float *camera_positions,
+    int width, int height, int sh_sigmoid, int activate, int accumulate, const uint8_t *mask,
+    const float *grad_points_img, int gp_stride, const float *grad_splat, int gs_stride,
+    float *grad_means, float *grad_scales, float *grad_quats, float *grad_opacities,
+    float *grad_dc, float *grad_rest, void *stream) {
+  if (n_total < 0 || first < 0 || count < 0 || (int64_t)first + count > n_total)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (count == 0) return GS_OK;
+  const size_t f = (size_t)first;
+  return preprocess_backward_impl(
+      count, num_views, means + 3 * f, scales + 3 * f, quats + 4 * f,
+      opacities ? opacities + f : nullptr, sh_dc + 3 * f, sh_rest + 45 * f, world_to_cameras,
+      intrinsics, camera_positions, width, height, sh_sigmoid, activate, accumulate, mask + f,
+      grad_points_img + (size_t)gp_stride * f, gp_stride, grad_splat + (size_t)gs_stride * f,
+      gs_stride, grad_means + 3 * f, grad_scales + 3 * f, grad_quats + 4 * f,
+      grad_opacities ? grad_opacities + f : nullptr, grad_dc + 3 * f, grad_rest + 45 * f, stream,
+      n_total);
 }

@@ -288,6 +288,33 @@ class FlatParams:
         ev.record()
         self._table_done[k] = ev
 
+    def gaussian_ranges(self, lo, hi):
+        """Element ranges (host int64 arrays: starts, counts) of the flat
+        buffer that hold Gaussians lo .. hi - 1 in each of the six groups (a
+        group holds its Gaussians contiguously); the range that ends the
+        group also takes its padding. lo and hi multiples of 4 (or hi = N)."""
+        n = self.num_gaussians
+        starts, counts = [], []
+        for k in GROUPS:
+            off, numel = self.spans[k]
+            w = numel // n if n else 0
+            a = off + w * lo
+            b = off + ((numel + 3) // 4 * 4 if hi >= n else w * hi)
+            starts.append(a)
+            counts.append(b - a)
+        return ((ctypes.c_int64 * len(GROUPS))(*starts),
+                (ctypes.c_int64 * len(GROUPS))(*counts))
+
+    def range_adam_step(self, ranges):
+        """Adam on the element ranges of gaussian_ranges(), reading the group
+        table last uploaded (upload_table) -- in a CUDA graph or not."""
+        starts_c, counts_c = ranges
+        nat.call("gs_adam_step_ranges", self.data.data_ptr(), self.grad.data_ptr(),
+                 self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), len(GROUPS),
+                 ctypes.cast(starts_c, ctypes.c_void_p), ctypes.cast(counts_c, ctypes.c_void_p),
+                 self._table_dev.data_ptr(), self.betas[0], self.betas[1],
+                 nat.stream_ptr(self.device))
+
     def fused_step(self, grad_shard_out=None):
         """The fused data-parallel optimizer step (see the class docstring).
         grad_shard_out, if given, receives this rank's shard of the summed

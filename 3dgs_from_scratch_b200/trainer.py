@@ -53,7 +53,8 @@ class NativeTrainer:
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,
-                 streams: int = 2, layout: str = "auto", **render_opts):
+                 streams: int = 2, layout: str = "auto", adam_overlap: bool = False,
+                 **render_opts):
         self.fp = FlatParams({k: raw[k] for k in GROUPS}, lrs=lrs, group=group, fused_dp=fused_dp)
         if not 0.0 <= float(ssim_lambda) <= 1.0:
             raise ValueError("ssim_lambda must lie in [0, 1]")
@@ -65,6 +66,7 @@ class NativeTrainer:
         self.opts = dict(RENDER_DEFAULTS)
         self.opts.update(render_opts)
         self.strategy = strategy  # a densify.DeviceStrategy, or None
+        self.adam_overlap = bool(adam_overlap)
         # Views are independent between the batched preprocess and the batched
         # preprocess backward: view v's layout, blend and loss run on stream
         # v % streams, so one view's latency-bound layout kernels overlap
@@ -298,14 +300,63 @@ class NativeTrainer:
             dev = [t.to(self.device, non_blocking=True) for t in targets]
         return dev, self._copy_stream.record_event()
 
-    def loss_and_backward(self, views, targets, accumulate=False, targets_ready=None):
+    # Gaussians per range of the backward overlapped with Adam (a multiple
+    # of the preprocess kernels' 128-Gaussian chunk)
+    ADAM_OVERLAP_RANGES = 4
+
+    def overlap_adam(self):
+        """Adam runs range by range behind the preprocess backward: opted in
+        with adam_overlap (measured 1% slower than one Adam launch after the
+        backward at config 1 -- the split backward launches are smaller and
+        Adam takes SMs from them), one GPU (the one-launch Adam, not the
+        data-parallel step) and enough Gaussians to split."""
+        return (self.adam_overlap and self.fp.world == 1 and not self.fp.fused
+                and self.fp.device.type == "cuda"
+                and self.n >= 4 * 128 * self.ADAM_OVERLAP_RANGES)
+
+    def _backward_with_adam(self, n, V, pargs, adam):
+        """The multi-view preprocess backward in ADAM_OVERLAP_RANGES ranges of
+        Gaussians on the current stream, each range's Adam update (its slices
+        of the six groups, gs_adam_step_ranges) on a second stream as soon
+        as its gradient is complete -- so Adam (HBM-bound) overlaps the
+        backward of the next range (latency-bound). adam = "eager" uploads
+        the group table of the coming step first and counts the step;
+        "graph" leaves both to the caller of the graph replay."""
+        dev = self.device
+        fp = self.fp
+        if adam == "eager":
+            fp.prepare_table()
+            fp.upload_table(fp.step_count + 1)
+            fp.step_count += 1
+        if not hasattr(self, "_adam_stream"):
+            self._adam_stream = torch.cuda.Stream(device=dev)
+        cur = torch.cuda.current_stream(dev)
+        R = self.ADAM_OVERLAP_RANGES
+        per = -(-n // R)
+        per = -(-per // 128) * 128
+        bounds = [min(n, i * per) for i in range(R + 1)]
+        for i in range(R):
+            lo, hi = bounds[i], bounds[i + 1]
+            if hi <= lo:
+                continue
+            nat.call("gs_preprocess_backward_views_range", n, lo, hi - lo, V, *pargs,
+                     nat.stream_ptr(dev))
+            self._adam_stream.wait_event(cur.record_event())
+            with torch.cuda.stream(self._adam_stream):
+                fp.range_adam_step(fp.gaussian_ranges(lo, hi))
+        cur.wait_event(self._adam_stream.record_event())
+
+    def loss_and_backward(self, views, targets, accumulate=False, targets_ready=None,
+                          adam=None):
         """Loss of every view against its target (H, W, 3; float in [0, 255]
         or uint8) -- L1, or (1 - ssim_lambda) L1 + ssim_lambda (1 - SSIM)
         when ssim_lambda > 0 -- and the backward into the flat gradient buffer.
         The views' gradients are summed by one multi-view preprocess backward
         and overwrite the buffer (every element is written, zeros for
         Gaussians every view culled) unless `accumulate`, which adds them.
-        Returns the per-view losses (device tensor)."""
+        With adam ("eager" or "graph", see _backward_with_adam) the Adam
+        step runs range by range behind the backward. Returns the per-view
+        losses (device tensor)."""
         o = self.opts
         dev = self.device
         st = nat.stream_ptr(dev)
@@ -343,13 +394,17 @@ class NativeTrainer:
         b = self._batch
         if V != b["mask"].shape[0]:
             raise ValueError("loss_and_backward takes the views of the last forward_views call")
-        nat.call("gs_preprocess_backward_views", n, V, self._ptr("means"), self._ptr("scales"),
-                 self._ptr("quaternions"), self._ptr("opacities"), self._ptr("sh_coeffs_dc"),
-                 self._ptr("sh_coeffs_rest"), b["w2c"].data_ptr(), b["K"].data_ptr(),
-                 b["campos"].data_ptr(), W, H, 0, 1, int(accumulate), b["mask"].data_ptr(),
-                 g_points_all.data_ptr(), 2, g_splat_all.data_ptr(), 8, self._gptr("means"),
-                 self._gptr("scales"), self._gptr("quaternions"), self._gptr("opacities"),
-                 self._gptr("sh_coeffs_dc"), self._gptr("sh_coeffs_rest"), st)
+        pargs = (self._ptr("means"), self._ptr("scales"), self._ptr("quaternions"),
+                 self._ptr("opacities"), self._ptr("sh_coeffs_dc"), self._ptr("sh_coeffs_rest"),
+                 b["w2c"].data_ptr(), b["K"].data_ptr(), b["campos"].data_ptr(), W, H, 0, 1,
+                 int(accumulate), b["mask"].data_ptr(), g_points_all.data_ptr(), 2,
+                 g_splat_all.data_ptr(), 8, self._gptr("means"), self._gptr("scales"),
+                 self._gptr("quaternions"), self._gptr("opacities"), self._gptr("sh_coeffs_dc"),
+                 self._gptr("sh_coeffs_rest"))
+        if adam is None:
+            nat.call("gs_preprocess_backward_views", n, V, *pargs, st)
+        else:
+            self._backward_with_adam(n, V, pargs, adam)
         l1 = loss_sums[:, 0] / npx
         if lam == 0:
             return l1
@@ -413,10 +468,12 @@ class NativeTrainer:
         host memory are copied while the views are rendered. Returns the
         losses."""
         targets, ready = self._stage_targets(targets)
+        overlap = optimizer_step and self.overlap_adam()
         for attempt in range(3):
             views = self.forward_views(world_to_cameras, intrinsics)
-            losses = self.loss_and_backward(views, targets, targets_ready=ready)
-            if optimizer_step:
+            losses = self.loss_and_backward(views, targets, targets_ready=ready,
+                                            adam="eager" if overlap else None)
+            if optimizer_step and not overlap:
                 self.fp.step()
             if not check_status:
                 break
@@ -525,8 +582,11 @@ class NativeTrainer:
         with torch.cuda.graph(fwd):
             views = self.forward_views(g["w2c"], g["K"])
         with torch.cuda.graph(bwd, pool=fwd.pool()):
-            g["losses"] = self.loss_and_backward(views, g["targets"])
-            self.fp.table_adam_step()
+            if self.overlap_adam():
+                g["losses"] = self.loss_and_backward(views, g["targets"], adam="graph")
+            else:
+                g["losses"] = self.loss_and_backward(views, g["targets"])
+                self.fp.table_adam_step()
         # launches recorded into the graphs, counted again at every replay
         g["kernels"] = nat.launch_count() - n0
         nat.lib().gs_note_launches(-g["kernels"])

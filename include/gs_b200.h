@@ -311,6 +311,20 @@ GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int6
                       float chi_squared_threshold, float *grad_points_img,
                       float *grad_splat, void *stream);
 
+/* gs_preprocess_backward_views for the Gaussians first .. first + count - 1
+ * of n_total: parameter and gradient pointers are those of all n_total
+ * Gaussians (offset here), the per-view upstream arrays hold n_total
+ * Gaussians per view. Lets the backward of one range of Gaussians overlap the
+ * optimizer step of the previous range. */
+GS_API int gs_preprocess_backward_views_range(
+    int n_total, int first, int count, int num_views, const float *means, const float *scales,
+    const float *quats, const float *opacities, const float *sh_dc, const float *sh_rest,
+    const float *world_to_cameras, const float *intrinsics, const float *camera_positions,
+    int width, int height, int sh_sigmoid, int activate, int accumulate, const uint8_t *mask,
+    const float *grad_points_img, int gp_stride, const float *grad_splat, int gs_stride,
+    float *grad_means, float *grad_scales, float *grad_quats, float *grad_opacities,
+    float *grad_dc, float *grad_rest, void *stream);
+
 /* Fused preprocess backward: projection, covariance and SH chain for every
  * Gaussian (zeros for culled ones), writing every output element. The
  * upstream gradients are read with element strides (so column views of a
@@ -392,6 +406,17 @@ GS_API int gs_adam_table(int64_t n, int num_groups, const int64_t *group_ends, c
 GS_API int gs_adam_step_table(int64_t n, float *params, const float *grads, float *exp_avg,
                               float *exp_avg_sq, const void *table_dev, float beta1, float beta2,
                               void *stream);
+
+/* The same Adam update over num_ranges (<= 8) disjoint element ranges of the
+ * flat buffers, range r (starts[r], counts[r]: multiples of 4, host arrays)
+ * using group r of the device table (gs_adam_table's layout): the slices of
+ * the six groups that hold a range of Gaussians, updated as soon as their
+ * gradients are complete while the next range's are computed. Same update
+ * and status gating as gs_adam_step. */
+GS_API int gs_adam_step_ranges(float *params, const float *grads, float *exp_avg,
+                               float *exp_avg_sq, int num_ranges, const int64_t *starts,
+                               const int64_t *counts, const void *table_dev, float beta1,
+                               float beta2, void *stream);
 
 /* The reference's per-view training loss on the raw blended image (H*W*3 =
  * n floats): rendered = clamp(raw, 0, 1) * 255 (wrapper.py:294),

@@ -7,7 +7,7 @@ import importlib
 import pytest
 import torch
 
-from test_gpu_layout_capped import _same_step, _scene, _trainer
+from test_gpu_layout_capped import GROUPS, _same_step, _scene, _trainer
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
@@ -81,3 +81,28 @@ def test_graph_step_with_host_targets_and_new_cameras(gs):
     la = a.step_graph(cams2.cpu().pin_memory(), K.cpu(), host, check_status=True)
     torch.cuda.synchronize()
     assert torch.allclose(la, lr, rtol=1e-6, atol=0)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_adam_overlapped_with_the_backward_equals_one_launch(gs, graph):
+    """adam_overlap: the preprocess backward in ranges of Gaussians, each
+    range's Adam (gs_adam_step_ranges over its slices of the six groups) on
+    a second stream -- the same update as one Adam launch after the whole
+    backward (up to the blend's atomics), eagerly and replayed from graphs."""
+    cfg, K, cams, targets = _scene(gs, 2, seed=9)
+    a = _trainer(gs, cfg, "binned")
+    a.adam_overlap = True
+    r = _trainer(gs, cfg, "binned")
+    assert a.overlap_adam() and not r.overlap_adam()
+    run = a.step_graph if graph else a.step
+    for step in range(3):
+        la = run(cams, K, targets, check_status=True).clone()
+        lr = r.step(cams, K, targets)
+        torch.cuda.synchronize()
+        if step == 0:
+            _same_step(a, r)
+        assert torch.allclose(la, lr, rtol=1e-4, atol=0)
+    assert a.fp.step_count == r.fp.step_count == 3
+    for k in GROUPS:
+        d = (a.params[k] - r.params[k]).abs().max().item()
+        assert d <= 6.0 * a.fp.lrs[k], (k, d)

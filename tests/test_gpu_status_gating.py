@@ -54,22 +54,31 @@ def test_adam_skips_update_while_status_holds_an_error(gs):
     assert not torch.equal(tr.fp.data, before)
 
 
-def test_step_raises_in_the_same_step_with_parameters_unchanged(gs):
+@pytest.mark.parametrize("overlap", [True, False])
+def test_step_raises_in_the_same_step_with_parameters_unchanged(gs, overlap):
+    """Whether Adam runs range by range behind the backward (the one-GPU
+    default) or as one launch after it."""
     tr, w2c, K, tg = small_trainer(gs)
+    tr.adam_overlap = overlap
+    assert tr.overlap_adam() == overlap
     tr.step(w2c, K, tg)
     before = tr.fp.data.clone()
-    clean_step = tr.fp.step
+    m_before = tr.fp.exp_avg.clone()
+    steps_before = tr.fp.step_count
+    clean = tr.loss_and_backward
 
-    def step_after_a_failed_wait():
-        plant_timeout()  # as if a bounded wait of this step had given up
-        clean_step()
+    def backward_after_a_failed_wait(*args, **kwargs):
+        plant_timeout()  # as if a bounded wait of this step's layout had given up
+        return clean(*args, **kwargs)
 
-    tr.fp.step = step_after_a_failed_wait
+    tr.loss_and_backward = backward_after_a_failed_wait
     with pytest.raises(nat.NativeError) as e:
         tr.step(w2c, K, tg)
     assert e.value.code == nat.GS_ERR_DEVICE_TIMEOUT
     assert torch.equal(tr.fp.data, before)
-    tr.fp.step = clean_step
+    assert torch.equal(tr.fp.exp_avg, m_before)
+    tr.loss_and_backward = clean
+    tr.fp.step_count = steps_before  # the failed step's update did not happen
     tr.step(w2c, K, tg)  # the next step runs normally
     assert not torch.equal(tr.fp.data, before)
 
