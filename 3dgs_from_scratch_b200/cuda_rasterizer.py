@@ -135,16 +135,42 @@ def _read_total(total_dev, dev):
     return int(host.item())
 
 
+# The binned layout (gs_tile_bins) is used while the pairs average at most
+# this many per tile: its per-tile sorts are cheap for short lists; longer
+# lists go to the two stable sorts of gs_tile_layout. Both give the same
+# lists and offsets bit for bit.
+BIN_MAX_PAIRS_PER_TILE = 1024
+
+
 def tile_layout_from_counts(points_image, radii, depths, counts, total, width, height,
-                            return_keys=False):
+                            return_keys=False, method="auto"):
     """Tile layout (pairs sorted by tile then depth bits, and per-tile start
-    offsets) from the per-Gaussian tile counts and their total."""
+    offsets) from the per-Gaussian tile counts and their total. method:
+    "sort" (gs_tile_layout, the two stable sorts; also whenever the keys are
+    returned), "bins" (gs_tile_bins) or "auto" (bins while the pairs average
+    at most BIN_MAX_PAIRS_PER_TILE per tile)."""
+    if method not in ("auto", "sort", "bins"):
+        raise ValueError(f"unknown tile layout method {method!r}")
     dev = points_image.device
     tx, ty = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+    n = points_image.shape[0]
+    bins = method == "bins" or (method == "auto" and total <= BIN_MAX_PAIRS_PER_TILE * tx * ty)
+    if bins and not return_keys and total > 0:
+        # capacity = the exact total, so the device-side count always fits
+        offsets = torch.empty((tx * ty + 1,), device=dev, dtype=torch.int32)
+        ids = torch.empty((total,), device=dev, dtype=torch.int32)
+        total_dev = torch.empty((1,), device=dev, dtype=torch.int64)
+        nbytes = int(nat.query("gs_tile_bins_scratch_bytes", n, int(total), int(width),
+                               int(height)))
+        scratch = torch.empty((max(nbytes, 8),), device=dev, dtype=torch.uint8)
+        nat.call("gs_tile_bins", n, points_image.data_ptr(), radii.data_ptr(), depths.data_ptr(),
+                 counts.data_ptr(), int(total), int(width), int(height), ids.data_ptr(),
+                 offsets.data_ptr(), total_dev.data_ptr(), scratch.data_ptr(), nbytes,
+                 nat.stream_ptr(dev))
+        return offsets[:tx * ty], ids
     indexing_offset = torch.empty((tx * ty,), device=dev, dtype=torch.int32)
     ids = torch.empty((total,), device=dev, dtype=torch.int32)
     keys = torch.empty((total,), device=dev, dtype=torch.int64) if return_keys else None
-    n = points_image.shape[0]
     nbytes = int(nat.query("gs_tile_layout_scratch_bytes", n, total, int(width), int(height)))
     scratch = torch.empty((nbytes,), device=dev, dtype=torch.uint8)
     nat.call("gs_tile_layout", n, points_image.data_ptr(), radii.data_ptr(), depths.data_ptr(),

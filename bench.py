@@ -473,7 +473,12 @@ class NativeBenchTrainer:
         self.targets = [t.to(device) for t in self.host_targets]
         self.host_cams = self.cams.cpu().pin_memory()
         self.host_K = self.K.cpu().pin_memory()
-        self.host_loss = torch.zeros(len(self.targets), dtype=torch.float64).pin_memory()
+        # two pinned loss buffers: step k's losses are read on the host while
+        # step k + 1 runs (see e2e_pending)
+        self.host_loss = [torch.zeros(len(self.targets), dtype=torch.float64).pin_memory()
+                          for _ in range(2)]
+        self._loss_slot = 0
+        self.e2e_pending = None
 
     def step(self, e2e=False, check=False):
         if e2e:
@@ -488,15 +493,22 @@ class NativeBenchTrainer:
             tg = self.host_targets
         else:
             cams, K, tg = self.cams, self.K, self.targets
-        # e2e reads the step's result back, so the status check after the
-        # optimizer rides on that synchronisation; the device-timed steps are
-        # queued back to back with no host synchronisation and their status
-        # is read after the timed region. With graph (one GPU) the step is
-        # replayed from CUDA graphs.
+        # Steps are queued with no host synchronisation (the warm-up steps
+        # read the status word, which sizes the layout buffers); the timed
+        # and e2e regions read it once at their end. With graph (one GPU)
+        # the step is replayed from CUDA graphs.
         run = self.nt.step_graph if self.graph else self.nt.step
-        losses = run(cams, K, tg, check_status=e2e or check)
+        losses = run(cams, K, tg, check_status=check)
         if e2e:
-            self.host_loss.copy_(losses, non_blocking=True)
+            # the losses go to a pinned host buffer; e2e_pending = (event,
+            # buffer) lets the caller read them once the copy has landed,
+            # after it has queued the next step
+            buf = self.host_loss[self._loss_slot]
+            self._loss_slot ^= 1
+            buf.copy_(losses, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            self.e2e_pending = (ev, buf)
         return losses
 
     def render_step(self, e2e=False):
@@ -599,6 +611,7 @@ def sub_config2(args, world, rank, device, steps=3, warmup=2):
                             graph=not args.no_graph)
     V = len(tr.targets)
     ms = timed_steps(tr.step, steps, warmup, world)
+    tr.graph = False  # the stage timer sees eager launches only (a replay is one graph launch)
     with StageTimer() as st:
         tr.step()
         torch.cuda.synchronize()
@@ -936,13 +949,34 @@ def main():
             run_step(e2e=True)
         torch.cuda.synchronize()
         barrier(world)
+        pipelined = isinstance(tr, NativeBenchTrainer) and not render_mode
+        loss_sum = 0.0
         with ClockSampler(local) as clk_e2e:
             t0 = time.perf_counter()
+            pending = None
             for _ in range(args.steps):
                 run_step(e2e=True)
-                torch.cuda.current_stream().synchronize()  # the step's result is on the host
+                if not pipelined:
+                    torch.cuda.current_stream().synchronize()  # the step's result is on the host
+                    continue
+                # a training loop's order: queue step k + 1, then read step
+                # k's losses on the host (their copy is in the stream behind
+                # step k), so the GPU does not wait for the host between steps
+                if pending is not None:
+                    pending[0].synchronize()
+                    loss_sum += float(pending[1].sum())
+                pending = tr.e2e_pending
+            if pending is not None:
+                pending[0].synchronize()
+                loss_sum += float(pending[1].sum())
+            torch.cuda.current_stream().synchronize()
             barrier(world)
             sec = max_over_ranks(time.perf_counter() - t0, world)
+        rc = nat.query("gs_check_status", nat.stream_ptr())
+        if rc:
+            raise nat.NativeError("e2e steps", rc, nat.lib().gs_last_cuda_error())
+        if pipelined and not math.isfinite(loss_sum):
+            raise RuntimeError(f"e2e steps: non-finite losses read back ({loss_sum})")
         if render_mode:
             h2d = V * (16 + 9) * 4
             d2h = V * cfg.width * cfg.height * 3
@@ -951,7 +985,9 @@ def main():
             d2h = V * 8
         e2e = {"value": total_views * args.steps / sec, "unit": unit,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "timing": "wall clock, max over ranks, right after the device-timed steps",
+               "timing": ("wall clock, max over ranks, right after the device-timed steps"
+                          + ("; the host reads step k's losses after queuing step k + 1"
+                             if pipelined else "; the host waits for each step's result")),
                "clocks": clk_e2e.summary()}
 
     # Per-stage times come from separate steps after the timed region, with

@@ -55,7 +55,7 @@ def test_capped_equals_host_sized_layout(gs, cfg_i, n, W, H, V, entry):
     b, totals, n = setup(gs, cfg, n, W, H, gs.scenes.orbit_cameras(cfg, V))
     for v, tot in enumerate(totals):
         r_off, r_ids = cr.tile_layout_from_counts(b["points"][v], b["radii"][v], b["depths"][v],
-                                                  b["counts"][v], tot, W, H)
+                                                  b["counts"][v], tot, W, H, method="sort")
         for cap in (tot, tot + 12_345):  # exact fit and headroom
             ids, offs, dtot, T = capped(b, v, n, cap, W, H, entry=entry)
             assert nat.query("gs_check_status", nat.stream_ptr()) == 0
@@ -66,6 +66,22 @@ def test_capped_equals_host_sized_layout(gs, cfg_i, n, W, H, V, entry):
             assert bool((ids[cap:] == -7).all()) and bool((offs[T + 1:] == -7).all())
 
 
+@pytest.mark.parametrize("cfg_i,n,W,H,V", CASES)
+def test_drop_in_layout_methods_agree(gs, cfg_i, n, W, H, V):
+    """tile_layout_from_counts (the layout render() and compute_tile_intersection
+    use): binned and two-sort forms give the same offsets (one per tile) and
+    ids, and "auto" gives them too."""
+    cfg = gs.scenes.CONFIGS[cfg_i]
+    b, totals, n = setup(gs, cfg, n, W, H, gs.scenes.orbit_cameras(cfg, V))
+    for v, tot in enumerate(totals):
+        args = (b["points"][v], b["radii"][v], b["depths"][v], b["counts"][v], tot, W, H)
+        s_off, s_ids = cr.tile_layout_from_counts(*args, method="sort")
+        for method in ("bins", "auto"):
+            off, ids = cr.tile_layout_from_counts(*args, method=method)
+            assert off.shape == s_off.shape and ids.shape == s_ids.shape, method
+            assert torch.equal(off, s_off) and torch.equal(ids, s_ids), (v, method)
+
+
 def test_bins_config3_clustered_4k_bit_exact(gs):
     """~100M pairs of clustered Gaussians at 3840x2160: buckets far above
     the on-chip chunk, sorted as chunks merged through global scratch."""
@@ -74,7 +90,8 @@ def test_bins_config3_clustered_4k_bit_exact(gs):
     tot = totals[0]
     assert tot > 50_000_000
     r_off, r_ids = cr.tile_layout_from_counts(b["points"][0], b["radii"][0], b["depths"][0],
-                                              b["counts"][0], tot, cfg.width, cfg.height)
+                                              b["counts"][0], tot, cfg.width, cfg.height,
+                                              method="sort")
     ids, offs, dtot, T = capped(b, 0, n, tot, cfg.width, cfg.height, guard=16, entry="bins")
     assert nat.query("gs_check_status", nat.stream_ptr()) == 0
     assert dtot == tot

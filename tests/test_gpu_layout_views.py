@@ -64,7 +64,7 @@ def check(gs, cfg, n, W, H, w2c, seed=0):
     start = 0
     for v, tot in enumerate(totals):
         r_off, r_ids = cr.tile_layout_from_counts(b["points"][v], b["radii"][v], b["depths"][v],
-                                                  b["counts"][v], tot, W, H)
+                                                  b["counts"][v], tot, W, H, method="sort")
         assert torch.equal(offs[v], r_off), f"view {v} offsets"
         assert torch.equal(ids[start:start + tot], r_ids), f"view {v} ids"
         start += tot
