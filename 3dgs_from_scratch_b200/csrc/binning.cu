@@ -488,8 +488,12 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
 //
 // A bucket of up to kRadChunk entries is sorted by one 256-thread block as a
 // stable LSD radix sort of its 32-bit depth keys (8-bit digits) in shared
-// memory, over only the low bits in which the bucket's keys differ (their
-// XOR with the first key, OR-reduced: typically 3 passes). Each pass ranks
+// memory. The keys are sorted as their offsets from the bucket's smallest
+// key (an order-preserving shift for unsigned keys), so only the bits of the
+// bucket's key range are sorted: a tile's depths spanning 5.0 to 12.0 give
+// offsets below 2^24, 3 passes, where the bits in which the keys differ
+// (their XOR) reach bit 24 and would take 4. Entries with an invalid id, and
+// the padding up to whole warps, take a key above every valid one. Each pass ranks
 // the digits warp by warp -- lanes with equal digits found with one ballot
 // per digit bit, items taken in position order (position 256 w + 32 k +
 // lane), so the ranking is stable -- scans the per-warp digit counts and
@@ -507,7 +511,7 @@ struct RadSmem {
   uint32_t whist[kRadWarps][256];
   uint32_t gbase[256];
   uint32_t tmp[kRadWarps + 1];
-  uint32_t diff;
+  uint32_t kmin, kmax, invalid;
 };
 
 __device__ __forceinline__ uint32_t rad_block_excl_scan(uint32_t x, uint32_t *s_tmp) {
@@ -545,31 +549,61 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   // largest key (sorts after every real key; stable, so real keys stay first)
   const int active_warps = (L + 32 * kRadItems - 1) / (32 * kRadItems);
   const int P = active_warps * 32 * kRadItems;
-  if (t == 0) S.diff = 0u;
-  __syncthreads();
-  uint32_t dif = 0;
-  uint32_t k0 = 0;
-  {
-    const int id0 = ids[beg];
-    k0 = (id0 >= 0 && id0 < n) ? __float_as_uint(depths[id0]) : 0xffffffffu;
+  if (t == 0) {
+    S.kmin = 0xffffffffu;
+    S.kmax = 0u;
+    S.invalid = 0u;
   }
+  __syncthreads();
+  uint32_t kmn = 0xffffffffu, kmx = 0u, bad = 0u;
   for (int p = t; p < P; p += kRadThreads) {
     uint32_t key = 0xffffffffu;
     int32_t val = -1;
     if (p < L) {
       val = ids[beg + p];
-      key = (val >= 0 && val < n) ? __float_as_uint(depths[val]) : 0xffffffffu;
-      dif |= key ^ k0;
+      if (val >= 0 && val < n) {
+        key = __float_as_uint(depths[val]);
+        kmn = min(kmn, key);
+        kmx = max(kmx, key);
+      } else {
+        bad = 1u;
+      }
     }
     S.key[0][p] = key;
     S.val[0][p] = val;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) dif |= __shfl_xor_sync(0xffffffffu, dif, o);
-  if (lane == 0 && dif) atomicOr(&S.diff, dif);
+  for (int o = 16; o > 0; o >>= 1) {
+    kmn = min(kmn, __shfl_xor_sync(0xffffffffu, kmn, o));
+    kmx = max(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if (lane == 0) {
+    atomicMin(&S.kmin, kmn);
+    atomicMax(&S.kmax, kmx);
+    if (bad) S.invalid = 1u;
+  }
   __syncthreads();
-  const uint32_t diff = S.diff;
-  const int bits = diff ? 32 - __clz(diff) : 0;
+  // sorted key = key - kmin for a valid entry, `sent` for an invalid one or
+  // padding; `bits` covers every sorted key. Padding sits after position L,
+  // so with no invalid entry it may tie the largest valid key (the sort is
+  // stable); an invalid entry needs a key above every valid one.
+  uint32_t kmin = S.kmin;
+  const uint32_t kmax = S.kmax;
+  const bool has_invalid = S.invalid != 0u;
+  int bits;
+  if (kmin > kmax) {  // no valid entry: every key is the sentinel
+    kmin = 0u;
+    bits = 0;
+  } else {
+    const uint64_t top = (uint64_t)(kmax - kmin) + (has_invalid ? 1u : 0u);
+    bits = top ? 64 - __clzll((long long)top) : 0;
+    if (bits > 32) {  // keys spanning the whole 32-bit range: sort them as they are
+      kmin = 0u;
+      bits = 32;
+    }
+  }
+  const uint32_t sent = bits >= 32 ? 0xffffffffu : ((1u << bits) - 1u);
   const int passes = (bits + 7) / 8;
   int cur = 0;
   for (int pass = 0; pass < passes; ++pass) {  // block-uniform
@@ -587,6 +621,7 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
         const int p = warp * 32 * kRadItems + q * 32 + (int)lane;
         key[q] = S.key[cur][p];
         val[q] = S.val[cur][p];
+        if (pass == 0) key[q] = ((uint32_t)val[q] < (uint32_t)n) ? key[q] - kmin : sent;
         const uint32_t d = (key[q] >> shift) & 0xffu;
         uint32_t peers = 0xffffffffu;
 #pragma unroll

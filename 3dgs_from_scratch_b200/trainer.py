@@ -505,15 +505,17 @@ class NativeTrainer:
         layout buffers and Adam's state; a pair count beyond the capacity
         (seen with check_status) grows the buffers, re-captures and repeats
         the step. Falls back to step() when graph_capable() is False.
-        Returns the per-view losses (a static device tensor, overwritten by
-        the next call)."""
+        Inputs may be device tensors or host tensors; host inputs in pinned
+        memory keep the call asynchronous (a pageable one is copied through
+        a staging buffer, which can block the host until the copy stream's
+        earlier work is done). Returns the per-view losses (a static device
+        tensor, overwritten by the next call)."""
         if not self.graph_capable():
             return self.step(world_to_cameras, intrinsics, targets, check_status=check_status)
         w2c = world_to_cameras.to(torch.float32)
         V = w2c.shape[0]
-        Ks = intrinsics.to(torch.float32)
-        if Ks.dim() == 2:
-            Ks = Ks.unsqueeze(0).expand(V, 3, 3)
+        K1 = intrinsics.to(torch.float32)
+        Ks = K1.unsqueeze(0).expand(V, 3, 3) if K1.dim() == 2 else K1
         key = (V, self.n, tuple(t.dtype for t in targets), tuple(targets[0].shape))
         g = getattr(self, "_graph", None)
         if g is None or g["key"] != key or g["cap"] != (self._cap[0] if self._cap else None):
@@ -536,7 +538,14 @@ class NativeTrainer:
             cs.wait_event(g["bwd_done"])
         with torch.cuda.stream(cs):
             g["w2c"].copy_(w2c, non_blocking=True)
-            g["K"].copy_(Ks, non_blocking=True)
+            if K1.dim() == 2 and not K1.is_cuda:
+                # one intrinsic for every view: the 3x3 goes to the device and
+                # is broadcast there (a broadcast host tensor would be copied
+                # through pageable memory, which blocks the host until the
+                # copy stream's earlier work -- the previous step -- is done)
+                g["K"].copy_(K1.to(self.device, non_blocking=True).expand(V, 3, 3))
+            else:
+                g["K"].copy_(Ks, non_blocking=True)
             cams_ready = cs.record_event()
         cur.wait_event(cams_ready)
         g["fwd"].replay()  # queued before the rest of the host work of the step
