@@ -495,8 +495,9 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
 // (their XOR) reach bit 24 and would take 4. Entries with an invalid id, and
 // the padding up to whole warps, take a key above every valid one. Each pass ranks
 // the digits warp by warp -- lanes with equal digits found with one ballot
-// per digit bit, items taken in position order (position 256 w + 32 k +
-// lane), so the ranking is stable -- scans the per-warp digit counts and
+// per digit bit, items taken in position order (position 32 (ipw w + k) +
+// lane for item k of lane `lane` in warp w, ipw items per lane), so the
+// ranking is stable -- scans the per-warp digit counts and
 // scatters into the other buffer. Equal depth keys keep the bucket's
 // (arbitrary) order, so runs of equal keys are then put in id order: the
 // (depth bits, id) order of the reference's stable 64-bit sort.
@@ -545,10 +546,12 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  // positions [0, P): whole warps' worth of items, the tail padded with the
-  // largest key (sorts after every real key; stable, so real keys stay first)
-  const int active_warps = (L + 32 * kRadItems - 1) / (32 * kRadItems);
-  const int P = active_warps * 32 * kRadItems;
+  // positions [0, P): ipw items per lane in every warp (the bucket spread
+  // over all warps, so a warp ranks as few items as the bucket allows), the
+  // tail padded with a key that sorts after every real key (stable, so the
+  // real keys stay first)
+  const int ipw = (L + kRadThreads - 1) / kRadThreads;  // 1..kRadItems, block-uniform
+  const int P = ipw * kRadThreads;
   if (t == 0) {
     S.kmin = 0xffffffffu;
     S.kmax = 0u;
@@ -612,13 +615,13 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
     __syncthreads();
     uint32_t key[kRadItems], rank[kRadItems];
     int32_t val[kRadItems];
-    const bool wact = warp < active_warps;
-    if (wact) {
+    {
       uint32_t lead_old[kRadItems];
       uint8_t leader_of[kRadItems];
 #pragma unroll
       for (int q = 0; q < kRadItems; ++q) {
-        const int p = warp * 32 * kRadItems + q * 32 + (int)lane;
+        if (q >= ipw) break;  // warp-uniform
+        const int p = warp * 32 * ipw + q * 32 + (int)lane;
         key[q] = S.key[cur][p];
         val[q] = S.val[cur][p];
         if (pass == 0) key[q] = ((uint32_t)val[q] < (uint32_t)n) ? key[q] - kmin : sent;
@@ -639,7 +642,7 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
       }
 #pragma unroll
       for (int q = 0; q < kRadItems; ++q)
-        rank[q] += __shfl_sync(0xffffffffu, lead_old[q], leader_of[q]);
+        if (q < ipw) rank[q] += __shfl_sync(0xffffffffu, lead_old[q], leader_of[q]);
     }
     __syncthreads();
     {  // thread t owns digit t: warp prefixes, then the digit prefix
@@ -654,9 +657,10 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
       S.gbase[d] = rad_block_excl_scan(c, S.tmp);
     }
     __syncthreads();
-    if (wact) {
+    {
 #pragma unroll
       for (int q = 0; q < kRadItems; ++q) {
+        if (q >= ipw) break;
         const uint32_t d = (key[q] >> shift) & 0xffu;
         const uint32_t pos = S.gbase[d] + S.whist[warp][d] + rank[q];
         S.key[cur ^ 1][pos] = key[q];
