@@ -693,7 +693,10 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
 
 // One block per tile sorts buckets of up to kRadChunk entries; longer
 // buckets are listed (ctl->num_long, long_tiles) for bin_sort_long_kernel.
-__global__ void __launch_bounds__(kRadThreads) bin_sort_kernel(const int32_t *__restrict__ offsets,
+#ifndef GS_BIN_SORT_MINB
+#define GS_BIN_SORT_MINB 4  // blocks per SM the bucket sort's registers target (64 each)
+#endif
+__global__ void __launch_bounds__(kRadThreads, GS_BIN_SORT_MINB) bin_sort_kernel(const int32_t *__restrict__ offsets,
                                                                const float *__restrict__ depths,
                                                                int n, int32_t *__restrict__ ids,
                                                                Ctl *ctl,
