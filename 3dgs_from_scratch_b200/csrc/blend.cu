@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kBlendThreads, GS_FWD_MINB) blend_forward_kern
     const float4 *__restrict__ splat, const float *__restrict__ conic,
     const float *__restrict__ opac, const float *__restrict__ colors, int width, int height,
     float alpha_thr, float trans_thr, float chi_thr, float *__restrict__ image,
-    float *__restrict__ final_t, int32_t *__restrict__ pixel_end) {
+    float *__restrict__ final_t, int32_t *__restrict__ pixel_end, uint8_t *__restrict__ reach) {
   __shared__ float4 s_g0[kBatch];
   __shared__ float4 s_g1[kBatch];
   __shared__ float s_b[kBatch];
@@ -294,8 +294,10 @@ __global__ void __launch_bounds__(kBlendThreads, GS_FWD_MINB) blend_forward_kern
         s_g0[slot] = r.g0;
         s_g1[slot] = r.g1;
         s_b[slot] = r.b;
-        s_mask[slot] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
-                                           alpha_thr, chi_thr, tile_x0, tile_y0);
+        const uint8_t m = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
+                                              alpha_thr, chi_thr, tile_x0, tile_y0);
+        s_mask[slot] = m;
+        if (reach != nullptr) reach[k] = m;  // kept for the backward
       }
     }
     __syncthreads();
@@ -590,7 +592,8 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
     const float *__restrict__ grad_image, const float *__restrict__ final_t,
     const int32_t *__restrict__ pixel_end, int width, int height, float alpha_thr,
     float trans_thr, float chi_thr, float *__restrict__ g_points, float *__restrict__ g_splat,
-    float *__restrict__ g_conic, float *__restrict__ g_opac, float *__restrict__ g_colors) {
+    float *__restrict__ g_conic, float *__restrict__ g_opac, float *__restrict__ g_colors,
+    const uint8_t *__restrict__ reach) {
   __shared__ float4 s_g0[kBatch];
   __shared__ float4 s_g1[kBatch];
   __shared__ float s_b[kBatch];
@@ -669,8 +672,12 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
         s_g1[slot] = r.g1;
         s_b[slot] = r.b;
         s_id[slot] = id;
-        s_mask[slot] = (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
-                                           alpha_thr, chi_thr, tile_x0, tile_y0);
+        // the forward's masks when it kept them (every entry below the
+        // tile's largest pixel end was loaded, so its mask was written)
+        s_mask[slot] = reach != nullptr
+                           ? __ldg(reach + k)
+                           : (uint8_t)reach_mask(r.g0.x, r.g0.y, r.g0.z, r.g0.w, r.g1.x, r.g1.y,
+                                                 alpha_thr, chi_thr, tile_x0, tile_y0);
       }
 #pragma unroll
       for (int q = 0; q < 9; ++q) s_acc[slot * 9 + q] = 0.f;
@@ -832,7 +839,7 @@ extern "C" int gs_rasterize(int num_tiles, const int32_t *indexing_offset, int64
   blend_forward_kernel<false, true><<<num_tiles, kBlendThreads, 0, as_stream(stream)>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, width, height, alpha_threshold, transmittance_threshold,
-      chi_squared_threshold, image, work_final_t, work_pixel_end);
+      chi_squared_threshold, image, work_final_t, work_pixel_end, nullptr);
   count_launch();
   return launch_status();
 }
@@ -859,13 +866,13 @@ extern "C" int gs_rasterize_backward(int num_tiles, const int32_t *indexing_offs
   blend_forward_kernel<false, false><<<num_tiles, kBlendThreads, 0, st>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, width, height, alpha_threshold, transmittance_threshold,
-      chi_squared_threshold, nullptr, work_final_t, work_pixel_end);
+      chi_squared_threshold, nullptr, work_final_t, work_pixel_end, nullptr);
   count_launch();
   blend_backward_kernel<false><<<num_tiles, kBlendThreads, 0, st>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, grad_image, work_final_t, work_pixel_end, width, height,
       alpha_threshold, transmittance_threshold, chi_squared_threshold, grad_points_img, nullptr,
-      grad_conic, grad_opacities, grad_colors);
+      grad_conic, grad_opacities, grad_colors, nullptr);
   count_launch();
   return launch_status();
 }
@@ -875,7 +882,7 @@ extern "C" int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, i
                                 const float *splat, int width, int height,
                                 float alpha_threshold, float transmittance_threshold,
                                 float chi_squared_threshold, float *image, float *final_t,
-                                int32_t *pixel_end, void *stream) {
+                                int32_t *pixel_end, uint8_t *reach, void *stream) {
   if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15)) return GS_ERR_INVALID_ARGUMENT;
@@ -885,7 +892,7 @@ extern "C" int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, i
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       reinterpret_cast<const float4 *>(splat), nullptr, nullptr, nullptr, width, height,
       alpha_threshold, transmittance_threshold, chi_squared_threshold, image, final_t,
-      pixel_end);
+      pixel_end, reach);
   count_launch();
   return launch_status();
 }
@@ -896,7 +903,8 @@ extern "C" int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, 
                                  const float *final_t, const int32_t *pixel_end, int width,
                                  int height, float alpha_threshold,
                                  float transmittance_threshold, float chi_squared_threshold,
-                                 float *grad_points_img, float *grad_splat, void *stream) {
+                                 float *grad_points_img, float *grad_splat,
+                                 const uint8_t *reach, void *stream) {
   if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15) || ((uintptr_t)grad_points_img & 7) ||
@@ -908,7 +916,7 @@ extern "C" int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, 
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       reinterpret_cast<const float4 *>(splat), nullptr, nullptr, nullptr, grad_image, final_t,
       pixel_end, width, height, alpha_threshold, transmittance_threshold, chi_squared_threshold,
-      grad_points_img, grad_splat, nullptr, nullptr, nullptr);
+      grad_points_img, grad_splat, nullptr, nullptr, nullptr, reach);
   count_launch();
   return launch_status();
 }

@@ -96,7 +96,7 @@ uint32_t *device_status_word() {
 
 using namespace gs;
 
-extern "C" int gs_version(void) { return 1; }
+extern "C" int gs_version(void) { return 2; }
 
 extern "C" int gs_last_cuda_error(void) { return g_last_cuda_error.load(); }
 

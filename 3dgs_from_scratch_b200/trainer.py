@@ -190,6 +190,7 @@ class NativeTrainer:
                     k = v % self.num_streams
                     cap, _, bufs = self._cap
                     s["ids"], s["offsets"] = bufs["ids"][v], bufs["offsets"][v]
+                    s["reach"] = bufs["reach"][v]
                     s["total_dev"] = bufs["totals"][v:v + 1]
                     scratch = bufs["scratch"][k]
                     nat.call(self._capacity_entry, n, s["points"].data_ptr(),
@@ -204,6 +205,7 @@ class NativeTrainer:
                     if self.layout != "batched":
                         s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
                             s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
+                    s["reach"] = torch.empty((max(total, 1),), device=dev, dtype=torch.uint8)
                 s["image"] = torch.empty((H, W, 3), **f)
                 s["final_t"] = torch.empty((H * W,), **f)
                 s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
@@ -211,7 +213,8 @@ class NativeTrainer:
                          s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(),
                          W, H, o["alpha_threshold"], o["transmittance_threshold"],
                          o["chi_squared_threshold"], s["image"].data_ptr(),
-                         s["final_t"].data_ptr(), s["pixel_end"].data_ptr(), vst)
+                         s["final_t"].data_ptr(), s["pixel_end"].data_ptr(),
+                         s["reach"].data_ptr(), vst)
         self._join()
         return views
 
@@ -253,6 +256,8 @@ class NativeTrainer:
         nbytes = int(nat.query(query, n, cap, self.width, self.height))
         bufs = dict(
             ids=[torch.empty((cap,), device=dev, dtype=torch.int32) for _ in range(V)],
+            # per list entry: the reach mask the forward blend keeps for the backward
+            reach=[torch.empty((cap,), device=dev, dtype=torch.uint8) for _ in range(V)],
             offsets=[torch.empty((T + 1,), device=dev, dtype=torch.int32) for _ in range(V)],
             totals=torch.zeros((V,), device=dev, dtype=torch.int64),
             scratch=[torch.empty((max(nbytes, 1),), device=dev, dtype=torch.uint8)
@@ -436,7 +441,7 @@ class NativeTrainer:
                  s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
                  s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
                  o["transmittance_threshold"], o["chi_squared_threshold"], g_points.data_ptr(),
-                 g_splat.data_ptr(), st)
+                 g_splat.data_ptr(), s["reach"].data_ptr(), st)
 
     def check_status(self):
         """Synchronise the device and raise NativeError if a kernel of this

@@ -45,7 +45,8 @@ extern "C" {
 /* Tile edge in pixels; the reference hard-codes 16 (src/cuda/wrapper.py:267). */
 #define GS_TILE 16
 
-/* Library version, last CUDA error code seen, and the number of kernels this
+/* Library version (2: gs_blend_forward / gs_blend_backward take the reach
+ * buffer), last CUDA error code seen, and the number of kernels this
  * library has launched since load (for launch accounting in benchmarks). */
 GS_API int gs_version(void);
 GS_API int gs_last_cuda_error(void);
@@ -293,23 +294,30 @@ GS_API int gs_preprocess_forward(int n, const float *means, const float *scales,
  * transmittance and end index (one past its last contributing list entry).
  * Every pixel of the image (H,W,3) is written. total is the number of list
  * entries, or -1 when indexing_offset holds num_tiles + 1 entries whose last
- * is the end of the last tile's list (as gs_tile_layout_capped writes it). */
+ * is the end of the last tile's list (as gs_tile_layout_capped writes it).
+ * reach: NULL, or one byte per list entry (as many as ids_sorted holds):
+ * the forward stores there, for the entries it visits, which 8x8 pixel
+ * blocks of its tile the entry's Gaussian can reach, and gs_blend_backward
+ * given the same buffer (layout and splat records unchanged) reads them
+ * instead of recomputing them. */
 GS_API int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                      const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                      int width, int height, float alpha_threshold,
                      float transmittance_threshold, float chi_squared_threshold,
-                     float *image, float *final_t, int32_t *pixel_end, void *stream);
+                     float *image, float *final_t, int32_t *pixel_end, uint8_t *reach,
+                     void *stream);
 
 /* Blend backward: gradient outputs (grad_points_img (N,2), grad_splat (N,8))
  * must be zeroed by the caller (they are accumulated). total as for
- * gs_blend_forward (-1: the end is indexing_offset[num_tiles]). */
+ * gs_blend_forward (-1: the end is indexing_offset[num_tiles]). reach: NULL
+ * (the masks are recomputed) or the buffer the forward of this view filled. */
 GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                       const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                       const float *grad_image, const float *final_t,
                       const int32_t *pixel_end, int width, int height,
                       float alpha_threshold, float transmittance_threshold,
                       float chi_squared_threshold, float *grad_points_img,
-                      float *grad_splat, void *stream);
+                      float *grad_splat, const uint8_t *reach, void *stream);
 
 /* gs_preprocess_backward_views for the Gaussians first .. first + count - 1
  * of n_total: parameter and gradient pointers are those of all n_total

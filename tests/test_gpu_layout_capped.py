@@ -177,3 +177,37 @@ def test_trainer_repeats_a_step_that_overflows(gs, layout):
     assert a._cap[0] > 1024
     assert torch.allclose(la, lr, rtol=1e-9, atol=0)
     _same_step(a, r)
+
+
+@pytest.mark.parametrize("cfg_i,n,W,H", [(0, 20_000, 256, 256), (1, None, 1920, 1080)])
+def test_blend_backward_reading_kept_reach_masks(gs, cfg_i, n, W, H):
+    """gs_blend_backward given the reach masks its forward kept gives the
+    gradients it gives when it recomputes them: the same (pixel, entry)
+    pairs contribute, so the two agree up to the order of the atomics."""
+    tr_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
+    cfg = gs.scenes.CONFIGS[cfg_i]
+    raw = {k: v.to(DEV) for k, v in gs.scenes.make_gaussians(cfg, seed=4, n=n).items()}
+    tr = tr_mod.NativeTrainer(raw, W, H, layout="binned")
+    K = gs.scenes.intrinsic_for(cfg, W, H).to(DEV)
+    cams = gs.scenes.orbit_cameras(cfg, 1).to(DEV)
+    views = tr.render_views(cams, K)
+    s, o, n = views[0], tr.opts, tr.n
+    g = torch.Generator(device=DEV).manual_seed(11)
+    grad_img = torch.randn((H, W, 3), device=DEV, generator=g)
+    out = []
+    for reach in (s["reach"], None):
+        gp = torch.zeros((n, 2), device=DEV)
+        gsp = torch.zeros((n, 8), device=DEV)
+        nat.call("gs_blend_backward", tr.tx * tr.ty, s["offsets"].data_ptr(), s["total"],
+                 s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(),
+                 grad_img.data_ptr(), s["final_t"].data_ptr(), s["pixel_end"].data_ptr(), W, H,
+                 o["alpha_threshold"], o["transmittance_threshold"],
+                 o["chi_squared_threshold"], gp.data_ptr(), gsp.data_ptr(),
+                 reach.data_ptr() if reach is not None else None, nat.stream_ptr())
+        out.append((gp, gsp))
+    torch.cuda.synchronize()
+    assert nat.query("gs_check_status", nat.stream_ptr()) == 0
+    for a, b in zip(out[0], out[1]):
+        scale = b.abs().max().item()
+        assert scale > 0
+        assert (a - b).abs().max().item() <= 1e-5 * scale
