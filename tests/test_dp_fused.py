@@ -151,7 +151,7 @@ def _tensors(n, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["p2p", "auto"])
+@pytest.mark.parametrize("mode", ["p2p", "multicast", "auto"])
 def test_two_ranks_fused_step_matches_allreduce_adam(tmp_path, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
