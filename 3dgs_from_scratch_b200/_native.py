@@ -68,8 +68,9 @@ SIGNATURES = {
                                   P, P]),
     "gs_preprocess_forward": (I, [I, P, P, P, P, P, P, P, P, P, F, F, F, F, F, I, I, I, I, P, P,
                                   P, P, P, P, P, P]),
-    "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P, P]),
-    "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P, P]),
+    "gs_blend_forward": (I, [I, P, I64, P, I, P, P, I, I, F, F, F, P, P, P, P, P, P]),
+    "gs_blend_backward": (I, [I, P, I64, P, I, P, P, P, P, P, I, I, F, F, F, P, P, P, P, P]),
+    "gs_tile_order": (I, [I, P, I64, P, P]),
     "gs_l1_loss_grad": (I, [I64, P, P, I, P, P, P]),
     "gs_adam_table_bytes": (SZ, []),
     "gs_adam_table": (I, [I64, I, P, P, P, F, F, I64, P, SZ]),

@@ -250,13 +250,15 @@ __global__ void __launch_bounds__(kBlendThreads, GS_FWD_MINB) blend_forward_kern
     const float4 *__restrict__ splat, const float *__restrict__ conic,
     const float *__restrict__ opac, const float *__restrict__ colors, int width, int height,
     float alpha_thr, float trans_thr, float chi_thr, float *__restrict__ image,
-    float *__restrict__ final_t, int32_t *__restrict__ pixel_end, uint8_t *__restrict__ reach) {
+    float *__restrict__ final_t, int32_t *__restrict__ pixel_end, uint8_t *__restrict__ reach,
+    const int32_t *__restrict__ order) {
   __shared__ float4 s_g0[kBatch];
   __shared__ float4 s_g1[kBatch];
   __shared__ float s_b[kBatch];
   __shared__ uint8_t s_mask[kBatch];
 
-  const int tile = blockIdx.x;
+  // block b blends tile order[b] (longest lists first), or tile b
+  const int tile = order != nullptr ? __ldg(order + blockIdx.x) : (int)blockIdx.x;
   const int tx = tiles_x_of(width);
   const int tile_x0 = (tile % tx) * GS_TILE, tile_y0 = (tile / tx) * GS_TILE;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -593,7 +595,7 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
     const int32_t *__restrict__ pixel_end, int width, int height, float alpha_thr,
     float trans_thr, float chi_thr, float *__restrict__ g_points, float *__restrict__ g_splat,
     float *__restrict__ g_conic, float *__restrict__ g_opac, float *__restrict__ g_colors,
-    const uint8_t *__restrict__ reach) {
+    const uint8_t *__restrict__ reach, const int32_t *__restrict__ order) {
   __shared__ float4 s_g0[kBatch];
   __shared__ float4 s_g1[kBatch];
   __shared__ float s_b[kBatch];
@@ -602,7 +604,8 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
   __shared__ float s_acc[9 * kBatch];
   __shared__ int s_max_end;
 
-  const int tile = blockIdx.x;
+  // block b blends tile order[b] (longest lists first), or tile b
+  const int tile = order != nullptr ? __ldg(order + blockIdx.x) : (int)blockIdx.x;
   const int tx = tiles_x_of(width);
   const int tile_x0 = (tile % tx) * GS_TILE, tile_y0 = (tile / tx) * GS_TILE;
   const int t = threadIdx.x, warp = t >> 5;
@@ -817,9 +820,94 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
   }
 }
 
+// Blend order of the tiles: longest lists first, so that the blend's last
+// wave holds short tiles instead of a few long ones that run on while most
+// SMs idle (list scheduling, longest first). One block: a counting sort of
+// the tiles by a length class that grows with the list length (exact up to
+// 7, then 8 steps per power of two), classes in descending order; tiles of
+// one class in any order.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderClasses = 256;
+
+__device__ __forceinline__ int length_class(int len) {
+  if (len < 8) return max(len, 0);
+  const int e = 31 - __clz(len);  // >= 3
+  return (e << 3) | ((len >> (e - 3)) & 7);  // <= 8 * 30 + 7
+}
+
+__global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
+    int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
+    int32_t *__restrict__ order) {
+  __shared__ uint32_t s_count[kOrderClasses];
+  const int t = threadIdx.x;
+  for (int c = t; c < kOrderClasses; c += kOrderThreads) s_count[c] = 0u;
+  __syncthreads();
+  auto cls_of = [&](int tile) {
+    const int b = offsets[tile];
+    const int e = (tile + 1 < num_tiles) ? offsets[tile + 1]
+                                         : (total >= 0 ? (int)total : offsets[num_tiles]);
+    return kOrderClasses - 1 - length_class(e - b);  // longest first
+  };
+  // lanes of a warp with the same class add once (many tiles share a class)
+  const int lane = t & 31;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const int rounds = (num_tiles + kOrderThreads - 1) / kOrderThreads;  // block-uniform
+  for (int r = 0; r < rounds; ++r) {
+    const int tile = r * kOrderThreads + t;
+    const int c = tile < num_tiles ? cls_of(tile) : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, c);
+    if (c >= 0 && (peers & lt_mask) == 0u) atomicAdd(&s_count[c], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+  if (t < 32) {  // exclusive scan of the 256 class counts by one warp, 8 per lane
+    uint32_t v[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = s_count[t * 8 + i];
+      sum += v[i];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (t >= o) incl += y;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s_count[t * 8 + i] = run;
+      run += v[i];
+    }
+  }
+  __syncthreads();
+  for (int r = 0; r < rounds; ++r) {
+    const int tile = r * kOrderThreads + t;
+    const int c = tile < num_tiles ? cls_of(tile) : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, c);
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (c >= 0 && lane == leader) base = atomicAdd(&s_count[c], (uint32_t)__popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (c >= 0) order[base + __popc(peers & lt_mask)] = tile;
+  }
+}
+static_assert(kOrderClasses == 32 * 8, "the class scan gives each lane 8 classes");
+
 }  // namespace gs
 
 using namespace gs;
+
+extern "C" int gs_tile_order(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                             int32_t *order, void *stream) {
+  if (num_tiles < 0 || total < -1 || total >= (1ll << 31) || indexing_offset == nullptr ||
+      order == nullptr)
+    return GS_ERR_INVALID_ARGUMENT;
+  if (num_tiles == 0) return GS_OK;
+  tile_order_kernel<<<1, kOrderThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      num_tiles, indexing_offset, total, order);
+  count_launch();
+  return launch_status();
+}
 
 static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -839,7 +927,7 @@ extern "C" int gs_rasterize(int num_tiles, const int32_t *indexing_offset, int64
   blend_forward_kernel<false, true><<<num_tiles, kBlendThreads, 0, as_stream(stream)>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, width, height, alpha_threshold, transmittance_threshold,
-      chi_squared_threshold, image, work_final_t, work_pixel_end, nullptr);
+      chi_squared_threshold, image, work_final_t, work_pixel_end, nullptr, nullptr);
   count_launch();
   return launch_status();
 }
@@ -866,13 +954,13 @@ extern "C" int gs_rasterize_backward(int num_tiles, const int32_t *indexing_offs
   blend_forward_kernel<false, false><<<num_tiles, kBlendThreads, 0, st>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, width, height, alpha_threshold, transmittance_threshold,
-      chi_squared_threshold, nullptr, work_final_t, work_pixel_end, nullptr);
+      chi_squared_threshold, nullptr, work_final_t, work_pixel_end, nullptr, nullptr);
   count_launch();
   blend_backward_kernel<false><<<num_tiles, kBlendThreads, 0, st>>>(
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       nullptr, conic, opacities, colors, grad_image, work_final_t, work_pixel_end, width, height,
       alpha_threshold, transmittance_threshold, chi_squared_threshold, grad_points_img, nullptr,
-      grad_conic, grad_opacities, grad_colors, nullptr);
+      grad_conic, grad_opacities, grad_colors, nullptr, nullptr);
   count_launch();
   return launch_status();
 }
@@ -882,7 +970,8 @@ extern "C" int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, i
                                 const float *splat, int width, int height,
                                 float alpha_threshold, float transmittance_threshold,
                                 float chi_squared_threshold, float *image, float *final_t,
-                                int32_t *pixel_end, uint8_t *reach, void *stream) {
+                                int32_t *pixel_end, uint8_t *reach, const int32_t *tile_order,
+                                void *stream) {
   if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15)) return GS_ERR_INVALID_ARGUMENT;
@@ -892,7 +981,7 @@ extern "C" int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, i
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       reinterpret_cast<const float4 *>(splat), nullptr, nullptr, nullptr, width, height,
       alpha_threshold, transmittance_threshold, chi_squared_threshold, image, final_t,
-      pixel_end, reach);
+      pixel_end, reach, tile_order);
   count_launch();
   return launch_status();
 }
@@ -904,7 +993,8 @@ extern "C" int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, 
                                  int height, float alpha_threshold,
                                  float transmittance_threshold, float chi_squared_threshold,
                                  float *grad_points_img, float *grad_splat,
-                                 const uint8_t *reach, void *stream) {
+                                 const uint8_t *reach, const int32_t *tile_order,
+                                 void *stream) {
   if (num_tiles < 0 || n < 0 || width <= 0 || height <= 0 || total < -1 || total >= (1ll << 31))
     return GS_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)points_img & 7) || ((uintptr_t)splat & 15) || ((uintptr_t)grad_points_img & 7) ||
@@ -916,7 +1006,7 @@ extern "C" int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, 
       num_tiles, indexing_offset, total, ids_sorted, n, reinterpret_cast<const float2 *>(points_img),
       reinterpret_cast<const float4 *>(splat), nullptr, nullptr, nullptr, grad_image, final_t,
       pixel_end, width, height, alpha_threshold, transmittance_threshold, chi_squared_threshold,
-      grad_points_img, grad_splat, nullptr, nullptr, nullptr, reach);
+      grad_points_img, grad_splat, nullptr, nullptr, nullptr, reach, tile_order);
   count_launch();
   return launch_status();
 }

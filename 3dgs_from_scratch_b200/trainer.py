@@ -190,7 +190,7 @@ class NativeTrainer:
                     k = v % self.num_streams
                     cap, _, bufs = self._cap
                     s["ids"], s["offsets"] = bufs["ids"][v], bufs["offsets"][v]
-                    s["reach"] = bufs["reach"][v]
+                    s["reach"], s["order"] = bufs["reach"][v], bufs["order"][v]
                     s["total_dev"] = bufs["totals"][v:v + 1]
                     scratch = bufs["scratch"][k]
                     nat.call(self._capacity_entry, n, s["points"].data_ptr(),
@@ -206,6 +206,10 @@ class NativeTrainer:
                         s["offsets"], s["ids"] = cuda_rasterizer.tile_layout_from_counts(
                             s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
                     s["reach"] = torch.empty((max(total, 1),), device=dev, dtype=torch.uint8)
+                    s["order"] = torch.empty((T,), device=dev, dtype=torch.int32)
+                # the tiles in blend order, longest lists first (both passes)
+                nat.call("gs_tile_order", T, s["offsets"].data_ptr(), s["total"],
+                         s["order"].data_ptr(), vst)
                 s["image"] = torch.empty((H, W, 3), **f)
                 s["final_t"] = torch.empty((H * W,), **f)
                 s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)
@@ -214,7 +218,7 @@ class NativeTrainer:
                          W, H, o["alpha_threshold"], o["transmittance_threshold"],
                          o["chi_squared_threshold"], s["image"].data_ptr(),
                          s["final_t"].data_ptr(), s["pixel_end"].data_ptr(),
-                         s["reach"].data_ptr(), vst)
+                         s["reach"].data_ptr(), s["order"].data_ptr(), vst)
         self._join()
         return views
 
@@ -258,6 +262,7 @@ class NativeTrainer:
             ids=[torch.empty((cap,), device=dev, dtype=torch.int32) for _ in range(V)],
             # per list entry: the reach mask the forward blend keeps for the backward
             reach=[torch.empty((cap,), device=dev, dtype=torch.uint8) for _ in range(V)],
+            order=[torch.empty((T,), device=dev, dtype=torch.int32) for _ in range(V)],
             offsets=[torch.empty((T + 1,), device=dev, dtype=torch.int32) for _ in range(V)],
             totals=torch.zeros((V,), device=dev, dtype=torch.int64),
             scratch=[torch.empty((max(nbytes, 1),), device=dev, dtype=torch.uint8)
@@ -441,7 +446,7 @@ class NativeTrainer:
                  s["splat"].data_ptr(), grad_img.data_ptr(), s["final_t"].data_ptr(),
                  s["pixel_end"].data_ptr(), W, H, o["alpha_threshold"],
                  o["transmittance_threshold"], o["chi_squared_threshold"], g_points.data_ptr(),
-                 g_splat.data_ptr(), s["reach"].data_ptr(), st)
+                 g_splat.data_ptr(), s["reach"].data_ptr(), s["order"].data_ptr(), st)
 
     def check_status(self):
         """Synchronise the device and raise NativeError if a kernel of this

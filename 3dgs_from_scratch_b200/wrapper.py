@@ -196,19 +196,26 @@ class _Blend(torch.autograd.Function):
         pixel_end = torch.empty((H * W,), device=dev, dtype=torch.int32)
         # each list entry's reach mask, written by the forward, read by the backward
         reach = torch.empty((max(ids.shape[0], 1),), device=dev, dtype=torch.uint8)
-        nat.call("gs_blend_forward", indexing_offset.shape[0], indexing_offset.data_ptr(),
+        # tiles blended longest list first (both passes)
+        T = indexing_offset.shape[0]
+        order = torch.empty((max(T, 1),), device=dev, dtype=torch.int32)
+        st = nat.stream_ptr(dev)
+        nat.call("gs_tile_order", T, indexing_offset.data_ptr(), ids.shape[0], order.data_ptr(),
+                 st)
+        nat.call("gs_blend_forward", T, indexing_offset.data_ptr(),
                  ids.shape[0], ids.data_ptr(), points.shape[0], points.data_ptr(),
                  splat.data_ptr(), W, H,
                  opts["alpha_threshold"], opts["transmittance_threshold"],
                  opts["chi_squared_threshold"], image.data_ptr(), final_t.data_ptr(),
-                 pixel_end.data_ptr(), reach.data_ptr(), nat.stream_ptr(dev))
-        ctx.save_for_backward(points, splat, indexing_offset, ids, final_t, pixel_end, reach)
+                 pixel_end.data_ptr(), reach.data_ptr(), order.data_ptr(), st)
+        ctx.save_for_backward(points, splat, indexing_offset, ids, final_t, pixel_end, reach,
+                              order)
         ctx.opts = opts
         return image
 
     @staticmethod
     def backward(ctx, grad_image):
-        points, splat, indexing_offset, ids, final_t, pixel_end, reach = ctx.saved_tensors
+        points, splat, indexing_offset, ids, final_t, pixel_end, reach, order = ctx.saved_tensors
         o = ctx.opts
         dev = points.device
         n = points.shape[0]
@@ -221,7 +228,7 @@ class _Blend(torch.autograd.Function):
                  final_t.data_ptr(), pixel_end.data_ptr(), o["width"], o["height"],
                  o["alpha_threshold"], o["transmittance_threshold"],
                  o["chi_squared_threshold"], g_points.data_ptr(), g_splat.data_ptr(),
-                 reach.data_ptr(), nat.stream_ptr(dev))
+                 reach.data_ptr(), order.data_ptr(), nat.stream_ptr(dev))
         return g_points, g_splat, None, None, None
 
 

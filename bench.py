@@ -183,7 +183,7 @@ class StageTimer:
     """CUDA events around each C-ABI call of interest, on the launching stream."""
 
     WATCH = ("gs_preprocess_forward", "gs_tile_layout", "gs_tile_layout_capped",
-             "gs_tile_bins", "gs_tile_layout_views",
+             "gs_tile_bins", "gs_tile_layout_views", "gs_tile_order",
              "gs_blend_forward", "gs_blend_backward",
              "gs_preprocess_backward", "gs_l1_loss_grad", "gs_l1_ssim_loss_grad", "gs_adam_step",
              "gs_dp_adam_step", "gs_preprocess_forward_views", "gs_preprocess_backward_views")
@@ -1075,6 +1075,7 @@ def main():
     lay_ms = (stage_ms.get("gs_tile_layout") or stage_ms.get("gs_tile_layout_capped")
               or stage_ms.get("gs_tile_bins"))
     if lay_ms:
+        lay_ms += stage_ms.get("gs_tile_order") or 0.0  # the blend order is part of the layout
         gbs = (LAYOUT_BYTES_PER_PAIR * K + 4 * T) / (lay_ms * 1e-3) / 1e9
         roof["tile_layout"] = {"bound": "hbm", "ms": lay_ms, "achieved": gbs,
                                "peak": hbm, "unit": "GB/s", "frac": gbs / hbm}

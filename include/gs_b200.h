@@ -46,7 +46,7 @@ extern "C" {
 #define GS_TILE 16
 
 /* Library version (2: gs_blend_forward / gs_blend_backward take the reach
- * buffer), last CUDA error code seen, and the number of kernels this
+ * buffer and the tile order), last CUDA error code seen, and the number of kernels this
  * library has launched since load (for launch accounting in benchmarks). */
 GS_API int gs_version(void);
 GS_API int gs_last_cuda_error(void);
@@ -299,25 +299,36 @@ GS_API int gs_preprocess_forward(int n, const float *means, const float *scales,
  * the forward stores there, for the entries it visits, which 8x8 pixel
  * blocks of its tile the entry's Gaussian can reach, and gs_blend_backward
  * given the same buffer (layout and splat records unchanged) reads them
- * instead of recomputing them. */
+ * instead of recomputing them. tile_order: NULL (block b blends tile b) or
+ * the num_tiles tile indices in the order to blend them (gs_tile_order). */
 GS_API int gs_blend_forward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                      const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                      int width, int height, float alpha_threshold,
                      float transmittance_threshold, float chi_squared_threshold,
                      float *image, float *final_t, int32_t *pixel_end, uint8_t *reach,
-                     void *stream);
+                     const int32_t *tile_order, void *stream);
 
 /* Blend backward: gradient outputs (grad_points_img (N,2), grad_splat (N,8))
  * must be zeroed by the caller (they are accumulated). total as for
  * gs_blend_forward (-1: the end is indexing_offset[num_tiles]). reach: NULL
- * (the masks are recomputed) or the buffer the forward of this view filled. */
+ * (the masks are recomputed) or the buffer the forward of this view filled.
+ * tile_order as for gs_blend_forward. */
 GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int64_t total,
                       const int32_t *ids_sorted, int n, const float *points_img, const float *splat,
                       const float *grad_image, const float *final_t,
                       const int32_t *pixel_end, int width, int height,
                       float alpha_threshold, float transmittance_threshold,
                       float chi_squared_threshold, float *grad_points_img,
-                      float *grad_splat, const uint8_t *reach, void *stream);
+                      float *grad_splat, const uint8_t *reach, const int32_t *tile_order,
+                      void *stream);
+
+/* The tiles in the order to blend them, longest lists first (by a length
+ * class: exact below 8 entries, then 8 classes per power of two), so that
+ * the blend kernels' last wave holds short tiles. num_tiles and total as
+ * for gs_blend_forward; order receives num_tiles tile indices. No
+ * counterpart in the reference (its blend launches tile b as block b). */
+GS_API int gs_tile_order(int num_tiles, const int32_t *indexing_offset, int64_t total,
+                         int32_t *order, void *stream);
 
 /* gs_preprocess_backward_views for the Gaussians first .. first + count - 1
  * of n_total: parameter and gradient pointers are those of all n_total

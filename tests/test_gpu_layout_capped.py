@@ -10,6 +10,8 @@ host-sized per-view layout step, and a step that overflows its capacity is
 repeated with grown buffers to the same result."""
 import importlib
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -203,7 +205,7 @@ def test_blend_backward_reading_kept_reach_masks(gs, cfg_i, n, W, H):
                  grad_img.data_ptr(), s["final_t"].data_ptr(), s["pixel_end"].data_ptr(), W, H,
                  o["alpha_threshold"], o["transmittance_threshold"],
                  o["chi_squared_threshold"], gp.data_ptr(), gsp.data_ptr(),
-                 reach.data_ptr() if reach is not None else None, nat.stream_ptr())
+                 reach.data_ptr() if reach is not None else None, None, nat.stream_ptr())
         out.append((gp, gsp))
     torch.cuda.synchronize()
     assert nat.query("gs_check_status", nat.stream_ptr()) == 0
@@ -211,3 +213,62 @@ def test_blend_backward_reading_kept_reach_masks(gs, cfg_i, n, W, H):
         scale = b.abs().max().item()
         assert scale > 0
         assert (a - b).abs().max().item() <= 1e-5 * scale
+
+
+def _length_class(n):
+    """Host restatement of the tile-order length class (exact below 8, then
+    8 classes per power of two)."""
+    n = n.astype(np.int64)
+    e = np.floor(np.log2(np.maximum(n, 1))).astype(np.int64)
+    cls = (e << 3) | ((n >> np.maximum(e - 3, 0)) & 7)
+    return np.where(n < 8, np.maximum(n, 0), cls)
+
+
+@pytest.mark.parametrize("cfg_i,n,W,H", [(0, 20_000, 256, 256), (1, None, 1920, 1080)])
+def test_tile_order_and_ordered_blend(gs, cfg_i, n, W, H):
+    """gs_tile_order returns every tile once, longest length class first; the
+    forward blend in that order writes the same image, final transmittance
+    and end indices bit for bit, and the backward the same gradients up to
+    the order of the atomics."""
+    tr_mod = importlib.import_module("3dgs_from_scratch_b200.trainer")
+    cfg = gs.scenes.CONFIGS[cfg_i]
+    raw = {k: v.to(DEV) for k, v in gs.scenes.make_gaussians(cfg, seed=4, n=n).items()}
+    tr = tr_mod.NativeTrainer(raw, W, H, layout="binned")
+    K = gs.scenes.intrinsic_for(cfg, W, H).to(DEV)
+    cams = gs.scenes.orbit_cameras(cfg, 1).to(DEV)
+    s = tr.render_views(cams, K)[0]
+    o, n, T = tr.opts, tr.n, tr.tx * tr.ty
+    order = s["order"].cpu().numpy()
+    assert np.array_equal(np.sort(order), np.arange(T))
+    offs = s["offsets"].cpu().numpy().astype(np.int64)
+    lens = offs[1:] - offs[:-1]
+    cls = _length_class(lens[order])
+    assert np.all(np.diff(cls) <= 0)
+    g = torch.Generator(device=DEV).manual_seed(12)
+    grad_img = torch.randn((H, W, 3), device=DEV, generator=g)
+    res = []
+    for ordered in (True, False):
+        img = torch.empty((H, W, 3), device=DEV)
+        ft = torch.empty((H * W,), device=DEV)
+        pe = torch.empty((H * W,), device=DEV, dtype=torch.int32)
+        reach = torch.empty_like(s["reach"])
+        ordp = s["order"].data_ptr() if ordered else None
+        nat.call("gs_blend_forward", T, s["offsets"].data_ptr(), s["total"], s["ids"].data_ptr(),
+                 n, s["points"].data_ptr(), s["splat"].data_ptr(), W, H, o["alpha_threshold"],
+                 o["transmittance_threshold"], o["chi_squared_threshold"], img.data_ptr(),
+                 ft.data_ptr(), pe.data_ptr(), reach.data_ptr(), ordp, nat.stream_ptr())
+        gp = torch.zeros((n, 2), device=DEV)
+        gsp = torch.zeros((n, 8), device=DEV)
+        nat.call("gs_blend_backward", T, s["offsets"].data_ptr(), s["total"],
+                 s["ids"].data_ptr(), n, s["points"].data_ptr(), s["splat"].data_ptr(),
+                 grad_img.data_ptr(), ft.data_ptr(), pe.data_ptr(), W, H,
+                 o["alpha_threshold"], o["transmittance_threshold"],
+                 o["chi_squared_threshold"], gp.data_ptr(), gsp.data_ptr(), reach.data_ptr(),
+                 ordp, nat.stream_ptr())
+        res.append((img, ft, pe, gp, gsp))
+    torch.cuda.synchronize()
+    assert nat.query("gs_check_status", nat.stream_ptr()) == 0
+    for a, b in zip(res[0][:3], res[1][:3]):
+        assert torch.equal(a, b)
+    for a, b in zip(res[0][3:], res[1][3:]):
+        assert (a - b).abs().max().item() <= 1e-5 * b.abs().max().item()
