@@ -65,8 +65,8 @@ BLEND_BWD_FLOP_PER_PAIR = 60
 # dram__bytes_read.sum + dram__bytes_write.sum from one-kernel ncu captures of
 # the same kernels on the same workload (preprocess_fwd is the one multi-view
 # launch).
-NCU_TRAFFIC_BYTES = {"preprocess_fwd": 415.7e6, "preprocess_bwd": 599.3e6, "blend_fwd": 56.9e6,
-                     "blend_bwd": 109.2e6, "loss": 50.8e6}
+NCU_TRAFFIC_BYTES = {"preprocess_fwd": 415.7e6, "preprocess_bwd": 599.3e6, "blend_fwd": 54.0e6,
+                     "blend_bwd": 111.0e6, "loss": 50.8e6}
 
 
 def parse():
