@@ -55,18 +55,34 @@ __device__ __forceinline__ int rect_tile(const TileRect &r, int q, int tx) {
 // rectangles by the calling thread, larger ones by the whole warp (lane q
 // takes the rectangle's q-th, q+32-th, ... tile). f(tile, gaussian). Called
 // by whole warps (every lane, valid or not).
+// One Gaussian's inputs, loaded together (the three loads are independent).
+struct PairSrc {
+  float2 p, rd;
+  int count;
+};
+
+__device__ __forceinline__ PairSrc load_pair_src(int i, bool valid,
+                                                 const float2 *__restrict__ points,
+                                                 const float2 *__restrict__ radii,
+                                                 const int32_t *__restrict__ counts) {
+  PairSrc g{make_float2(0.f, 0.f), make_float2(0.f, 0.f), 0};
+  if (valid) {
+    g.count = counts[i];
+    g.p = points[i];
+    g.rd = radii[i];
+  }
+  return g;
+}
+
 template <typename F>
-__device__ __forceinline__ void pairs_of(int i, bool valid, const float2 *__restrict__ points,
-                                         const float2 *__restrict__ radii,
-                                         const int32_t *__restrict__ counts, int width,
-                                         int height, F f) {
+__device__ __forceinline__ void pairs_from(int i, bool valid, const PairSrc &g, int width,
+                                           int height, F f) {
   const int lane = threadIdx.x & 31;
   const int tx = tiles_x_of(width);
   TileRect r{0, -1, 0, -1, true};
   int area = 0;
-  if (valid && counts[i] > 0) {
-    const float2 p = points[i], rd = radii[i];
-    r = tile_rect(p.x, p.y, rd.x, rd.y, width, height);
+  if (valid && g.count > 0) {
+    r = tile_rect(g.p.x, g.p.y, g.rd.x, g.rd.y, width, height);
     if (!r.empty) area = (r.x1 - r.x0 + 1) * (r.y1 - r.y0 + 1);
   }
   const bool big = area > kSmallRect;
@@ -84,6 +100,32 @@ __device__ __forceinline__ void pairs_of(int i, bool valid, const float2 *__rest
     const int aj = __shfl_sync(0xffffffffu, area, j);
     const int gj = __shfl_sync(0xffffffffu, i, j);
     for (int q = lane; q < aj; q += 32) f(rect_tile(rj, q, tx), gj);
+  }
+}
+
+template <typename F>
+__device__ __forceinline__ void pairs_of(int i, bool valid, const float2 *__restrict__ points,
+                                         const float2 *__restrict__ radii,
+                                         const int32_t *__restrict__ counts, int width,
+                                         int height, F f) {
+  pairs_from(i, valid, load_pair_src(i, valid, points, radii, counts), width, height, f);
+}
+
+// A block's contiguous range [lo, hi) of Gaussians, kPrivThreads at a time,
+// the next Gaussian's inputs loaded while the current one's pairs are made.
+template <int THREADS, typename F>
+__device__ __forceinline__ void pairs_of_range(int lo, int hi, const float2 *__restrict__ points,
+                                               const float2 *__restrict__ radii,
+                                               const int32_t *__restrict__ counts, int width,
+                                               int height, F f) {
+  int i = lo + (int)threadIdx.x;
+  PairSrc cur = load_pair_src(i, i < hi, points, radii, counts);
+  for (int base = lo; base < hi; base += THREADS) {  // block-uniform trip count
+    const int inext = i + THREADS;
+    const PairSrc next = load_pair_src(inext, inext < hi, points, radii, counts);
+    pairs_from(i, i < hi, cur, width, height, f);
+    i = inext;
+    cur = next;
   }
 }
 
@@ -231,11 +273,8 @@ __global__ void __launch_bounds__(kPrivThreads) bin_hist_kernel(
   __syncthreads();
   int lo, hi;
   block_gaussian_range(n, lo, hi);
-  for (int base = lo; base < hi; base += kPrivThreads) {  // block-uniform trip count
-    const int i = base + threadIdx.x;
-    pairs_of(i, i < hi, points, radii, counts, width, height,
-             [&](int tile, int) { atomicAdd(s_cnt + tile, 1u); });
-  }
+  pairs_of_range<kPrivThreads>(lo, hi, points, radii, counts, width, height,
+                               [&](int tile, int) { atomicAdd(s_cnt + tile, 1u); });
   __syncthreads();
   uint32_t *row = hist + (size_t)blockIdx.x * T;
   for (int k = threadIdx.x; k < T; k += kPrivThreads) row[k] = s_cnt[k];
@@ -283,11 +322,8 @@ __global__ void __launch_bounds__(kPrivThreads) bin_place_kernel(
   __syncthreads();
   int lo, hi;
   block_gaussian_range(n, lo, hi);
-  for (int base = lo; base < hi; base += kPrivThreads) {
-    const int i = base + threadIdx.x;
-    pairs_of(i, i < hi, points, radii, counts, width, height,
-             [&](int tile, int g) { ids[atomicAdd(s_cur + tile, 1u)] = g; });
-  }
+  pairs_of_range<kPrivThreads>(lo, hi, points, radii, counts, width, height,
+                               [&](int tile, int g) { ids[atomicAdd(s_cur + tile, 1u)] = g; });
 }
 
 // ---- per-tile sort ---------------------------------------------------------
@@ -546,12 +582,11 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  // positions [0, P): ipw items per lane in every warp (the bucket spread
-  // over all warps, so a warp ranks as few items as the bucket allows), the
-  // tail padded with a key that sorts after every real key (stable, so the
-  // real keys stay first)
+  // positions [0, 256 ipw): ipw items per lane in every warp (the bucket
+  // spread over all warps, so a warp ranks as few items as the bucket
+  // allows), the tail padded with a key that sorts after every real key
+  // (stable, so the real keys stay first)
   const int ipw = (L + kRadThreads - 1) / kRadThreads;  // 1..kRadItems, block-uniform
-  const int P = ipw * kRadThreads;
   if (t == 0) {
     S.kmin = 0xffffffffu;
     S.kmax = 0u;
@@ -559,11 +594,22 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   }
   __syncthreads();
   uint32_t kmn = 0xffffffffu, kmx = 0u, bad = 0u;
-  for (int p = t; p < P; p += kRadThreads) {
+  // positions t + 256 q, q < ipw: every id load first, then the depth loads
+  // (one round trip each instead of two per position)
+  int32_t vals[kRadItems];
+#pragma unroll
+  for (int q = 0; q < kRadItems; ++q) {
+    if (q >= ipw) break;
+    const int p = t + q * kRadThreads;
+    vals[q] = p < L ? ids[beg + p] : -1;
+  }
+#pragma unroll
+  for (int q = 0; q < kRadItems; ++q) {
+    if (q >= ipw) break;
+    const int p = t + q * kRadThreads;
+    const int32_t val = vals[q];
     uint32_t key = 0xffffffffu;
-    int32_t val = -1;
     if (p < L) {
-      val = ids[beg + p];
       if (val >= 0 && val < n) {
         key = __float_as_uint(depths[val]);
         kmn = min(kmn, key);
