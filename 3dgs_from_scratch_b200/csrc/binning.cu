@@ -21,10 +21,12 @@
 //      then complete but in arbitrary order);
 //   4. bin_sort_kernel: one block per tile sorts its bucket by the key
 //      (depth bits << 32 | id), built from the view's depths: buckets of up
-//      to 2048 entries by 256 threads, up to 8192 by 1024 threads, in
+//      to 2048 entries by 256 threads as a block radix sort of the depth
+//      bits (ties then put in id order); longer ones, listed by that kernel,
+//      by 1024-thread blocks (bin_sort_long_kernel) up to 8192 entries in
 //      registers and shared memory (a sorting network on each thread's 8
-//      keys, then merge-path merges of sorted runs); longer buckets as
-//      sorted chunks merged run by run through global scratch.
+//      keys, then merge-path merges of sorted runs), beyond that as sorted
+//      chunks merged run by run through global scratch.
 // With up to kMaxPrivTiles tiles, steps 1 and 3 keep the tile counters in
 // shared memory per block (bin_hist_kernel, bin_colscan_kernel,
 // bin_place_kernel) instead of global atomics.
@@ -51,10 +53,6 @@ __device__ __forceinline__ int rect_tile(const TileRect &r, int q, int tx) {
   return (r.y0 + row) * tx + r.x0 + col;
 }
 
-// Visits every (Gaussian, tile) pair of Gaussian i (valid: i < n): small
-// rectangles by the calling thread, larger ones by the whole warp (lane q
-// takes the rectangle's q-th, q+32-th, ... tile). f(tile, gaussian). Called
-// by whole warps (every lane, valid or not).
 // One Gaussian's inputs, loaded together (the three loads are independent).
 struct PairSrc {
   float2 p, rd;
@@ -74,6 +72,10 @@ __device__ __forceinline__ PairSrc load_pair_src(int i, bool valid,
   return g;
 }
 
+// Visits every (Gaussian, tile) pair of Gaussian i (valid: i < n): small
+// rectangles by the calling thread, larger ones by the whole warp (lane q
+// takes the rectangle's q-th, q+32-th, ... tile). f(tile, gaussian). Called
+// by whole warps (every lane, valid or not).
 template <typename F>
 __device__ __forceinline__ void pairs_from(int i, bool valid, const PairSrc &g, int width,
                                            int height, F f) {
