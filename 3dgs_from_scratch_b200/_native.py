@@ -58,7 +58,7 @@ SIGNATURES = {
     "gs_tile_layout": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
     "gs_tile_layout_capped": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
     "gs_tile_bins_scratch_bytes": (SZ, [I, I64, I, I]),
-    "gs_tile_bins": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P]),
+    "gs_tile_bins": (I, [I, P, P, P, P, I64, I, I, P, P, P, P, SZ, P, P]),
     "gs_tile_layout_views_scratch_bytes": (SZ, [I, I, P, I, I]),
     "gs_tile_layout_views": (I, [I, I, P, P, P, P, P, I, I, P, P, P, SZ, P]),
     "gs_sort_scratch_bytes": (SZ, [I64]),

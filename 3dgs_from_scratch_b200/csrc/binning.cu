@@ -189,8 +189,9 @@ __device__ __forceinline__ long long block_excl_scan_ll(long long x, long long *
 __global__ void __launch_bounds__(kScanThreads) bin_scan_kernel(
     const uint32_t *__restrict__ tile_count, int T, int64_t capacity,
     int32_t *__restrict__ offsets, uint32_t *__restrict__ cursor, int64_t *__restrict__ total_dev,
-    Ctl *ctl, uint32_t *status) {
+    Ctl *ctl, uint32_t *status, int32_t *__restrict__ tile_order) {
   __shared__ long long s_warp[33];
+  __shared__ uint32_t s_class[kOrderClasses];
   const int t = threadIdx.x;
   // pass 1: the total
   long long sum = 0;
@@ -203,6 +204,9 @@ __global__ void __launch_bounds__(kScanThreads) bin_scan_kernel(
     ctl->overflow = over ? 1 : 0;
     if (over) atomicCAS(status, 0u, (uint32_t)GS_ERR_CAPACITY);
   }
+  if (tile_order != nullptr)  // the blend order (every list empty beyond the capacity)
+    tile_order_block(T, [&](int k) { return over ? 0 : (int)tile_count[k]; }, tile_order,
+                     s_class);
   if (over) {  // block-uniform
     for (int k = t; k <= T; k += kScanThreads) offsets[k] = 0;
     return;
@@ -824,7 +828,7 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
                             const float *depths, const int32_t *counts, int64_t capacity,
                             int width, int height, int32_t *ids_sorted, int32_t *indexing_offset,
                             int64_t *total_dev, void *scratch, size_t scratch_bytes,
-                            void *stream) {
+                            int32_t *tile_order, void *stream) {
   using namespace gs::binning;
   if (n < 0 || width <= 0 || height <= 0 || capacity < 0 || total_dev == nullptr)
     return GS_ERR_INVALID_ARGUMENT;
@@ -864,7 +868,7 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
     count_launch();
   }
   bin_scan_kernel<<<1, kScanThreads, 0, st>>>(tcount, T, capacity, indexing_offset, cursor,
-                                              total_dev, ctl, device_status_word());
+                                              total_dev, ctl, device_status_word(), tile_order);
   count_launch();
   if (n > 0) {
     if (L.blocks > 0) {

@@ -822,76 +822,22 @@ __global__ void __launch_bounds__(kBlendThreads, GS_BWD_MINB) blend_backward_ker
 
 // Blend order of the tiles: longest lists first, so that the blend's last
 // wave holds short tiles instead of a few long ones that run on while most
-// SMs idle (list scheduling, longest first). One block: a counting sort of
-// the tiles by a length class that grows with the list length (exact up to
-// 7, then 8 steps per power of two), classes in descending order; tiles of
-// one class in any order.
+// SMs idle (list scheduling, longest first). One block (tile_order_block).
 constexpr int kOrderThreads = 1024;
-constexpr int kOrderClasses = 256;
-
-__device__ __forceinline__ int length_class(int len) {
-  if (len < 8) return max(len, 0);
-  const int e = 31 - __clz(len);  // >= 3
-  return (e << 3) | ((len >> (e - 3)) & 7);  // <= 8 * 30 + 7
-}
 
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
     int num_tiles, const int32_t *__restrict__ offsets, int64_t total,
     int32_t *__restrict__ order) {
   __shared__ uint32_t s_count[kOrderClasses];
-  const int t = threadIdx.x;
-  for (int c = t; c < kOrderClasses; c += kOrderThreads) s_count[c] = 0u;
-  __syncthreads();
-  auto cls_of = [&](int tile) {
-    const int b = offsets[tile];
-    const int e = (tile + 1 < num_tiles) ? offsets[tile + 1]
-                                         : (total >= 0 ? (int)total : offsets[num_tiles]);
-    return kOrderClasses - 1 - length_class(e - b);  // longest first
-  };
-  // lanes of a warp with the same class add once (many tiles share a class)
-  const int lane = t & 31;
-  const uint32_t lt_mask = (1u << lane) - 1u;
-  const int rounds = (num_tiles + kOrderThreads - 1) / kOrderThreads;  // block-uniform
-  for (int r = 0; r < rounds; ++r) {
-    const int tile = r * kOrderThreads + t;
-    const int c = tile < num_tiles ? cls_of(tile) : -1;
-    const uint32_t peers = __match_any_sync(0xffffffffu, c);
-    if (c >= 0 && (peers & lt_mask) == 0u) atomicAdd(&s_count[c], (uint32_t)__popc(peers));
-  }
-  __syncthreads();
-  if (t < 32) {  // exclusive scan of the 256 class counts by one warp, 8 per lane
-    uint32_t v[8], sum = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[i] = s_count[t * 8 + i];
-      sum += v[i];
-    }
-    uint32_t incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (t >= o) incl += y;
-    }
-    uint32_t run = incl - sum;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s_count[t * 8 + i] = run;
-      run += v[i];
-    }
-  }
-  __syncthreads();
-  for (int r = 0; r < rounds; ++r) {
-    const int tile = r * kOrderThreads + t;
-    const int c = tile < num_tiles ? cls_of(tile) : -1;
-    const uint32_t peers = __match_any_sync(0xffffffffu, c);
-    const int leader = __ffs(peers) - 1;
-    uint32_t base = 0;
-    if (c >= 0 && lane == leader) base = atomicAdd(&s_count[c], (uint32_t)__popc(peers));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (c >= 0) order[base + __popc(peers & lt_mask)] = tile;
-  }
+  tile_order_block(
+      num_tiles,
+      [&](int tile) {
+        const int e = (tile + 1 < num_tiles) ? offsets[tile + 1]
+                                             : (total >= 0 ? (int)total : offsets[num_tiles]);
+        return e - offsets[tile];
+      },
+      order, s_count);
 }
-static_assert(kOrderClasses == 32 * 8, "the class scan gives each lane 8 classes");
 
 }  // namespace gs
 

@@ -787,6 +787,72 @@ __device__ __forceinline__ void sh_view_backward(const ViewDir &d, const float b
   gm[2] += j02 * tx + j12 * ty + j22 * tz;
 }
 
+// ---- blend order of the tiles ---------------------------------------------------
+
+// Length class of a tile list for the blend order: exact below 8 entries,
+// then 8 classes per power of two (the leading bit's position and the next
+// three bits), at most 8 * 30 + 7.
+constexpr int kOrderClasses = 256;
+
+__device__ __forceinline__ int length_class(int len) {
+  if (len < 8) return max(len, 0);
+  const int e = 31 - __clz(len);  // >= 3
+  return (e << 3) | ((len >> (e - 3)) & 7);
+}
+
+// One block writes the num_tiles tile indices into `order`, longest lists
+// first: a counting sort by descending length class (tiles of one class in
+// any order), with lanes of a warp that share a class adding once. len(tile)
+// gives a tile's list length; s_count is kOrderClasses words of shared
+// memory. Every thread of the block calls it (blockDim.x a multiple of 32).
+template <typename LenF>
+__device__ void tile_order_block(int num_tiles, LenF len, int32_t *__restrict__ order,
+                                 uint32_t *s_count) {
+  const int t = threadIdx.x, lane = t & 31, nt = blockDim.x;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int c = t; c < kOrderClasses; c += nt) s_count[c] = 0u;
+  __syncthreads();
+  const int rounds = (num_tiles + nt - 1) / nt;  // block-uniform
+  for (int r = 0; r < rounds; ++r) {
+    const int tile = r * nt + t;
+    const int c = tile < num_tiles ? kOrderClasses - 1 - length_class(len(tile)) : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, c);
+    if (c >= 0 && (peers & lt_mask) == 0u) atomicAdd(&s_count[c], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+  if (t < 32) {  // exclusive scan of the class counts by one warp, 8 per lane
+    uint32_t v[kOrderClasses / 32], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kOrderClasses / 32; ++i) {
+      v[i] = s_count[t * (kOrderClasses / 32) + i];
+      sum += v[i];
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (t >= o) incl += y;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int i = 0; i < kOrderClasses / 32; ++i) {
+      s_count[t * (kOrderClasses / 32) + i] = run;
+      run += v[i];
+    }
+  }
+  __syncthreads();
+  for (int r = 0; r < rounds; ++r) {
+    const int tile = r * nt + t;
+    const int c = tile < num_tiles ? kOrderClasses - 1 - length_class(len(tile)) : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, c);
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (c >= 0 && lane == leader) base = atomicAdd(&s_count[c], (uint32_t)__popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (c >= 0) order[base + __popc(peers & lt_mask)] = tile;
+  }
+}
+
 // ---- tiles --------------------------------------------------------------------
 
 // floorf followed by the float->int32 conversion (kernel.cu:804-807).

@@ -165,7 +165,7 @@ def tile_layout_from_counts(points_image, radii, depths, counts, total, width, h
         scratch = torch.empty((max(nbytes, 8),), device=dev, dtype=torch.uint8)
         nat.call("gs_tile_bins", n, points_image.data_ptr(), radii.data_ptr(), depths.data_ptr(),
                  counts.data_ptr(), int(total), int(width), int(height), ids.data_ptr(),
-                 offsets.data_ptr(), total_dev.data_ptr(), scratch.data_ptr(), nbytes,
+                 offsets.data_ptr(), total_dev.data_ptr(), scratch.data_ptr(), nbytes, None,
                  nat.stream_ptr(dev))
         return offsets[:tx * ty], ids
     indexing_offset = torch.empty((tx * ty,), device=dev, dtype=torch.int32)

@@ -193,11 +193,15 @@ class NativeTrainer:
                     s["reach"], s["order"] = bufs["reach"][v], bufs["order"][v]
                     s["total_dev"] = bufs["totals"][v:v + 1]
                     scratch = bufs["scratch"][k]
+                    # the binned layout writes the blend order in the same launch
+                    # as its offsets; after the two-sort layout gs_tile_order does
+                    fused_order = self._capacity_entry == "gs_tile_bins"
+                    extra = (s["order"].data_ptr(),) if fused_order else ()
                     nat.call(self._capacity_entry, n, s["points"].data_ptr(),
                              s["radii"].data_ptr(), s["depths"].data_ptr(),
                              s["counts"].data_ptr(), cap, W, H, s["ids"].data_ptr(),
                              s["offsets"].data_ptr(), s["total_dev"].data_ptr(),
-                             scratch.data_ptr(), scratch.numel(), vst)
+                             scratch.data_ptr(), scratch.numel(), *extra, vst)
                     s["total"] = -1
                 else:
                     total = self.last_totals[v]
@@ -207,9 +211,11 @@ class NativeTrainer:
                             s["points"], s["radii"], s["depths"], s["counts"], total, W, H)
                     s["reach"] = torch.empty((max(total, 1),), device=dev, dtype=torch.uint8)
                     s["order"] = torch.empty((T,), device=dev, dtype=torch.int32)
-                # the tiles in blend order, longest lists first (both passes)
-                nat.call("gs_tile_order", T, s["offsets"].data_ptr(), s["total"],
-                         s["order"].data_ptr(), vst)
+                    fused_order = False
+                if not fused_order:
+                    # the tiles in blend order, longest lists first (both passes)
+                    nat.call("gs_tile_order", T, s["offsets"].data_ptr(), s["total"],
+                             s["order"].data_ptr(), vst)
                 s["image"] = torch.empty((H, W, 3), **f)
                 s["final_t"] = torch.empty((H * W,), **f)
                 s["pixel_end"] = torch.empty((H * W,), device=dev, dtype=torch.int32)

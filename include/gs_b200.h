@@ -204,12 +204,16 @@ GS_API int gs_tile_layout_capped(int n, const float *points_img, const float *ra
  * counters, their scan, an atomic scatter of every Gaussian's id into its
  * tiles' buckets, and a sort of each bucket on its own by (depth bits, id)
  * -- the order the reference's stable 64-bit sort gives within a tile
- * (kernel.cu:820-914,1341-1388). Scratch: gs_tile_bins_scratch_bytes. */
+ * (kernel.cu:820-914,1341-1388). Scratch: gs_tile_bins_scratch_bytes.
+ * tile_order: NULL, or num_tiles ints that receive the blend order of the
+ * tiles, as gs_tile_order writes it (computed in the same launch as the
+ * offsets, saving gs_tile_order's launch). */
 GS_API size_t gs_tile_bins_scratch_bytes(int n, int64_t capacity, int width, int height);
 GS_API int gs_tile_bins(int n, const float *points_img, const float *radii, const float *depths,
                         const int32_t *counts, int64_t capacity, int width, int height,
                         int32_t *ids_sorted, int32_t *indexing_offset, int64_t *total_dev,
-                        void *scratch, size_t scratch_bytes, void *stream);
+                        void *scratch, size_t scratch_bytes, int32_t *tile_order,
+                        void *stream);
 
 /* Scratch bytes for gs_tile_layout_views (0 on invalid arguments). totals
  * is a HOST array of num_views pair counts. */

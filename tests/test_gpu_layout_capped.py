@@ -31,11 +31,26 @@ def capped(b, v, n, cap, W, H, guard=4096, entry="capped"):
     tot = torch.full((1,), -5, device=DEV, dtype=torch.int64)
     nb = int(nat.query(sfn, n, max(cap, 1), W, H))
     scratch = torch.empty((max(nb, 1),), device=DEV, dtype=torch.uint8)
+    # the binned layout also writes the blend order of the tiles
+    order = torch.full((T,), -1, device=DEV, dtype=torch.int32) if entry == "bins" else None
+    extra = (order.data_ptr(),) if order is not None else ()
     nat.call(fn, n, b["points"][v].data_ptr(), b["radii"][v].data_ptr(),
              b["depths"][v].data_ptr(), b["counts"][v].data_ptr(), cap, W, H, ids.data_ptr(),
-             offs.data_ptr(), tot.data_ptr(), scratch.data_ptr(), nb, nat.stream_ptr())
+             offs.data_ptr(), tot.data_ptr(), scratch.data_ptr(), nb, *extra, nat.stream_ptr())
     torch.cuda.synchronize()
+    if order is not None:
+        check_blend_order(order, offs[:T + 1])
     return ids, offs, int(tot.item()), T
+
+
+def check_blend_order(order, offsets):
+    """order holds every tile once, longest length class first."""
+    order = order.cpu().numpy()
+    offs = offsets.cpu().numpy().astype(np.int64)
+    T = offs.shape[0] - 1
+    assert np.array_equal(np.sort(order), np.arange(T))
+    lens = offs[1:] - offs[:-1]
+    assert np.all(np.diff(_length_class(lens[order])) <= 0)
 
 
 def setup(gs, cfg, n, W, H, cams, seed=0):
@@ -238,12 +253,11 @@ def test_tile_order_and_ordered_blend(gs, cfg_i, n, W, H):
     cams = gs.scenes.orbit_cameras(cfg, 1).to(DEV)
     s = tr.render_views(cams, K)[0]
     o, n, T = tr.opts, tr.n, tr.tx * tr.ty
-    order = s["order"].cpu().numpy()
-    assert np.array_equal(np.sort(order), np.arange(T))
-    offs = s["offsets"].cpu().numpy().astype(np.int64)
-    lens = offs[1:] - offs[:-1]
-    cls = _length_class(lens[order])
-    assert np.all(np.diff(cls) <= 0)
+    check_blend_order(s["order"], s["offsets"])  # written by the binned layout
+    standalone = torch.full((T,), -1, device=DEV, dtype=torch.int32)
+    nat.call("gs_tile_order", T, s["offsets"].data_ptr(), s["total"], standalone.data_ptr(),
+             nat.stream_ptr())
+    check_blend_order(standalone, s["offsets"])
     g = torch.Generator(device=DEV).manual_seed(12)
     grad_img = torch.randn((H, W, 3), device=DEV, generator=g)
     res = []
