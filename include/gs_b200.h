@@ -330,7 +330,8 @@ GS_API int gs_blend_backward(int num_tiles, const int32_t *indexing_offset, int6
  * class: exact below 8 entries, then 8 classes per power of two), so that
  * the blend kernels' last wave holds short tiles. num_tiles and total as
  * for gs_blend_forward; order receives num_tiles tile indices. No
- * counterpart in the reference (its blend launches tile b as block b). */
+ * counterpart in the reference (its blend launches block b on tile b,
+ * kernel.cu:1430-1433). */
 GS_API int gs_tile_order(int num_tiles, const int32_t *indexing_offset, int64_t total,
                          int32_t *order, void *stream);
 
