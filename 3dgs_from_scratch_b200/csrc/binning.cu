@@ -43,7 +43,8 @@ constexpr uint64_t kPad = ~0ull;  // sorts after every real key
 
 struct Ctl {
   int32_t overflow;   // set by the scan when the total exceeds the capacity
-  int32_t num_long;   // buckets longer than the short sort's chunk, listed in long_tiles
+  int32_t num_long;   // buckets longer than the mid sort's chunk, listed in long_tiles
+  int32_t num_mid;    // buckets longer than the short sort's chunk, listed in mid_tiles
 };
 
 // The tiles of one Gaussian's rectangle, row-major, q-th of them.
@@ -528,7 +529,8 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
 
 // ---- short buckets: block radix sort on the depth bits -----------------------
 //
-// A bucket of up to kRadChunk entries is sorted by one 256-thread block as a
+// A bucket of up to kRadChunk entries is sorted by one 256-thread block (up
+// to kRadMidChunk by a 512-thread block) as a
 // stable LSD radix sort of its 32-bit depth keys (8-bit digits) in shared
 // memory. The keys are sorted as their offsets from the bucket's smallest
 // key (an order-preserving shift for unsigned keys), so only the bits of the
@@ -543,21 +545,25 @@ __device__ void sort_bucket(int beg, int L, const float *__restrict__ depths, in
 // scatters into the other buffer. Equal depth keys keep the bucket's
 // (arbitrary) order, so runs of equal keys are then put in id order: the
 // (depth bits, id) order of the reference's stable 64-bit sort.
-constexpr int kRadThreads = 256;
-constexpr int kRadWarps = kRadThreads / 32;
+constexpr int kRadThreads = 256;                    // buckets up to 2048 entries
+constexpr int kRadMidThreads = 512;                 // 2049 to 4096 entries
 constexpr int kRadItems = 8;
 constexpr int kRadChunk = kRadThreads * kRadItems;  // 2048
+constexpr int kRadMidChunk = kRadMidThreads * kRadItems;  // 4096
 
+template <int THREADS>
 struct RadSmem {
-  uint32_t key[2][kRadChunk];
-  int32_t val[2][kRadChunk];
-  uint32_t whist[kRadWarps][256];
+  uint32_t key[2][THREADS * kRadItems];
+  int32_t val[2][THREADS * kRadItems];
+  uint32_t whist[THREADS / 32][256];
   uint32_t gbase[256];
-  uint32_t tmp[kRadWarps + 1];
+  uint32_t tmp[THREADS / 32 + 1];
   uint32_t kmin, kmax, invalid;
 };
 
+template <int THREADS>
 __device__ __forceinline__ uint32_t rad_block_excl_scan(uint32_t x, uint32_t *s_tmp) {
+  constexpr int kWarps = THREADS / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t incl = x;
 #pragma unroll
@@ -568,14 +574,14 @@ __device__ __forceinline__ uint32_t rad_block_excl_scan(uint32_t x, uint32_t *s_
   if (lane == 31) s_tmp[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t w = lane < kRadWarps ? s_tmp[lane] : 0u;
+    const uint32_t w = lane < kWarps ? s_tmp[lane] : 0u;
     uint32_t wi = w;
 #pragma unroll
-    for (int o = 1; o < kRadWarps; o <<= 1) {
+    for (int o = 1; o < kWarps; o <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, wi, o);
       if (lane >= o) wi += y;
     }
-    if (lane < kRadWarps) s_tmp[lane] = wi - w;
+    if (lane < kWarps) s_tmp[lane] = wi - w;
   }
   __syncthreads();
   const uint32_t r = incl - x + s_tmp[warp];
@@ -583,8 +589,12 @@ __device__ __forceinline__ uint32_t rad_block_excl_scan(uint32_t x, uint32_t *s_
   return r;
 }
 
+// THREADS = 256 or 512 threads sort a bucket of up to 8 THREADS entries;
+// threads 0-255 own the 256 digits in each pass's digit scan.
+template <int THREADS>
 __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ depths, int n,
-                                  int32_t *__restrict__ ids, RadSmem &S) {
+                                  int32_t *__restrict__ ids, RadSmem<THREADS> &S) {
+  constexpr int kWarps = THREADS / 32;
   const int t = threadIdx.x, warp = t >> 5;
   const uint32_t lane = t & 31;
   const uint32_t lt_mask = (1u << lane) - 1u;
@@ -592,7 +602,7 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   // spread over all warps, so a warp ranks as few items as the bucket
   // allows), the tail padded with a key that sorts after every real key
   // (stable, so the real keys stay first)
-  const int ipw = (L + kRadThreads - 1) / kRadThreads;  // 1..kRadItems, block-uniform
+  const int ipw = (L + THREADS - 1) / THREADS;  // 1..kRadItems, block-uniform
   if (t == 0) {
     S.kmin = 0xffffffffu;
     S.kmax = 0u;
@@ -606,13 +616,13 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
 #pragma unroll
   for (int q = 0; q < kRadItems; ++q) {
     if (q >= ipw) break;
-    const int p = t + q * kRadThreads;
+    const int p = t + q * THREADS;
     vals[q] = p < L ? ids[beg + p] : -1;
   }
 #pragma unroll
   for (int q = 0; q < kRadItems; ++q) {
     if (q >= ipw) break;
-    const int p = t + q * kRadThreads;
+    const int p = t + q * THREADS;
     const int32_t val = vals[q];
     uint32_t key = 0xffffffffu;
     if (p < L) {
@@ -663,7 +673,7 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
   int cur = 0;
   for (int pass = 0; pass < passes; ++pass) {  // block-uniform
     const int shift = 8 * pass;
-    for (int k = t; k < kRadWarps * 256; k += kRadThreads) (&S.whist[0][0])[k] = 0u;
+    for (int k = t; k < kWarps * 256; k += THREADS) (&S.whist[0][0])[k] = 0u;
     __syncthreads();
     uint32_t key[kRadItems], rank[kRadItems];
     int32_t val[kRadItems];
@@ -697,16 +707,19 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
         if (q < ipw) rank[q] += __shfl_sync(0xffffffffu, lead_old[q], leader_of[q]);
     }
     __syncthreads();
-    {  // thread t owns digit t: warp prefixes, then the digit prefix
+    {  // thread t < 256 owns digit t: warp prefixes, then the digit prefix
       const int d = t;
       uint32_t c = 0;
+      if (d < 256) {
 #pragma unroll
-      for (int w = 0; w < kRadWarps; ++w) {
-        const uint32_t x = S.whist[w][d];
-        S.whist[w][d] = c;
-        c += x;
+        for (int w = 0; w < kWarps; ++w) {
+          const uint32_t x = S.whist[w][d];
+          S.whist[w][d] = c;
+          c += x;
+        }
       }
-      S.gbase[d] = rad_block_excl_scan(c, S.tmp);
+      const uint32_t g = rad_block_excl_scan<THREADS>(c, S.tmp);
+      if (d < 256) S.gbase[d] = g;
     }
     __syncthreads();
     {
@@ -723,7 +736,7 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
     cur ^= 1;
   }
   // runs of equal depth keys in id order, each by the thread at its start
-  for (int p = t; p < L; p += kRadThreads) {
+  for (int p = t; p < L; p += THREADS) {
     const uint32_t kp = S.key[cur][p];
     if ((p == 0 || S.key[cur][p - 1] != kp) && p + 1 < L && S.key[cur][p + 1] == kp) {
       int e = p + 1;
@@ -740,11 +753,13 @@ __device__ void radix_sort_bucket(int beg, int L, const float *__restrict__ dept
     }
   }
   __syncthreads();
-  for (int p = t; p < L; p += kRadThreads) ids[beg + p] = S.val[cur][p];
+  for (int p = t; p < L; p += THREADS) ids[beg + p] = S.val[cur][p];
 }
 
 // One block per tile sorts buckets of up to kRadChunk entries; longer
-// buckets are listed (ctl->num_long, long_tiles) for bin_sort_long_kernel.
+// buckets are listed: up to kRadMidChunk for bin_sort_mid_kernel
+// (ctl->num_mid, mid_tiles), the rest for bin_sort_long_kernel
+// (ctl->num_long, long_tiles).
 #ifndef GS_BIN_SORT_MINB
 #define GS_BIN_SORT_MINB 4  // blocks per SM the bucket sort's registers target (64 each)
 #endif
@@ -752,17 +767,39 @@ __global__ void __launch_bounds__(kRadThreads, GS_BIN_SORT_MINB) bin_sort_kernel
                                                                const float *__restrict__ depths,
                                                                int n, int32_t *__restrict__ ids,
                                                                Ctl *ctl,
-                                                               int32_t *__restrict__ long_tiles) {
+                                                               int32_t *__restrict__ long_tiles,
+                                                               int32_t *__restrict__ mid_tiles) {
   extern __shared__ __align__(16) unsigned char rad_raw[];
-  RadSmem &S = *reinterpret_cast<RadSmem *>(rad_raw);
+  RadSmem<kRadThreads> &S = *reinterpret_cast<RadSmem<kRadThreads> *>(rad_raw);
   const int tile = blockIdx.x;
   const int beg = offsets[tile], L = offsets[tile + 1] - beg;
   if (L <= 1) return;  // block-uniform
   if (L > kRadChunk) {
-    if (threadIdx.x == 0) long_tiles[atomicAdd(&ctl->num_long, 1)] = tile;
+    if (threadIdx.x == 0) {
+      if (L <= kRadMidChunk)
+        mid_tiles[atomicAdd(&ctl->num_mid, 1)] = tile;
+      else
+        long_tiles[atomicAdd(&ctl->num_long, 1)] = tile;
+    }
     return;
   }
-  radix_sort_bucket(beg, L, depths, n, ids, S);
+  radix_sort_bucket<kRadThreads>(beg, L, depths, n, ids, S);
+}
+
+// The listed buckets of kRadChunk + 1 to kRadMidChunk entries, a 512-thread
+// block at a time over the list (two blocks per SM).
+__global__ void __launch_bounds__(kRadMidThreads, 2) bin_sort_mid_kernel(
+    const int32_t *__restrict__ offsets, const float *__restrict__ depths, int n,
+    int32_t *__restrict__ ids, const Ctl *ctl, const int32_t *__restrict__ mid_tiles) {
+  extern __shared__ __align__(16) unsigned char rad_raw[];
+  RadSmem<kRadMidThreads> &S = *reinterpret_cast<RadSmem<kRadMidThreads> *>(rad_raw);
+  const int count = ctl->num_mid;
+  for (int q = blockIdx.x; q < count; q += gridDim.x) {  // block-uniform
+    const int tile = mid_tiles[q];
+    const int beg = offsets[tile], L = offsets[tile + 1] - beg;
+    radix_sort_bucket<kRadMidThreads>(beg, L, depths, n, ids, S);
+    __syncthreads();  // the shared buffers are reused by the next bucket
+  }
 }
 
 // The listed long buckets, a block at a time over the list.
@@ -787,7 +824,7 @@ constexpr int kSortLarge = 1024;  // buckets above kRadChunk: on chip up to 8192
 
 // Scratch of gs_tile_bins, carved in this order.
 struct BinScratch {
-  size_t ctl, count, cursor, longs, hist, keys_a, keys_b, total;
+  size_t ctl, count, cursor, longs, mids, hist, keys_a, keys_b, total;
   int blocks;  // blocks of the privatised binning (0: direct global atomics)
 };
 
@@ -808,7 +845,8 @@ static BinScratch bin_scratch(int64_t capacity, int num_tiles) {
   L.count = bin_align(sizeof(binning::Ctl));
   L.cursor = bin_align(L.count + 4 * (size_t)num_tiles);
   L.longs = bin_align(L.cursor + 4 * (size_t)num_tiles);
-  L.hist = bin_align(L.longs + 4 * (size_t)num_tiles);
+  L.mids = bin_align(L.longs + 4 * (size_t)num_tiles);
+  L.hist = bin_align(L.mids + 4 * (size_t)num_tiles);
   L.keys_a = bin_align(L.hist + 4 * (size_t)num_tiles * (size_t)L.blocks);
   L.keys_b = bin_align(L.keys_a + 8 * cap);
   L.total = bin_align(L.keys_b + 8 * cap);
@@ -882,17 +920,23 @@ extern "C" int gs_tile_bins(int n, const float *points_img, const float *radii,
     uint64_t *ka = reinterpret_cast<uint64_t *>(p + L.keys_a);
     uint64_t *kb = reinterpret_cast<uint64_t *>(p + L.keys_b);
     int32_t *longs = reinterpret_cast<int32_t *>(p + L.longs);
-    const size_t smem_small = sizeof(RadSmem);
+    int32_t *mids = reinterpret_cast<int32_t *>(p + L.mids);
+    const size_t smem_small = sizeof(RadSmem<kRadThreads>);
+    const size_t smem_mid = sizeof(RadSmem<kRadMidThreads>);
     const size_t smem_large = sizeof(uint64_t) * kSortLarge * kItems;
     cudaFuncSetAttribute(bin_sort_long_kernel<kSortLarge>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_large);
     cudaFuncSetAttribute(bin_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem_small);
+    cudaFuncSetAttribute(bin_sort_mid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem_mid);
     bin_sort_kernel<<<T, kRadThreads, smem_small, st>>>(indexing_offset, depths, n, ids_sorted,
-                                                        ctl, longs);
+                                                        ctl, longs, mids);
+    bin_sort_mid_kernel<<<2 * bin_sm_count(), kRadMidThreads, smem_mid, st>>>(
+        indexing_offset, depths, n, ids_sorted, ctl, mids);
     bin_sort_long_kernel<kSortLarge><<<2 * bin_sm_count(), kSortLarge, smem_large, st>>>(
         indexing_offset, depths, n, ids_sorted, ctl, longs, ka, kb);
-    count_launch(2);
+    count_launch(3);
   }
   return launch_status();
 }

@@ -136,10 +136,12 @@ def _read_total(total_dev, dev):
 
 
 # The binned layout (gs_tile_bins) is used while the pairs average at most
-# this many per tile: its per-tile sorts are cheap for short lists; longer
-# lists go to the two stable sorts of gs_tile_layout. Both give the same
+# this many per tile: its per-tile radix sorts are cheap for lists of up to
+# 4096 entries; scenes whose lists run far longer (the clustered 4K scene of
+# configuration 3 averages ~3000 pairs per tile, most of them in lists above
+# 4096) go to the two stable sorts of gs_tile_layout. Both give the same
 # lists and offsets bit for bit.
-BIN_MAX_PAIRS_PER_TILE = 1024
+BIN_MAX_PAIRS_PER_TILE = 2560
 
 
 def tile_layout_from_counts(points_image, radii, depths, counts, total, width, height,

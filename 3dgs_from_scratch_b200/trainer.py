@@ -49,7 +49,7 @@ class NativeTrainer:
     """Gaussians as raw parameters (means, log-scales, raw quaternions,
     opacity logits, SH dc, SH rest) in one flat buffer on one CUDA device."""
 
-    AUTO_BIN_PAIRS_PER_TILE = 1024
+    AUTO_BIN_PAIRS_PER_TILE = 2560  # as cuda_rasterizer.BIN_MAX_PAIRS_PER_TILE
 
     def __init__(self, raw: dict, width: int, height: int, lrs: dict | None = None,
                  ssim_lambda: float = 0.0, group=None, fused_dp=False, strategy=None,

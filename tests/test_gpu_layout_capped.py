@@ -62,7 +62,8 @@ def setup(gs, cfg, n, W, H, cams, seed=0):
 
 
 CASES = [(0, 20_000, 256, 256, 2), (0, 513, 200, 120, 1), (0, 40, 64, 48, 1),
-         (1, None, 1920, 1080, 2), (1, 200_000, 5120, 3840, 1)]
+         (1, None, 1920, 1080, 2), (1, 200_000, 5120, 3840, 1),
+         (2, None, 1600, 1064, 1)]  # config 2: a quarter of the buckets above 2048 entries
 
 
 @pytest.mark.parametrize("entry", ["capped", "bins"])
