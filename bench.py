@@ -603,7 +603,8 @@ def restore_state(tr, state):
             fp.exp_avg.copy_(moments[0])
             fp.exp_avg_sq.copy_(moments[1])
     fp.step_count = step_count
-    torch.cuda.synchronize()
+    if fp.data.is_cuda:
+        torch.cuda.synchronize(fp.data.device)
 
 
 def timed_steps(fn, steps, warmup, world):

@@ -50,3 +50,33 @@ def test_explicit_views_and_lambda():
     assert (total, mine) == (7, 3) and args.strong is True
     with pytest.raises(SystemExit):
         plan(["--global-views", "1"], 2, 0)
+
+
+def test_state_snapshot_round_trip():
+    """snapshot_state / restore_state put parameters, Adam moments and the
+    step count back in the same buffers (the e2e region replays the
+    device-timed steps from that state)."""
+    import types
+
+    import torch
+
+    dp = importlib.import_module("3dgs_from_scratch_b200.dp")
+    raw = bench.scenes.make_gaussians(bench.scenes.CONFIGS[0], seed=1, n=257)
+    fp = dp.FlatParams(raw)
+    fp.exp_avg = torch.randn_like(fp.data)
+    fp.exp_avg_sq = torch.rand_like(fp.data)
+    fp.step_count = 7
+    tr = types.SimpleNamespace(fp=fp)
+    ptrs = (fp.data.data_ptr(), fp.exp_avg.data_ptr(), fp.exp_avg_sq.data_ptr())
+    before = (fp.data.clone(), fp.exp_avg.clone(), fp.exp_avg_sq.clone())
+    state = bench.snapshot_state(tr)
+    with torch.no_grad():
+        fp.data.add_(1.0)
+        fp.exp_avg.mul_(3.0)
+        fp.exp_avg_sq.zero_()
+    fp.step_count = 12
+    bench.restore_state(tr, state)
+    assert (fp.data.data_ptr(), fp.exp_avg.data_ptr(), fp.exp_avg_sq.data_ptr()) == ptrs
+    for a, b in zip((fp.data, fp.exp_avg, fp.exp_avg_sq), before):
+        assert torch.equal(a, b)
+    assert fp.step_count == 7
