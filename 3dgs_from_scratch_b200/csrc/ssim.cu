@@ -46,6 +46,8 @@ constexpr int kSsimRunH = 8;                   // outputs per thread, horizontal
 constexpr int kSsimRunV = 4;                   // outputs per thread, vertical pass
 constexpr int kSsimStageRows = 6;              // staged rows per step (6 x 42 threads)
 constexpr int kSsimStageThreads = kSsimStageRows * kSsimHW;
+constexpr int kSsimStageSteps = kSsimHH / kSsimStageRows;  // 7 staged rows per thread
+static_assert(kSsimHH % kSsimStageRows == 0, "every staging thread takes kSsimStageSteps rows");
 constexpr int kSsimThreads = 256;
 constexpr float kSsimC1 = 0.01f * 0.01f;
 constexpr float kSsimC2 = 0.03f * 0.03f;
@@ -179,12 +181,21 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_fwd_kernel(SsimSrc<HWC, TT>
     const int c = threadIdx.x % kSsimHW, r0 = threadIdx.x / kSsimHW;
     const int gx = gx0 - kSsimR + c;
     const bool in_x = gx >= 0 && gx < W;
-    for (int r = r0; r < kSsimHH; r += kSsimStageRows) {
-      const int gy = gy0 - kSsimR + r;
-      float xv = 0.0f, yv = 0.0f;
-      if (in_x && gy >= 0 && gy < H) src.load(plane, gy, gx, xv, yv);
-      sx[r * kSsimStride + c] = xv;
-      sy[r * kSsimStride + c] = yv;
+    // every load of the thread's 7 rows first, then the stores (one round
+    // trip to memory instead of seven)
+    float xv[kSsimStageSteps], yv[kSsimStageSteps];
+#pragma unroll
+    for (int i = 0; i < kSsimStageSteps; ++i) {
+      const int gy = gy0 - kSsimR + r0 + i * kSsimStageRows;
+      xv[i] = 0.0f;
+      yv[i] = 0.0f;
+      if (in_x && gy >= 0 && gy < H) src.load(plane, gy, gx, xv[i], yv[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kSsimStageSteps; ++i) {
+      const int r = r0 + i * kSsimStageRows;
+      sx[r * kSsimStride + c] = xv[i];
+      sy[r * kSsimStride + c] = yv[i];
     }
   }
   __syncthreads();
@@ -260,18 +271,25 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_bwd_kernel(
     const int c = threadIdx.x % kSsimHW, r0 = threadIdx.x / kSsimHW;
     const int gx = gx0 - kSsimR + c;
     const bool in_x = gx >= 0 && gx < W;
-    for (int r = r0; r < kSsimHH; r += kSsimStageRows) {
-      const int gy = gy0 - kSsimR + r;
-      float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+    // every load of the thread's 7 rows first, then the stores
+    float v0[kSsimStageSteps], v1[kSsimStageSteps], v2[kSsimStageSteps];
+#pragma unroll
+    for (int i = 0; i < kSsimStageSteps; ++i) {
+      const int gy = gy0 - kSsimR + r0 + i * kSsimStageRows;
+      v0[i] = v1[i] = v2[i] = 0.f;
       if (in_x && gy >= 0 && gy < H) {
         const int o = pbase + gy * W + gx;
-        v0 = m0[o];
-        v1 = m1[o];
-        v2 = m2[o];
+        v0[i] = m0[o];
+        v1[i] = m1[o];
+        v2[i] = m2[o];
       }
-      sm[0][r * kSsimStride + c] = v0;
-      sm[1][r * kSsimStride + c] = v1;
-      sm[2][r * kSsimStride + c] = v2;
+    }
+#pragma unroll
+    for (int i = 0; i < kSsimStageSteps; ++i) {
+      const int r = r0 + i * kSsimStageRows;
+      sm[0][r * kSsimStride + c] = v0[i];
+      sm[1][r * kSsimStride + c] = v1[i];
+      sm[2][r * kSsimStride + c] = v2[i];
     }
   }
   __syncthreads();
