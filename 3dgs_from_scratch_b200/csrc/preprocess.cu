@@ -156,7 +156,7 @@ constexpr int kPreBlock = 128;  // Gaussians (and threads) per chunk
 
 // Shared-memory image of one chunk's parameter slice, AoS as in HBM. Every
 // member starts on a 16-byte boundary (bulk-copy destinations).
-struct PreSmem {
+struct PreSmem {  // stage_chunk relies on this order and on there being no padding
   float means[kPreBlock * 3];
   float scales[kPreBlock * 3];
   float quats[kPreBlock * 4];
@@ -175,6 +175,79 @@ __device__ __forceinline__ void stage(float *__restrict__ dst, const float *__re
     for (int k = threadIdx.x; k < (count >> 2); k += blockDim.x) d4[k] = __ldg(s4 + k);
   } else {
     for (int k = threadIdx.x; k < count; k += blockDim.x) dst[k] = __ldg(src + k);
+  }
+}
+
+// Stages one chunk's parameter slices (means, scales, quats, opacities if
+// with_opac, dc, rest: count Gaussians from Gaussian `first`) as one index
+// space of float4s, kStageBatch loads in flight per thread before their
+// stores (the slices one after the other would wait on memory once per
+// slice and loop trip). Falls back to stage() per slice unless every source
+// slice is 16-byte aligned and count % 4 == 0.
+constexpr int kStageBatch = 8;
+static_assert(sizeof(PreSmem) == sizeof(float) * kPreBlock * (3 + 3 + 4 + 1 + 3 + 45),
+              "PreSmem is the six slices back to back");
+
+__device__ __forceinline__ void stage_chunk(PreSmem &S, const float *__restrict__ means,
+                                            const float *__restrict__ scales,
+                                            const float *__restrict__ quats,
+                                            const float *__restrict__ opac,
+                                            const float *__restrict__ dc,
+                                            const float *__restrict__ rest, size_t first,
+                                            int count, bool with_opac) {
+  const float *p0 = means + 3 * first, *p1 = scales + 3 * first, *p2 = quats + 4 * first;
+  const float *p3 = with_opac ? opac + first : nullptr, *p4 = dc + 3 * first;
+  const float *p5 = rest + 45 * first;
+  const uintptr_t bits = (uintptr_t)p0 | (uintptr_t)p1 | (uintptr_t)p2 | (uintptr_t)p3 |
+                         (uintptr_t)p4 | (uintptr_t)p5;
+  if ((bits & 15) != 0 || (count & 3) != 0) {
+    stage(S.means, p0, 3 * count);
+    stage(S.scales, p1, 3 * count);
+    stage(S.quats, p2, 4 * count);
+    if (with_opac) stage(S.opac, p3, count);
+    stage(S.dc, p4, 3 * count);
+    stage(S.rest, p5, 45 * count);
+    return;
+  }
+  // float4 counts of the six slices and their running ends
+  const int q = count >> 2;
+  const int e0 = 3 * q, e1 = e0 + 3 * q, e2 = e1 + 4 * q, e3 = e2 + (with_opac ? q : 0),
+            e4 = e3 + 3 * q, e5 = e4 + 45 * q;
+  const float4 *s0 = reinterpret_cast<const float4 *>(p0), *s1 = reinterpret_cast<const float4 *>(p1),
+               *s2 = reinterpret_cast<const float4 *>(p2), *s3 = reinterpret_cast<const float4 *>(p3),
+               *s4 = reinterpret_cast<const float4 *>(p4), *s5 = reinterpret_cast<const float4 *>(p5);
+  auto src_of = [&](int i) -> const float4 * {
+    return i < e0 ? s0 + i
+         : i < e1 ? s1 + (i - e0)
+         : i < e2 ? s2 + (i - e1)
+         : i < e3 ? s3 + (i - e2)
+         : i < e4 ? s4 + (i - e3)
+                  : s5 + (i - e4);
+  };
+  auto dst_of = [&](int i) -> float4 * {
+    float *d = i < e0 ? S.means + 4 * i
+             : i < e1 ? S.scales + 4 * (i - e0)
+             : i < e2 ? S.quats + 4 * (i - e1)
+             : i < e3 ? S.opac + 4 * (i - e2)
+             : i < e4 ? S.dc + 4 * (i - e3)
+                      : S.rest + 4 * (i - e4);
+    return reinterpret_cast<float4 *>(d);
+  };
+  const int step = blockDim.x;
+  // PreSmem holds the six slices back to back, each kPreBlock Gaussians long
+  const bool dense = count == kPreBlock && with_opac;
+  for (int i0 = threadIdx.x; i0 < e5; i0 += kStageBatch * step) {
+    float4 v[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = i0 + u * step;
+      if (i < e5) v[u] = __ldg(src_of(i));
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = i0 + u * step;
+      if (i < e5) *(dense ? reinterpret_cast<float4 *>(&S) + i : dst_of(i)) = v[u];
+    }
   }
 }
 
@@ -362,12 +435,7 @@ __global__ void __launch_bounds__(kPreBlock) preprocess_forward_kernel(PreFwdArg
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
-  stage(S.means, A.means + 3 * f, 3 * cnt);
-  stage(S.scales, A.scales + 3 * f, 3 * cnt);
-  stage(S.quats, A.quats + 4 * f, 4 * cnt);
-  stage(S.opac, A.opac + f, cnt);
-  stage(S.dc, A.dc + 3 * f, 3 * cnt);
-  stage(S.rest, A.rest + 45 * f, 45 * cnt);
+  stage_chunk(S, A.means, A.scales, A.quats, A.opac, A.dc, A.rest, f, cnt, true);
   __syncthreads();
   pre_fwd_views(A, S, s_cam, t, first + t, t < cnt, s_tot);
   flush_totals(A, s_tot);
@@ -625,12 +693,7 @@ __global__ void __launch_bounds__(kPreBlock, MULTI ? GS_PRE_MULTI_MINB : 1)
   const int first = base + blockIdx.x * kPreBlock;
   const int cnt = min(kPreBlock, n - first);
   const size_t f = (size_t)first;
-  stage(S.means, A.means + 3 * f, 3 * cnt);
-  stage(S.scales, A.scales + 3 * f, 3 * cnt);
-  stage(S.quats, A.quats + 4 * f, 4 * cnt);
-  if (A.activate) stage(S.opac, A.opac + f, cnt);
-  stage(S.dc, A.dc + 3 * f, 3 * cnt);
-  stage(S.rest, A.rest + 45 * f, 45 * cnt);
+  stage_chunk(S, A.means, A.scales, A.quats, A.opac, A.dc, A.rest, f, cnt, A.activate != 0);
   __syncthreads();
   const int t = threadIdx.x;
   if (t < cnt) pre_bwd_one<MULTI>(A, S, s_cam, rest_acc + 45 * t, t, first + t);
