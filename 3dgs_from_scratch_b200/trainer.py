@@ -87,8 +87,9 @@ class NativeTrainer:
         # step, which step() repeats with grown buffers).
         # "auto" picks one of the two at every sizing of the buffers: binning
         # while the views average at most AUTO_BIN_PAIRS_PER_TILE pairs per
-        # tile (its per-tile sorts are cheap for short lists), the two sorts
-        # above (long lists, e.g. configurations 2-4).
+        # tile (its per-tile radix sorts are cheap for lists of up to 4096
+        # entries: configurations 1, 2 and 4), the two sorts above for longer
+        # lists (the clustered 4K scene of configuration 3).
         if layout not in ("auto", "binned", "capped", "batched", "per_view"):
             raise ValueError("layout must be 'auto', 'binned', 'capped', 'batched' or 'per_view'")
         self.layout = layout

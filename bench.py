@@ -89,8 +89,8 @@ def parse():
                    default="auto",
                    help="tile layout: one per view into fixed-capacity buffers with the pair "
                         "counts kept on the device (no host synchronisation in a step), by "
-                        "per-tile binning or by two radix sorts (auto: binning for short "
-                        "per-tile lists); every view in one cooperative launch; or one per "
+                        "per-tile binning or by two radix sorts (auto: binning up to 2560 pairs "
+                        "per tile on average); every view in one cooperative launch; or one per "
                         "view sized by a host read of the pair counts")
     p.add_argument("--dp", choices=["nccl", "fused", "fused-p2p", "fused-mc"], default="fused",
                    help="multi-GPU optimizer step: NCCL all-reduce + Adam, or the fused "
